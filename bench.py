@@ -1,0 +1,325 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-GEMM stress workload's hot path on B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the configuration BASELINE.json's metric is quoted on that fits one
+GPU): configs[1], INT8 W8A8 GEMM M=N=K=8192, INT8 operands uniform in
+[-127,127] (seed 1), fp32 per-row / per-column scales, INT32 accumulate, bf16
+output.  A step is one GEMM (one pass of the hot path over one operand set);
+two operand sets rotate (2 x 128 MiB of operands > the 126 MB L2), so every
+step streams its operands from HBM.
+
+Printed by rank 0, one JSON line:
+  value     whole-job TOPS (2*M*N*K per step, summed over ranks), device-timed
+            with CUDA events on the launch stream, max over ranks;
+  e2e       the same metric through the C ABI with HOST buffers: per step the
+            pinned-host operands are uploaded (qg_upload), the GEMM runs
+            (qg_run_copy) and the bf16 result is read back (qg_download);
+  roofline  tensor-bound: achieved TOPS of the GEMM kernel vs the measured
+            peak (2 x the measured bf16 dense burst figure of
+            MEASURED_PEAKS.json, INT8 being twice bf16 on this part);
+  cpu_baseline  the CPU oracle's INT8 GEMM (OpenMP, all host threads) on a
+            bounded sample of rows of the same GEMM, rank 0 at N=1 only.
+Multi-GPU: one process per GPU (torchrun), each an independent instance with
+no data-path collective ("scaling": "weak"); NCCL carries only the barrier and
+the max of the timings.
+
+--impl reference times the reference side on the host cores: the reference
+has no INT8 GEMM (its quantized_gemm is a synthetic hash loop), so the arm is
+the oracle's CPU port of the GEMM, plus, for context, the reference's own MOCK
+binary of the path when it was built into oracle/_ref.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "quant GEMM TOPS/GPU & % tensor peak; W4A16 GEMV HBM GB/s; mismatches=0"
+M = N = K = 8192
+DATASHEET_INT8_TOPS = 4500.0
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16_tflops": float(d["bf16_tflops"]), "bf16_tflops_sustained": float(d["bf16_tflops_sustained"]),
+                "hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _traffic():
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("gemm_i8_8192")
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            if self.uuid and parts[1] != self.uuid:
+                continue
+            rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower() == "active"})
+        power = [float(r[4]) for r in rows if r[4].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "power_w_max": max(power) if power else None, "samples": len(rows)}
+
+
+def cpu_baseline(target_s: float = 10.0):
+    """The oracle's INT8 GEMM on a bounded sample of rows of the 8192^3 GEMM (all host threads)."""
+    import numpy as np
+    from oracle import qg_oracle as O
+    # rows 0..255 of A (the first rows of the full A's stream), the full B
+    A, B, sa, sb = O.int8_operands(256, N, K, seed=1)
+    rows = np.arange(1, dtype=np.int32)
+    t0 = time.perf_counter()
+    O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
+    t1 = time.perf_counter() - t0
+    nrows = int(max(1, min(256, target_s / max(t1, 1e-6))))
+    rows = np.arange(nrows, dtype=np.int32)
+    t0 = time.perf_counter()
+    O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
+    dt = time.perf_counter() - t0
+    tops = 2.0 * nrows * N * K / dt / 1e12
+    return {"value": tops, "unit": "TOPS", "cores": O.threads(), "kind": "port",
+            "sample": f"{nrows} of 8192 output rows of the 8192x8192x8192 INT8 GEMM (bf16 epilogue), {dt:.1f} s",
+            "seconds": dt}
+
+
+def reference_mock_rate():
+    """The reference's own MOCK binary of this path (synthetic hash loop), if built into oracle/_ref."""
+    ref = ROOT / "oracle" / "_ref" / "quantized_gemm_mock"
+    if not ref.exists():
+        return None
+    p = subprocess.run([str(ref), "0", "2", "5", "--verify"], capture_output=True, text=True, timeout=120)
+    for line in p.stdout.splitlines():
+        if line.startswith("Throughput:"):
+            v = float(line.split()[1])
+            return {"printed_ai_ops_per_s": v, "executed_ai_ops_per_s": v / 1024.0, "rc": p.returncode,
+                    "note": "reference MOCK quantized_gemm: integer hash loop, not a GEMM; prints 1024x the "
+                            "executed thread-iterations (mock grid counted, one logical thread run)"}
+    return None
+
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return 0
+    steps = max(1, args.steps)
+    warm = max(0, args.warmup)
+    import numpy as np
+    from oracle import qg_oracle as O
+    A, B, sa, sb = O.int8_operands(64, N, K, seed=1)
+    rows = np.arange(4, dtype=np.int32)   # bounded sample per step: 4 rows of the GEMM
+    for _ in range(min(warm, 1)):
+        O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows[:1])
+    t0 = time.perf_counter()
+    for s in range(steps):
+        O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
+    dt = time.perf_counter() - t0
+    tops = 2.0 * len(rows) * N * K * steps / dt / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": args.gpus,
+        "steps": steps, "warmup": warm, "ms_per_step": dt / steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "configs[1] INT8 W8A8 GEMM 8192x8192x8192, bf16 out (CPU: 4 rows per step)"},
+        "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": O.threads(), "kind": "port",
+                         "sample": f"{len(rows)} of 8192 output rows per step, {steps} steps"},
+        "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_mock": reference_mock_rate(),
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+    import pantheon_b200 as pb
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device(f"cuda:{local_rank}")
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    steps = max(1, args.steps)
+    warm = max(3, args.warmup)
+    w = pb.Workload(pb.QG_FMT_INT8, M, N, K, copies=2, seed=1, device=local_rank)
+    w.fill(1)
+    w.golden()
+    stream = torch.cuda.current_stream(dev)
+    ops = w.ops_per_launch
+
+    # ---------------- device-timed region: K GEMMs, operands resident in HBM
+    w.run(warm)
+    torch.cuda.synchronize(dev)
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(uuid) as clk:
+        barrier()
+        torch.cuda.synchronize(dev)
+        ev0.record(stream)
+        w.run(steps, stream)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+    ms = ev0.elapsed_time(ev1)
+    clocks = clk.summary()
+    mismatches = w.verify()
+    status = pb.device_status(local_rank)
+
+    # ---------------- end-to-end: host operands -> GEMM -> host result, through the C ABI
+    host_ops = []
+    for slot in range(4):
+        t = w.tensor(0, slot).cpu().pin_memory()
+        host_ops.append(t)
+    _, out_bytes = w.tensor_ptr(0, w.SLOT_OUT)
+    host_out = torch.empty((out_bytes,), dtype=torch.uint8).pin_memory()
+    h2d = sum(t.numel() for t in host_ops)
+    e2e_steps = max(3, min(steps, 20))
+    for _ in range(2):
+        w.upload(0, host_ops, stream)
+        w.run_copy(0, stream)
+        w.download(0, host_out, stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        w.upload(0, host_ops, stream)
+        w.run_copy(0, stream)
+        w.download(0, host_out, stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    t = torch.tensor([ms, e2e_ms, float(mismatches), float(status != 0)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max, e2e_max, mm_max, bad = t.tolist()
+
+    result = None
+    if rank == 0:
+        peaks = _peaks()
+        per_launch_s = ms / 1e3 / steps
+        achieved = ops / per_launch_s / 1e12
+        peak = 2.0 * peaks["bf16_tflops"]
+        value = ops * steps * world / (ms_max / 1e3) / 1e12
+        e2e_value = ops * e2e_steps * world / (e2e_max / 1e3) / 1e12
+        traffic = _traffic()
+        result = {
+            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "configs[1] INT8 W8A8 GEMM 8192x8192x8192, bf16 out, fp32 row/col scales",
+                       "M": M, "N": N, "K": K, "seed": 1, "operand_sets": 2,
+                       "l2": "inputs larger than L2: 2 rotating operand sets of 128 MiB each",
+                       "parallelism": f"replicas x{world} (independent instance per GPU)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"2 x {peaks['source']} bf16 dense burst ({peaks['bf16_tflops']} TFLOP/s)",
+                         "frac_of_datasheet_4500": achieved / DATASHEET_INT8_TOPS},
+            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_bytes,
+                    "path": "qg_upload + qg_run_copy + qg_download (pinned host buffers)", "steps": e2e_steps},
+            "clocks": clocks,
+            "gpu_launches": steps,
+            "mismatches": int(mm_max),
+            "device_timeouts": int(bad),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline()
+    w.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    return run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,202 @@
+/*
+ * pantheon_qgemm.h -- C ABI of the B200-native quantized-GEMM stress workload.
+ *
+ * This library is what sits behind the `quantized_gemm` workload binary that
+ * Pantheon's runner launches once per GPU.  The reference implementation of
+ * that binary is the synthetic harness in
+ *   kernels/quantized_gemm/quantized_gemm.cpp:1-2  (kind 3 of)
+ *   kernels/common/ai_workload_template.h:351-380  (main: argv, warm-up,
+ *                                                   timed loop, verify, exit)
+ * and the entry points below replace, one for one, the pieces of that harness
+ * (cited beside each declaration).  The process contract (argv in; the
+ * "Throughput:" / "Verification:" lines and the exit code out) is kept by the
+ * binary built from pantheon_b200/csrc/quantized_gemm_main.cpp on top of this
+ * ABI.
+ *
+ * Conventions
+ *   - Plain C types only.  Device pointers are `const void*` / `void*`; a CUDA
+ *     stream is passed as `void*` (a cudaStream_t, NULL = legacy stream).
+ *   - Every int-returning call returns QG_OK (0) on success, a negative value
+ *     for a CUDA / argument error, and a positive value when a kernel's
+ *     bounded wait expired (QG_ERR_DEVICE_TIMEOUT); the context is then still
+ *     usable and qg_last_error() says where.  No call aborts the process.
+ *   - Layouts are row-major with the contraction dimension K contiguous for
+ *     both operands ("TN": A[M,K], B[N,K]), as the reference vendor GEMM uses
+ *     (kernels/common/vendor_gemm.h:276-279,334-337).
+ *   - Built for sm_100a only.  There is no CPU fallback: on a machine without
+ *     a B200 every compute call fails with QG_ERR_CUDA.
+ */
+#ifndef PANTHEON_QGEMM_H
+#define PANTHEON_QGEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QG_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define QG_API __attribute__((visibility("default")))
+#else
+#define QG_API
+#endif
+
+/* Return codes. */
+#define QG_OK                  0
+#define QG_ERR_ARG            -1   /* bad argument, unsupported shape or format */
+#define QG_ERR_CUDA           -2   /* a CUDA runtime call failed (no device, OOM, fault) */
+#define QG_ERR_UNSUPPORTED    -3   /* device is not sm_100 */
+#define QG_ERR_DEVICE_TIMEOUT  1   /* a kernel's bounded mbarrier/TMEM wait expired */
+
+/* Operand formats (the `--format` flag of the workload binary). */
+#define QG_FMT_INT8   0   /* INT8 x INT8 -> INT32, fp32 per-row/per-col scales   */
+#define QG_FMT_FP8    1   /* FP8 e4m3, 1x128 (A) and 128x128 (B) fp32 block scales */
+#define QG_FMT_NVFP4  2   /* e2m1 + ue4m3 per 16 along K + fp32 per-tensor scale   */
+#define QG_FMT_W4A16  3   /* bf16 activations x int4 weights, fp16 scale/zero per 128 */
+
+/* Output element types. */
+#define QG_OUT_BF16   0
+#define QG_OUT_F32    1
+#define QG_OUT_S32    2   /* raw INT32 accumulators (INT8 only) */
+
+/* Workload configuration for a context. Zero fields take the format default. */
+typedef struct qg_cfg {
+    int32_t  format;     /* QG_FMT_* */
+    int32_t  m, n, k;    /* GEMM: C[m,n] = A[m,k] B[n,k]^T ; W4A16: Y[m,n] = X[m,k] W[k,n] */
+    int32_t  out_type;   /* QG_OUT_BF16 (default) or QG_OUT_F32 */
+    int32_t  copies;     /* rotating operand sets (>= 1); each has its own output and golden */
+    uint64_t seed;       /* generator seed (tensor ids keep A and B on separate streams) */
+} qg_cfg;
+
+typedef struct qg_ctx qg_ctx;
+
+/* One recorded verification mismatch (first few are kept, as the reference's
+ * device fault log does: kernels/common/fault_log.h:36-50). */
+typedef struct qg_mismatch {
+    uint64_t index;      /* output word index */
+    uint32_t expected;   /* golden word */
+    uint32_t actual;     /* observed word */
+} qg_mismatch;
+
+/* ---------------------------------------------------------------- context API */
+
+/* Allocate every device buffer of one workload instance on `device`.
+ * Replaces: the cudaMalloc block of ai_workload_template.h:361-366 and the
+ * working-set sizing at :359. */
+QG_API int  qg_create(qg_ctx** out, int device, const qg_cfg* cfg);
+
+/* Bytes of device memory a context with this configuration allocates
+ * (used by the binary's --mem sizing). */
+QG_API int  qg_required_bytes(const qg_cfg* cfg, uint64_t* bytes);
+
+/* Fill all operand copies from the counter-based generator.
+ * Replaces: ai_initialize (ai_workload_template.h:85-94) and
+ *           pantheon_gemm_fill (kernels/common/vendor_gemm.h:184-191). */
+QG_API int  qg_fill(qg_ctx* ctx, uint64_t seed);
+
+/* Run every copy once and keep the outputs (and INT8 row checksums) as the
+ * golden result of this run.
+ * Replaces: the golden GEMM + D2D copy of kernels/mma_virus/mma_virus.cpp:331-337. */
+QG_API int  qg_golden(qg_ctx* ctx);
+
+/* Launch `iters` GEMMs (or GEMVs), rotating over the operand copies, on `stream`.
+ * Replaces: the ai_workload_kernel launch of the timed loop
+ *           (ai_workload_template.h:370). Asynchronous. */
+QG_API int  qg_run(qg_ctx* ctx, int iters, void* stream);
+
+/* Compare every copy's latest output (and checksums) with the golden result on
+ * the device; `*mismatches` receives the number of differing 32-bit words.
+ * Replaces: ai_verify_output (ai_workload_template.h:343-349) and
+ *           verify_mma_kernel (kernels/mma_virus/mma_virus.cpp:156-173). Synchronous. */
+QG_API int  qg_verify(qg_ctx* ctx, uint64_t* mismatches);
+
+/* Copy out up to `cap` recorded mismatches of the last qg_verify; returns how many. */
+QG_API int  qg_mismatch_log(qg_ctx* ctx, qg_mismatch* out, int cap);
+
+/* Flip one bit of copy 0's output, so the next qg_verify must fail.
+ * Replaces: --inject_error (ai_workload_template.h:90-92) and
+ *           pantheon_gemm_flip_bit (kernels/common/vendor_gemm.h:193-195). */
+QG_API int  qg_inject(qg_ctx* ctx);
+
+/* Useful work of one launch: 2*M*N*K integer or floating-point operations
+ * (GEMMs), or the algorithmic bytes moved (W4A16). */
+QG_API double qg_ops_per_launch(const qg_ctx* ctx);
+QG_API double qg_bytes_per_launch(const qg_ctx* ctx);
+
+/* Copy the context's operands from / its output to HOST memory (pinned or
+ * pageable), on `stream`; used for the end-to-end path.  The host layouts are
+ * the device layouts described under the direct entry points below. */
+QG_API int  qg_upload(qg_ctx* ctx, int copy, const void* const* host_operands, void* stream);
+QG_API int  qg_download(qg_ctx* ctx, int copy, void* host_out, void* stream);
+
+/* Device pointers of copy `copy`'s tensors (for tests and the bench):
+ * slot 0..4 = operands in the order of the direct entry point of the format,
+ * slot 5 = output, slot 6 = golden output, slot 7 = row checksums. */
+QG_API int  qg_tensor(qg_ctx* ctx, int copy, int slot, void** ptr, uint64_t* bytes);
+
+/* Launch one GEMM (or GEMV) on copy `copy` (end-to-end path: qg_upload,
+ * qg_run_copy, qg_download). Asynchronous. */
+QG_API int  qg_run_copy(qg_ctx* ctx, int copy, void* stream);
+
+/* Wait for all work on the context's device; returns QG_ERR_DEVICE_TIMEOUT if
+ * a kernel's bounded wait expired. Replaces the per-launch hipDeviceSynchronize
+ * of the timed loop (ai_workload_template.h:370). */
+QG_API int  qg_synchronize(qg_ctx* ctx);
+
+/* Free and total device memory of `device` (the --mem sizing input,
+ * ai_workload_template.h:359). */
+QG_API int  qg_mem_info(int device, uint64_t* free_bytes, uint64_t* total_bytes);
+
+/* QG_ABI_VERSION of the loaded library. */
+QG_API int  qg_abi_version(void);
+
+/* Last error message of this context (or of the library when ctx is NULL). */
+QG_API int  qg_last_error(const qg_ctx* ctx, char* buf, size_t len);
+
+QG_API void qg_destroy(qg_ctx* ctx);
+
+/* ---------------------------------------------------------------- direct entry points
+ * Stateless kernels over caller-owned device memory (all asynchronous on `stream`).
+ * They replace the per-kind body of ai_workload_kernel
+ * (ai_workload_template.h:157-177, kind 3 "Quantized GEMM") with real GEMMs. */
+
+/* INT8 W8A8:  C[m,n] = out( f32(sum_k A[m,k]*B[n,k]) * sa[m] * sb[n] )
+ *   A int8 [M,K], B int8 [N,K] (K contiguous, K % 16 == 0), sa fp32 [M], sb fp32 [N];
+ *   out_type QG_OUT_BF16 / QG_OUT_F32 / QG_OUT_S32 (raw accumulators, scales ignored).
+ *   row_checksums (optional, uint32 [M]) receives
+ *   sum_n (uint32)acc[m,n] * qg_cksum_weight(m,n)  (mod 2^32), a bit-exact
+ *   fingerprint of the INT32 accumulators. */
+QG_API int  qg_gemm_i8(const void* A, const void* B, const void* sa, const void* sb,
+                void* C, int out_type, void* row_checksums,
+                int M, int N, int K, void* stream);
+
+/* Bounded-wait status of the most recent kernel on this device (QG_OK or
+ * QG_ERR_DEVICE_TIMEOUT); clears the flag. Synchronous. */
+QG_API int  qg_device_status(int device);
+
+/* Compare two word arrays on the device.  `count` is a device uint64[2]:
+ * count[0] += number of differing 32-bit words, count[1] += number of
+ * differences seen for logging; the first `log_cap` differences are written to
+ * `log` (device qg_mismatch array).  Arrays must be 16-byte aligned.
+ * Replaces: ai_verify_output (ai_workload_template.h:343-349). */
+QG_API int  qg_verify_words(const void* actual, const void* expected, uint64_t nwords,
+                     void* count, void* log, int log_cap, void* stream);
+
+/* Counter-based generator (identical arithmetic to the CPU restatement in the
+ * test oracle): out[i] = uniform int8 in [-127,127] from (seed, tensor_id, i).
+ * Replaces: ai_initialize's hash fill (ai_workload_template.h:85-94). */
+QG_API int  qg_gen_i8(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream);
+/* out[i] = lo + (hi-lo) * u(seed, tensor_id, i), fp32. */
+QG_API int  qg_gen_uniform_f32(void* out, uint64_t n, float lo, float hi,
+                        uint64_t seed, uint32_t tensor_id, void* stream);
+/* out[i] = standard normal deviate (seed, tensor_id, i), fp32. */
+QG_API int  qg_gen_normal_f32(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PANTHEON_QGEMM_H */

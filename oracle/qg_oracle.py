@@ -1,0 +1,155 @@
+"""ctypes binding of the CPU oracle (oracle/libqg_oracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU-baseline legs of bench.py, as the checker or the timed CPU baseline; never
+by pantheon_b200/.  Parity of the workload's NUMERICS with the reference is
+unpinned (the reference has no such arithmetic, see qg_oracle.h); the oracle's
+conversions and integer GEMM are pinned against numpy/torch in tests.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "libqg_oracle.so"
+REF_DIR = HERE / "_ref"
+
+_lib = None
+_P = C.c_void_p
+
+
+def build(quiet: bool = True) -> None:
+    """Build the oracle (and, when the reference tree is present, oracle/_ref)."""
+    proc = subprocess.run(["make", "-C", str(HERE)], capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"oracle build failed:\n{proc.stdout}\n{proc.stderr}")
+    if not quiet:
+        print(proc.stdout)
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            build()
+        L = C.CDLL(str(LIB))
+        sig = {
+            "qgo_splitmix64": (C.c_uint64, [C.c_uint64]),
+            "qgo_hash64": (C.c_uint64, [C.c_uint64, C.c_uint32, C.c_uint64]),
+            "qgo_normal_from_hash": (C.c_float, [C.c_uint64]),
+            "qgo_logf": (C.c_float, [C.c_float]),
+            "qgo_gen_i8": (None, [_P, C.c_uint64, C.c_uint64, C.c_uint32]),
+            "qgo_gen_uniform_f32": (None, [_P, C.c_uint64, C.c_float, C.c_float, C.c_uint64, C.c_uint32]),
+            "qgo_gen_normal_f32": (None, [_P, C.c_uint64, C.c_uint64, C.c_uint32]),
+            "qgo_f32_to_bf16": (C.c_uint16, [C.c_float]),
+            "qgo_bf16_to_f32": (C.c_float, [C.c_uint16]),
+            "qgo_f32_to_f16": (C.c_uint16, [C.c_float]),
+            "qgo_f16_to_f32": (C.c_float, [C.c_uint16]),
+            "qgo_f32_to_e4m3": (C.c_uint8, [C.c_float]),
+            "qgo_e4m3_to_f32": (C.c_float, [C.c_uint8]),
+            "qgo_f32_to_e2m1": (C.c_uint8, [C.c_float]),
+            "qgo_e2m1_to_f32": (C.c_float, [C.c_uint8]),
+            "qgo_cksum_weight": (C.c_uint32, [C.c_uint32, C.c_uint32]),
+            "qgo_gemm_i8": (None, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, _P, _P, _P]),
+            "qgo_quant_fp8_rows": (None, [_P, C.c_int, C.c_int, _P, _P]),
+            "qgo_quant_fp8_blocks": (None, [_P, C.c_int, C.c_int, _P, _P]),
+            "qgo_gemm_fp8_b128": (None, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, _P]),
+            "qgo_nvfp4_global_scale": (C.c_float, [_P, C.c_uint64]),
+            "qgo_quant_nvfp4": (None, [_P, C.c_int, C.c_int, C.c_float, _P, _P]),
+            "qgo_gemm_nvfp4": (None, [_P, _P, C.c_float, _P, _P, C.c_float, C.c_int, C.c_int, C.c_int, _P,
+                                      C.c_int, C.c_int, _P]),
+            "qgo_gemv_w4a16": (None, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, _P]),
+            "qgo_count_mismatch_u32": (C.c_uint64, [_P, _P, C.c_uint64]),
+            "qgo_max_rel_err": (C.c_double, [_P, _P, C.c_uint64, C.c_int]),
+            "qgo_threads": (C.c_int, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags.c_contiguous
+    return C.c_void_p(a.ctypes.data)
+
+
+# ---------------------------------------------------------------- generator
+def gen_i8(n: int, seed: int, tensor_id: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.int8)
+    lib().qgo_gen_i8(_p(out), n, seed, tensor_id)
+    return out
+
+
+def gen_uniform_f32(n: int, lo: float, hi: float, seed: int, tensor_id: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().qgo_gen_uniform_f32(_p(out), n, lo, hi, seed, tensor_id)
+    return out
+
+
+def gen_normal_f32(n: int, seed: int, tensor_id: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().qgo_gen_normal_f32(_p(out), n, seed, tensor_id)
+    return out
+
+
+def int8_operands(M: int, N: int, K: int, seed: int, copy: int = 0):
+    """The INT8 workload's operands of copy `copy` (tensor ids 8*copy + 0..3)."""
+    b = 8 * copy
+    A = gen_i8(M * K, seed, b + 0).reshape(M, K)
+    B = gen_i8(N * K, seed, b + 1).reshape(N, K)
+    sa = gen_uniform_f32(M, 0.001, 0.01, seed, b + 2)
+    sb = gen_uniform_f32(N, 0.001, 0.01, seed, b + 3)
+    return A, B, sa, sb
+
+
+# ---------------------------------------------------------------- GEMMs
+def gemm_i8(A, B, sa, sb, out_type: int = 0, rows=None, want_acc: bool = False, want_cksum: bool = False):
+    """Oracle INT8 GEMM. out_type 0 = bf16 (returned as uint16 bits), 1 = f32, 2 = s32."""
+    A = np.ascontiguousarray(A, dtype=np.int8)
+    B = np.ascontiguousarray(B, dtype=np.int8)
+    M, K = A.shape
+    N = B.shape[0]
+    r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int32)
+    nr = M if r is None else len(r)
+    dt = {0: np.uint16, 1: np.float32, 2: np.int32}[out_type]
+    C_ = np.empty((nr, N), dtype=dt)
+    acc = np.empty((nr, N), dtype=np.int32) if want_acc else None
+    ck = np.empty(nr, dtype=np.uint32) if want_cksum else None
+    sa = None if sa is None else np.ascontiguousarray(sa, dtype=np.float32)
+    sb = None if sb is None else np.ascontiguousarray(sb, dtype=np.float32)
+    lib().qgo_gemm_i8(_p(A), _p(B), _p(sa), _p(sb), M, N, K, _p(r), nr, out_type, _p(C_), _p(acc), _p(ck))
+    res = [C_]
+    if want_acc:
+        res.append(acc)
+    if want_cksum:
+        res.append(ck)
+    return res[0] if len(res) == 1 else tuple(res)
+
+
+# ---------------------------------------------------------------- conversions
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    f = lib().qgo_f32_to_bf16
+    return np.array([f(float(v)) for v in np.asarray(x, dtype=np.float32).ravel()], dtype=np.uint16)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def max_rel_err(y: np.ndarray, r: np.ndarray, kind: int) -> float:
+    y = np.ascontiguousarray(y)
+    r = np.ascontiguousarray(r)
+    return lib().qgo_max_rel_err(_p(y), _p(r), y.size, kind)
+
+
+def threads() -> int:
+    return lib().qgo_threads()

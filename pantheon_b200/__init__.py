@@ -1,0 +1,42 @@
+"""pantheon_b200 -- B200-native quantized-GEMM stress workload (sm_100a).
+
+Python side of the C ABI in include/pantheon_qgemm.h.  The workload itself is
+the `quantized_gemm` binary (pantheon_b200/lib/quantized_gemm) that Pantheon's
+runner launches once per GPU; this module is the same library seen from
+Python, for the tests and the benchmark.
+
+There is no CPU fallback: importing works anywhere, but every compute call
+needs the in-tree library (built by `python -m pantheon_b200.build`) and a
+B200; otherwise it raises.
+"""
+from __future__ import annotations
+
+from ._lib import (  # noqa: F401
+    LIB_PATH,
+    BIN_PATH,
+    QG_FMT_INT8,
+    QG_FMT_FP8,
+    QG_FMT_NVFP4,
+    QG_FMT_W4A16,
+    QG_OUT_BF16,
+    QG_OUT_F32,
+    QG_OUT_S32,
+    QGError,
+    load_library,
+)
+from .ops import (  # noqa: F401
+    Workload,
+    device_status,
+    gemm_i8,
+    gen_i8,
+    gen_normal_f32,
+    gen_uniform_f32,
+    verify_words,
+)
+
+__all__ = [
+    "LIB_PATH", "BIN_PATH", "QGError", "load_library", "Workload", "device_status",
+    "gemm_i8", "gen_i8", "gen_uniform_f32", "gen_normal_f32", "verify_words",
+    "QG_FMT_INT8", "QG_FMT_FP8", "QG_FMT_NVFP4", "QG_FMT_W4A16",
+    "QG_OUT_BF16", "QG_OUT_F32", "QG_OUT_S32",
+]

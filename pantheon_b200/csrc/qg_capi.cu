@@ -1,0 +1,298 @@
+// qg_capi.cu -- the context API of include/pantheon_qgemm.h: one workload
+// instance per device (operands, outputs, golden results, verification
+// counters), driven by the quantized_gemm binary, the Python wrapper and the
+// benchmark.  The instance owns its device memory; the caller owns the handle.
+#include "qg_common.cuh"
+#include "qg_formats.cuh"
+
+#include <cstdarg>
+#include <cstdlib>
+#include <new>
+#include <string>
+#include <vector>
+
+struct qg_ctx {
+    qg_cfg cfg{};
+    int device = 0;
+    qg::Layout layout{};
+    std::vector<qg::CopyBuffers> copies;
+    unsigned long long* counters = nullptr;   // [0] mismatching words, [1] log entries
+    qg_mismatch* log = nullptr;
+    int log_cap = 64;
+    int next_copy = 0;
+    bool golden_ready = false;
+    cudaStream_t stream = nullptr;            // internal stream for fill / golden / verify
+    std::string err;
+};
+
+namespace {
+
+int fail(qg_ctx* c, int rc) {
+    if (c) c->err = qg::last_error();
+    return rc;
+}
+
+#define CTX_CUDA(c, call)                                                                       \
+    do {                                                                                        \
+        cudaError_t e_ = (call);                                                                \
+        if (e_ != cudaSuccess) {                                                                \
+            ::qg::set_error("%s failed: %s (%d)", #call, cudaGetErrorString(e_), (int)e_);     \
+            return fail(c, QG_ERR_CUDA);                                                        \
+        }                                                                                       \
+    } while (0)
+
+void free_ctx_memory(qg_ctx* c) {
+    for (auto& cp : c->copies) {
+        for (int i = 0; i < qg::kMaxOperands; ++i)
+            if (cp.op[i]) cudaFree(cp.op[i]);
+        if (cp.out) cudaFree(cp.out);
+        if (cp.golden) cudaFree(cp.golden);
+        if (cp.cksum) cudaFree(cp.cksum);
+        if (cp.golden_cksum) cudaFree(cp.golden_cksum);
+        if (cp.scratch) cudaFree(cp.scratch);
+    }
+    c->copies.clear();
+    if (c->counters) cudaFree(c->counters);
+    if (c->log) cudaFree(c->log);
+    c->counters = nullptr;
+    c->log = nullptr;
+}
+
+int alloc(void** p, uint64_t bytes) {
+    if (bytes == 0) { *p = nullptr; return QG_OK; }
+    QG_CUDA(cudaMalloc(p, (size_t)bytes));
+    return QG_OK;
+}
+
+} // namespace
+
+extern "C" {
+
+int qg_required_bytes(const qg_cfg* cfg, uint64_t* bytes) {
+    QG_CHECK_ARG(cfg && bytes, "qg_required_bytes: null argument");
+    qg::Layout L;
+    int rc = qg::layout_for(*cfg, &L);
+    if (rc) return rc;
+    const int copies = cfg->copies > 0 ? cfg->copies : 1;
+    uint64_t per = 0;
+    for (int i = 0; i < L.n_ops; ++i) per += L.op_bytes[i];
+    per += 2 * L.out_bytes + 2 * L.cksum_bytes + L.scratch_bytes;
+    *bytes = per * (uint64_t)copies + 4096;
+    return QG_OK;
+}
+
+int qg_create(qg_ctx** out, int device, const qg_cfg* cfg) {
+    QG_CHECK_ARG(out && cfg, "qg_create: null argument");
+    *out = nullptr;
+    qg_ctx* c = new (std::nothrow) qg_ctx;
+    if (!c) { qg::set_error("qg_create: out of host memory"); return QG_ERR_ARG; }
+    c->cfg = *cfg;
+    if (c->cfg.copies <= 0) c->cfg.copies = 1;
+    c->device = device;
+    int rc = qg::layout_for(c->cfg, &c->layout);
+    if (rc) { delete c; return rc; }
+    c->cfg.m = c->layout.M;
+    c->cfg.n = c->layout.N;
+    c->cfg.k = c->layout.K;
+    if (cudaSetDevice(device) != cudaSuccess) {
+        qg::set_error("qg_create: cudaSetDevice(%d) failed", device);
+        delete c;
+        return QG_ERR_CUDA;
+    }
+    qg::DeviceInfo* info = nullptr;
+    if ((rc = qg::current_device_info(&info))) { delete c; return rc; }
+    c->copies.resize((size_t)c->cfg.copies);
+    const qg::Layout& L = c->layout;
+    for (auto& cp : c->copies) {
+        for (int i = 0; i < L.n_ops; ++i)
+            if ((rc = alloc(&cp.op[i], L.op_bytes[i]))) goto oom;
+        if ((rc = alloc(&cp.out, L.out_bytes))) goto oom;
+        if ((rc = alloc(&cp.golden, L.out_bytes))) goto oom;
+        if ((rc = alloc(&cp.cksum, L.cksum_bytes))) goto oom;
+        if ((rc = alloc(&cp.golden_cksum, L.cksum_bytes))) goto oom;
+        if ((rc = alloc(&cp.scratch, L.scratch_bytes))) goto oom;
+    }
+    if ((rc = alloc(reinterpret_cast<void**>(&c->counters), 2 * sizeof(unsigned long long)))) goto oom;
+    if ((rc = alloc(reinterpret_cast<void**>(&c->log), sizeof(qg_mismatch) * (size_t)c->log_cap))) goto oom;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        qg::set_error("qg_create: cudaStreamCreate failed");
+        rc = QG_ERR_CUDA;
+        goto oom;
+    }
+    *out = c;
+    return QG_OK;
+oom:
+    free_ctx_memory(c);
+    delete c;
+    return rc;
+}
+
+void qg_destroy(qg_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) { cudaStreamSynchronize(c->stream); cudaStreamDestroy(c->stream); }
+    free_ctx_memory(c);
+    delete c;
+}
+
+int qg_fill(qg_ctx* c, uint64_t seed) {
+    QG_CHECK_ARG(c, "qg_fill: null context");
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    c->cfg.seed = seed;
+    for (size_t i = 0; i < c->copies.size(); ++i) {
+        int rc = qg::fill_copy(c->cfg, c->layout, c->copies[i], (int)i, seed, c->stream);
+        if (rc) return fail(c, rc);
+    }
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    c->golden_ready = false;
+    return QG_OK;
+}
+
+int qg_golden(qg_ctx* c) {
+    QG_CHECK_ARG(c, "qg_golden: null context");
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    for (auto& cp : c->copies) {
+        int rc = qg::launch_copy(c->cfg, c->layout, cp, c->stream);
+        if (rc) return fail(c, rc);
+        CTX_CUDA(c, cudaMemcpyAsync(cp.golden, cp.out, c->layout.out_bytes, cudaMemcpyDeviceToDevice, c->stream));
+        if (c->layout.cksum_bytes)
+            CTX_CUDA(c, cudaMemcpyAsync(cp.golden_cksum, cp.cksum, c->layout.cksum_bytes, cudaMemcpyDeviceToDevice,
+                                        c->stream));
+    }
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    int st = qg_device_status(c->device);
+    if (st) return fail(c, st);
+    c->golden_ready = true;
+    c->next_copy = 0;
+    return QG_OK;
+}
+
+int qg_run(qg_ctx* c, int iters, void* stream) {
+    QG_CHECK_ARG(c && iters >= 0, "qg_run: bad argument");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < iters; ++i) {
+        int rc = qg::launch_copy(c->cfg, c->layout, c->copies[(size_t)c->next_copy], s);
+        if (rc) return fail(c, rc);
+        c->next_copy = (c->next_copy + 1) % (int)c->copies.size();
+    }
+    return QG_OK;
+}
+
+int qg_verify(qg_ctx* c, uint64_t* mismatches) {
+    QG_CHECK_ARG(c && mismatches, "qg_verify: null argument");
+    QG_CHECK_ARG(c->golden_ready, "qg_verify: no golden result (call qg_golden first)");
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    // Outputs written on another stream must be complete before the compare.
+    CTX_CUDA(c, cudaDeviceSynchronize());
+    CTX_CUDA(c, cudaMemsetAsync(c->counters, 0, 2 * sizeof(unsigned long long), c->stream));
+    for (auto& cp : c->copies) {
+        int rc = qg::verify_words(cp.out, cp.golden, c->layout.out_bytes / 4, c->counters, c->log, c->log_cap, c->stream);
+        if (rc) return fail(c, rc);
+        if (c->layout.cksum_bytes) {
+            rc = qg::verify_words(cp.cksum, cp.golden_cksum, c->layout.cksum_bytes / 4, c->counters, c->log, c->log_cap,
+                                  c->stream);
+            if (rc) return fail(c, rc);
+        }
+    }
+    unsigned long long h[2] = {0, 0};
+    CTX_CUDA(c, cudaMemcpyAsync(h, c->counters, sizeof(h), cudaMemcpyDeviceToHost, c->stream));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    int st = qg_device_status(c->device);
+    if (st) return fail(c, st);
+    *mismatches = h[0];
+    return QG_OK;
+}
+
+int qg_mismatch_log(qg_ctx* c, qg_mismatch* out, int cap) {
+    QG_CHECK_ARG(c && (out || cap == 0), "qg_mismatch_log: null argument");
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    unsigned long long h[2] = {0, 0};
+    CTX_CUDA(c, cudaMemcpy(h, c->counters, sizeof(h), cudaMemcpyDeviceToHost));
+    int n = (int)(h[1] < (unsigned long long)c->log_cap ? h[1] : (unsigned long long)c->log_cap);
+    if (n > cap) n = cap;
+    if (n > 0) CTX_CUDA(c, cudaMemcpy(out, c->log, sizeof(qg_mismatch) * (size_t)n, cudaMemcpyDeviceToHost));
+    return n;
+}
+
+int qg_inject(qg_ctx* c) {
+    QG_CHECK_ARG(c, "qg_inject: null context");
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    CTX_CUDA(c, cudaDeviceSynchronize());
+    int rc = qg::flip_bit(c->copies[0].out, c->stream);
+    if (rc) return fail(c, rc);
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    return QG_OK;
+}
+
+double qg_ops_per_launch(const qg_ctx* c) { return c ? c->layout.ops : 0.0; }
+double qg_bytes_per_launch(const qg_ctx* c) { return c ? c->layout.bytes : 0.0; }
+
+int qg_upload(qg_ctx* c, int copy, const void* const* host, void* stream) {
+    QG_CHECK_ARG(c && host && copy >= 0 && copy < (int)c->copies.size(), "qg_upload: bad argument");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < c->layout.n_ops; ++i) {
+        QG_CHECK_ARG(host[i], "qg_upload: null host operand %d", i);
+        CTX_CUDA(c, cudaMemcpyAsync(c->copies[(size_t)copy].op[i], host[i], c->layout.op_bytes[i],
+                                    cudaMemcpyHostToDevice, s));
+    }
+    return QG_OK;
+}
+
+int qg_download(qg_ctx* c, int copy, void* host_out, void* stream) {
+    QG_CHECK_ARG(c && host_out && copy >= 0 && copy < (int)c->copies.size(), "qg_download: bad argument");
+    CTX_CUDA(c, cudaMemcpyAsync(host_out, c->copies[(size_t)copy].out, c->layout.out_bytes, cudaMemcpyDeviceToHost,
+                                static_cast<cudaStream_t>(stream)));
+    return QG_OK;
+}
+
+// Launch one GEMM on copy `copy` (used by the end-to-end path after qg_upload).
+int qg_run_copy(qg_ctx* c, int copy, void* stream) {
+    QG_CHECK_ARG(c && copy >= 0 && copy < (int)c->copies.size(), "qg_run_copy: bad argument");
+    int rc = qg::launch_copy(c->cfg, c->layout, c->copies[(size_t)copy], static_cast<cudaStream_t>(stream));
+    return rc ? fail(c, rc) : QG_OK;
+}
+
+int qg_tensor(qg_ctx* c, int copy, int slot, void** ptr, uint64_t* bytes) {
+    QG_CHECK_ARG(c && ptr && copy >= 0 && copy < (int)c->copies.size(), "qg_tensor: bad argument");
+    const qg::CopyBuffers& cp = c->copies[(size_t)copy];
+    const qg::Layout& L = c->layout;
+    void* p = nullptr;
+    uint64_t b = 0;
+    if (slot >= 0 && slot < L.n_ops) { p = cp.op[slot]; b = L.op_bytes[slot]; }
+    else if (slot == 5) { p = cp.out; b = L.out_bytes; }
+    else if (slot == 6) { p = cp.golden; b = L.out_bytes; }
+    else if (slot == 7) { p = cp.cksum; b = L.cksum_bytes; }
+    else { qg::set_error("qg_tensor: no slot %d for this format", slot); return QG_ERR_ARG; }
+    *ptr = p;
+    if (bytes) *bytes = b;
+    return QG_OK;
+}
+
+int qg_last_error(const qg_ctx* c, char* buf, size_t len) {
+    if (!buf || len == 0) return QG_ERR_ARG;
+    const char* msg = (c && !c->err.empty()) ? c->err.c_str() : qg::last_error();
+    snprintf(buf, len, "%s", msg);
+    return QG_OK;
+}
+
+int qg_abi_version(void) { return QG_ABI_VERSION; }
+
+int qg_synchronize(qg_ctx* c) {
+    QG_CHECK_ARG(c, "qg_synchronize: null context");
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    CTX_CUDA(c, cudaDeviceSynchronize());
+    int st = qg_device_status(c->device);
+    return st ? fail(c, st) : QG_OK;
+}
+
+int qg_mem_info(int device, uint64_t* free_bytes, uint64_t* total_bytes) {
+    QG_CHECK_ARG(free_bytes && total_bytes, "qg_mem_info: null argument");
+    QG_CUDA(cudaSetDevice(device));
+    size_t f = 0, t = 0;
+    QG_CUDA(cudaMemGetInfo(&f, &t));
+    *free_bytes = f;
+    *total_bytes = t;
+    return QG_OK;
+}
+
+} // extern "C"

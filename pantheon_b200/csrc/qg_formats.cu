@@ -1,0 +1,71 @@
+// qg_formats.cu -- per-format layout, generation and launch for the context API.
+//
+// Format defaults are the workload configurations: INT8 W8A8 at M=N=K=8192
+// with bf16 output; FP8 block-128 at M=N=8192, K=16384; NVFP4 at 16384^3;
+// W4A16 at M=1, K=8192, N=28672.  Tensor ids give every tensor of every copy
+// its own generator stream: id = 8 * copy + slot.
+#include "qg_formats.cuh"
+
+namespace qg {
+
+static int out_elem_bytes(int out_type) { return out_type == QG_OUT_BF16 ? 2 : 4; }
+
+int layout_for(const qg_cfg& cfg, Layout* L) {
+    Layout l;
+    l.format = cfg.format;
+    l.out_type = cfg.out_type;
+    switch (cfg.format) {
+        case QG_FMT_INT8: {
+            l.M = cfg.m > 0 ? cfg.m : 8192;
+            l.N = cfg.n > 0 ? cfg.n : 8192;
+            l.K = cfg.k > 0 ? cfg.k : 8192;
+            QG_CHECK_ARG(l.K % 16 == 0 && l.K <= 131072, "INT8: K=%d must be a multiple of 16 and <= 131072", l.K);
+            QG_CHECK_ARG(l.out_type == QG_OUT_BF16 || l.out_type == QG_OUT_F32 || l.out_type == QG_OUT_S32,
+                         "INT8: bad out_type %d", l.out_type);
+            l.n_ops = 4;
+            l.op_bytes[0] = (uint64_t)l.M * l.K;
+            l.op_bytes[1] = (uint64_t)l.N * l.K;
+            l.op_bytes[2] = 4ull * l.M;
+            l.op_bytes[3] = 4ull * l.N;
+            l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
+            l.cksum_bytes = 4ull * l.M;
+            l.ops = 2.0 * l.M * (double)l.N * l.K;
+            l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes + l.cksum_bytes);
+            break;
+        }
+        default:
+            set_error("format %d is not available in this build", cfg.format);
+            return QG_ERR_ARG;
+    }
+    QG_CHECK_ARG(l.M > 0 && l.N > 0 && l.K > 0, "empty shape %dx%dx%d", l.M, l.N, l.K);
+    *L = l;
+    return QG_OK;
+}
+
+int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_index, uint64_t seed, cudaStream_t s) {
+    const uint32_t base = 8u * (uint32_t)copy_index;
+    int rc = QG_OK;
+    switch (cfg.format) {
+        case QG_FMT_INT8:
+            if ((rc = gen_i8(cp.op[0], L.op_bytes[0], seed, base + 0, s))) return rc;
+            if ((rc = gen_i8(cp.op[1], L.op_bytes[1], seed, base + 1, s))) return rc;
+            if ((rc = gen_uniform(cp.op[2], (uint64_t)L.M, 0.001f, 0.01f, seed, base + 2, s))) return rc;
+            if ((rc = gen_uniform(cp.op[3], (uint64_t)L.N, 0.001f, 0.01f, seed, base + 3, s))) return rc;
+            return QG_OK;
+        default:
+            set_error("format %d is not available in this build", cfg.format);
+            return QG_ERR_ARG;
+    }
+}
+
+int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaStream_t s) {
+    switch (cfg.format) {
+        case QG_FMT_INT8:
+            return gemm_i8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, cp.cksum, L.M, L.N, L.K, s);
+        default:
+            set_error("format %d is not available in this build", cfg.format);
+            return QG_ERR_ARG;
+    }
+}
+
+} // namespace qg

@@ -1,0 +1,51 @@
+// qg_formats.cuh -- per-format buffer layout, operand generation and launch,
+// shared by the context API; plus the internal entry points of each kernel file.
+#pragma once
+
+#include "qg_common.cuh"
+
+namespace qg {
+
+constexpr int kMaxOperands = 5;
+
+// Sizes of one operand set and its results for a given configuration.
+struct Layout {
+    int format = 0;
+    int M = 0, N = 0, K = 0;
+    int out_type = QG_OUT_BF16;
+    int n_ops = 0;
+    uint64_t op_bytes[kMaxOperands] = {};
+    uint64_t out_bytes = 0;
+    uint64_t cksum_bytes = 0;
+    uint64_t scratch_bytes = 0;
+    double ops = 0.0;     // useful arithmetic per launch (2 M N K)
+    double bytes = 0.0;   // algorithmic bytes moved per launch
+    float global_a = 1.0f, global_b = 1.0f;   // NVFP4 per-tensor scales
+};
+
+// Device buffers of one operand copy.
+struct CopyBuffers {
+    void* op[kMaxOperands] = {};
+    void* out = nullptr;
+    void* golden = nullptr;
+    void* cksum = nullptr;
+    void* golden_cksum = nullptr;
+    void* scratch = nullptr;
+    float global_a = 1.0f, global_b = 1.0f;
+};
+
+int layout_for(const qg_cfg& cfg, Layout* L);
+int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_index, uint64_t seed, cudaStream_t s);
+int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaStream_t s);
+
+// Kernel entry points (one per kernel file).
+int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type, void* row_cksum,
+            int M, int N, int K, cudaStream_t stream);
+int gen_i8(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, cudaStream_t s);
+int gen_uniform(void* out, uint64_t n, float lo, float hi, uint64_t seed, uint32_t tensor_id, cudaStream_t s);
+int gen_normal(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, cudaStream_t s);
+int verify_words(const void* actual, const void* expected, uint64_t nwords, void* counters, void* log, int log_cap,
+                 cudaStream_t s);
+int flip_bit(void* word, cudaStream_t s);
+
+} // namespace qg

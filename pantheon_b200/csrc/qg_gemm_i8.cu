@@ -1,0 +1,349 @@
+// qg_gemm_i8.cu -- INT8 x INT8 -> INT32 GEMM on the sm_100a tensor cores
+// (tcgen05.mma kind::i8), with the fp32 per-row / per-column dequant epilogue.
+//
+// Replaces the body of the reference's "Quantized GEMM" workload kernel
+// (kernels/common/ai_workload_template.h:157-177, kind 3), which is a synthetic
+// integer hash loop, with the GEMM the workload is named after:
+//     C[m,n] = out( f32(sum_k A[m,k] B[n,k]) * sa[m] * sb[n] )
+//
+// Structure (one persistent CTA per SM, 256 threads):
+//   warp 0      TMA producer: A 128x128 and B 256x128 int8 tiles per stage,
+//               128-byte swizzled, into a 4-stage shared-memory ring.
+//   warp 1      MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=32) per stage
+//               into a TMEM accumulator; tcgen05.commit frees the stage.
+//   warp 2      TMEM allocator (512 columns = two 128x256 s32 accumulators,
+//               so the epilogue of tile i overlaps the mainloop of tile i+1).
+//   warps 4-7   epilogue: tcgen05.ld 32 columns at a time, convert, scale,
+//               round, store, and fold the INT32 accumulators into a per-row
+//               checksum (a bit-exact fingerprint of the integer result).
+// Every barrier wait is bounded (qg_ptx.cuh); on expiry the kernel records
+// the site in the device status word, drains its in-flight copies and MMAs,
+// frees TMEM and returns.
+#include "qg_common.cuh"
+
+#include <cuda_bf16.h>
+
+namespace qg {
+namespace i8 {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;            // int8 elements = bytes = one 128-byte swizzle row
+constexpr int UMMA_K = 32;         // K per tcgen05.mma kind::i8
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK;   // 16 KB
+constexpr int B_BYTES = BN * BK;   // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int ACC_COLS = BN;       // s32 accumulator columns per buffer
+constexpr int TMEM_COLS = 2 * ACC_COLS;
+constexpr int THREADS = 256;
+constexpr int EPI_WARP0 = 4;
+constexpr int GROUP_M = 16;        // tile rasterisation: 16 row-tiles share B tiles in L2
+
+// Barrier block that follows the operand ring in shared memory.
+struct Barriers {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+
+// Status sites: kernel id 1 (INT8 GEMM) in the high half.
+constexpr uint32_t SITE_PRODUCER = 0x00010001u;
+constexpr uint32_t SITE_MMA_FULL = 0x00010002u;
+constexpr uint32_t SITE_MMA_TMEM = 0x00010003u;
+constexpr uint32_t SITE_EPI = 0x00010004u;
+
+struct Params {
+    int M, N, K;
+    const float* sa;
+    const float* sb;
+    void* C;
+    uint32_t* row_cksum;
+    DeviceStatus* status;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
+    const int group = GROUP_M * tiles_n;
+    const int g = t / group;
+    const int first_m = g * GROUP_M;
+    const int gm = min(tiles_m - first_m, GROUP_M);
+    const int r = t - g * group;
+    mt = first_m + r % gm;
+    nt = r / gm;
+}
+
+__device__ __forceinline__ uint32_t cksum_weight(uint32_t m, uint32_t n) {
+    return (m * 0x9E3779B1u + n * 0x85EBCA77u) | 1u;
+}
+
+template <int OUT>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment: the 128-byte swizzle pattern is a function of the
+    // address bits, and the UMMA descriptors assume base offset 0.
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * A_BYTES;
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tiles_m = (p.M + BM - 1) / BM;
+    const int tiles_n = (p.N + BN - 1) / BN;
+    const int tiles = tiles_m * tiles_n;
+    const int nk = (p.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&bars->full[s], 1); mbar_init(&bars->empty[s], 1); }
+        for (int a = 0; a < 2; ++a) { mbar_init(&bars->tmem_full[a], 1); mbar_init(&bars->tmem_empty[a], 4 * 32); }
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 2) {
+        tmem_alloc(&bars->tmem_base, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+    volatile int* abort_flag = &bars->abort;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------ producer
+        uint32_t stage = 0, phase = 0;
+        uint32_t armed = 0, armed_phase = 0;   // bitmasks over stages, for the abort drain
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            int mt, nt;
+            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER)) { ok = false; break; }
+                mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
+                tma_load_2d(sA + stage * A_BYTES, &tmA, &bars->full[stage], kb * BK, mt * BM);
+                tma_load_2d(sB + stage * B_BYTES, &tmB, &bars->full[stage], kb * BK, nt * BN);
+                armed |= 1u << stage;
+                armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        if (!ok) {
+            // Let every copy already issued land before the CTA's shared memory goes away.
+            for (int s = 0; s < STAGES; ++s)
+                if (armed & (1u << s)) mbar_wait(&bars->full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------------ MMA issuer
+        constexpr uint32_t IDESC = make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, BM, BN);
+        uint32_t stage = 0, phase = 0;
+        bool ok = true, issued = false;
+        int iter = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++iter) {
+            const uint32_t acc = iter & 1;
+            const uint32_t acc_phase = (iter >> 1) & 1;
+            if (!mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.status, SITE_MMA_TMEM)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_MMA_FULL)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+                const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                for (int k = 0; k < BK / UMMA_K; ++k) {
+                    const uint64_t ad = make_sdesc_kmajor_sw128(a_addr + k * UMMA_K);
+                    const uint64_t bd = make_sdesc_kmajor_sw128(b_addr + k * UMMA_K);
+                    umma_i8(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+                }
+                issued = true;
+                umma_commit(&bars->empty[stage]);
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (ok) umma_commit(&bars->tmem_full[acc]);
+        }
+        if (!ok && issued) {
+            // Wait for the MMAs already in flight before TMEM is released.
+            umma_commit(&bars->drain);
+            mbar_wait(&bars->drain, 0, nullptr, nullptr, 0);
+        }
+    } else if (warp >= EPI_WARP0) {
+        // ------------------------------------------------------------ epilogue
+        const int ew = warp - EPI_WARP0;               // TMEM lane quarter of this warp
+        const int row = ew * 32 + lane;
+        int iter = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
+            int mt, nt;
+            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            const uint32_t acc = iter & 1;
+            const uint32_t acc_phase = (iter >> 1) & 1;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&bars->tmem_full[acc], acc_phase, abort_flag, p.status, SITE_EPI) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+
+            const int m = mt * BM + row;
+            const bool row_ok = m < p.M;
+            const float sam = (OUT != QG_OUT_S32 && row_ok) ? __ldg(p.sa + m) : 0.0f;
+            uint32_t ck = 0;
+            const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * ACC_COLS;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(t_row + c, r);
+                tmem_ld_wait();
+                const int n0 = nt * BN + c;
+                if (!row_ok || n0 >= p.N) continue;
+                const bool full_chunk = (n0 + 32 <= p.N);
+                if (p.row_cksum) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (full_chunk || n0 + i < p.N) ck += r[i] * cksum_weight((uint32_t)m, (uint32_t)(n0 + i));
+                }
+                if (OUT == QG_OUT_S32) {
+                    int32_t* dst = static_cast<int32_t*>(p.C) + (size_t)m * p.N + n0;
+                    if (full_chunk && (p.N % 4) == 0) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<uint4*>(dst + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (n0 + i < p.N) dst[i] = (int32_t)r[i];
+                    }
+                    continue;
+                }
+                float f[32];
+                if (full_chunk) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + i));
+                        f[i + 0] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 0]), sam), s4.x);
+                        f[i + 1] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 1]), sam), s4.y);
+                        f[i + 2] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 2]), sam), s4.z);
+                        f[i + 3] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 3]), sam), s4.w);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float sbn = (n0 + i < p.N) ? __ldg(p.sb + n0 + i) : 0.0f;
+                        f[i] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i]), sam), sbn);
+                    }
+                }
+                if (OUT == QG_OUT_F32) {
+                    float* dst = static_cast<float*>(p.C) + (size_t)m * p.N + n0;
+                    if (full_chunk && (p.N % 4) == 0) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (n0 + i < p.N) dst[i] = f[i];
+                    }
+                } else {
+                    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
+                    if (full_chunk && (p.N % 8) == 0) {
+                        uint32_t w[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+                            w[i] = *reinterpret_cast<uint32_t*>(&h);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4)
+                            *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (n0 + i < p.N) dst[i] = __float2bfloat16_rn(f[i]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&bars->tmem_empty[acc]);
+            if (p.row_cksum && row_ok) atomicAdd(p.row_cksum + m, ck);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+template <int OUT>
+static int launch(const void* A, const void* B, const float* sa, const float* sb, void* C, uint32_t* cksum,
+                  int M, int N, int K, cudaStream_t stream) {
+    DeviceInfo* info = nullptr;
+    int rc = current_device_info(&info);
+    if (rc) return rc;
+    DeviceStatus* status = nullptr;
+    if ((rc = device_status_ptr(&status))) return rc;
+
+    CUtensorMap tmA, tmB;
+    if ((rc = make_tmap_2d(&tmA, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)M, (uint64_t)K, BK, BM,
+                           CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    if ((rc = make_tmap_2d(&tmB, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)N, (uint64_t)K, BK, BN,
+                           CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+
+    static bool attr_set[64] = {};
+    int dev = 0;
+    QG_CUDA(cudaGetDevice(&dev));
+    if (!attr_set[dev & 63]) {
+        QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<QG_OUT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<QG_OUT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<QG_OUT_S32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        attr_set[dev & 63] = true;
+    }
+    if (cksum) QG_CUDA(cudaMemsetAsync(cksum, 0, sizeof(uint32_t) * (size_t)M, stream));
+
+    Params p{M, N, K, sa, sb, C, cksum, status};
+    const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
+    const int grid = tiles < info->sm_count ? tiles : info->sm_count;
+    gemm_i8_kernel<OUT><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, p);
+    QG_CUDA(cudaGetLastError());
+    return QG_OK;
+}
+
+} // namespace i8
+
+int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type, void* row_cksum,
+            int M, int N, int K, cudaStream_t stream) {
+    QG_CHECK_ARG(A && B && C, "qg_gemm_i8: null operand or output");
+    QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemm_i8: empty shape %dx%dx%d", M, N, K);
+    QG_CHECK_ARG(K % 16 == 0, "qg_gemm_i8: K=%d must be a multiple of 16 (TMA row stride)", K);
+    QG_CHECK_ARG(K <= 131072, "qg_gemm_i8: K=%d exceeds 131072 (INT32 accumulator range)", K);
+    QG_CHECK_ARG(out_type == QG_OUT_S32 || (sa && sb), "qg_gemm_i8: scales required for a dequantised output");
+    const float* fsa = static_cast<const float*>(sa);
+    const float* fsb = static_cast<const float*>(sb);
+    uint32_t* ck = static_cast<uint32_t*>(row_cksum);
+    switch (out_type) {
+        case QG_OUT_BF16: return i8::launch<QG_OUT_BF16>(A, B, fsa, fsb, C, ck, M, N, K, stream);
+        case QG_OUT_F32: return i8::launch<QG_OUT_F32>(A, B, fsa, fsb, C, ck, M, N, K, stream);
+        case QG_OUT_S32: return i8::launch<QG_OUT_S32>(A, B, fsa, fsb, C, ck, M, N, K, stream);
+        default: set_error("qg_gemm_i8: unknown out_type %d", out_type); return QG_ERR_ARG;
+    }
+}
+
+} // namespace qg
+
+extern "C" int qg_gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type,
+                          void* row_checksums, int M, int N, int K, void* stream) {
+    return qg::gemm_i8(A, B, sa, sb, C, out_type, row_checksums, M, N, K, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,204 @@
+"""Python entry points over the C ABI (torch tensors in, device pointers out).
+
+These mirror, one for one, the pieces of the reference workload harness
+(kernels/common/ai_workload_template.h:85-94 init, :157-177 kernel, :343-349
+verify, :351-380 main) that include/pantheon_qgemm.h replaces.  Every call goes
+to the sm_100a kernels in libpantheon_qgemm.so; there is no other path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._lib import (QG_FMT_INT8, QG_OUT_BF16, QG_OUT_F32, QG_OUT_S32, QGCfg, QGMismatch, QGError, check,
+                   last_error, load_library)
+
+_OUT_DTYPES = {QG_OUT_BF16: torch.bfloat16, QG_OUT_F32: torch.float32, QG_OUT_S32: torch.int32}
+
+
+class _DeviceBytes:
+    """A raw device allocation of the library seen as a uint8 array (CUDA array interface)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(device) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("pantheon_b200 kernels take CUDA tensors only (no CPU fallback)")
+        if t is not None and not t.is_contiguous():
+            raise ValueError("pantheon_b200 kernels take contiguous tensors")
+
+
+def gemm_i8(A: torch.Tensor, B: torch.Tensor, sa: torch.Tensor | None, sb: torch.Tensor | None,
+            out_type: int = QG_OUT_BF16, row_checksums: bool = False, out: torch.Tensor | None = None):
+    """C = out(f32(A @ B^T) * sa[:, None] * sb[None, :]) on the tcgen05 INT8 path.
+
+    A int8 [M,K], B int8 [N,K] (K contiguous, K % 16 == 0); sa fp32 [M]; sb fp32 [N].
+    Returns C (and the uint32 per-row checksums of the INT32 accumulators when
+    row_checksums=True).  Asynchronous on the current stream.
+    """
+    _require_cuda(A, B, sa, sb)
+    if A.dtype != torch.int8 or B.dtype != torch.int8:
+        raise ValueError("A and B must be int8")
+    M, K = A.shape
+    N, K2 = B.shape
+    if K != K2:
+        raise ValueError(f"K mismatch {K} vs {K2}")
+    if out is None:
+        out = torch.empty((M, N), dtype=_OUT_DTYPES[out_type], device=A.device)
+    ck = torch.empty((M,), dtype=torch.int32, device=A.device) if row_checksums else None
+    lib = load_library()
+    check("qg_gemm_i8", lib.qg_gemm_i8(_ptr(A), _ptr(B), _ptr(sa), _ptr(sb), _ptr(out), out_type, _ptr(ck),
+                                       M, N, K, _stream(A.device)))
+    return (out, ck) if row_checksums else out
+
+
+def gen_i8(n: int, seed: int, tensor_id: int, device="cuda") -> torch.Tensor:
+    """Counter-based uniform int8 in [-127, 127] (same bits as the CPU oracle)."""
+    out = torch.empty(((n + 15) // 16) * 16, dtype=torch.int8, device=device)
+    check("qg_gen_i8", load_library().qg_gen_i8(_ptr(out), n, seed, tensor_id, _stream(out.device)))
+    return out[:n]
+
+
+def gen_uniform_f32(n: int, lo: float, hi: float, seed: int, tensor_id: int, device="cuda") -> torch.Tensor:
+    out = torch.empty((n,), dtype=torch.float32, device=device)
+    check("qg_gen_uniform_f32",
+          load_library().qg_gen_uniform_f32(_ptr(out), n, lo, hi, seed, tensor_id, _stream(out.device)))
+    return out
+
+
+def gen_normal_f32(n: int, seed: int, tensor_id: int, device="cuda") -> torch.Tensor:
+    out = torch.empty((n,), dtype=torch.float32, device=device)
+    check("qg_gen_normal_f32", load_library().qg_gen_normal_f32(_ptr(out), n, seed, tensor_id, _stream(out.device)))
+    return out
+
+
+def verify_words(actual: torch.Tensor, expected: torch.Tensor, log_cap: int = 16):
+    """Device word compare: returns (mismatching words, [(index, expected, actual), ...])."""
+    _require_cuda(actual, expected)
+    nwords = actual.numel() * actual.element_size() // 4
+    counters = torch.zeros((2,), dtype=torch.int64, device=actual.device)
+    log = torch.zeros((max(log_cap, 1), 2), dtype=torch.int64, device=actual.device)
+    check("qg_verify_words", load_library().qg_verify_words(_ptr(actual), _ptr(expected), nwords, _ptr(counters),
+                                                            _ptr(log), log_cap, _stream(actual.device)))
+    c = counters.cpu().tolist()
+    entries = []
+    for idx, packed in log[: min(c[1], log_cap)].cpu().tolist():
+        entries.append((idx, packed & 0xFFFFFFFF, (packed >> 32) & 0xFFFFFFFF))
+    return c[0], entries
+
+
+def device_status(device: int = 0) -> int:
+    """QG_OK, or QG_ERR_DEVICE_TIMEOUT if a kernel's bounded wait expired (clears it)."""
+    return load_library().qg_device_status(device)
+
+
+class Workload:
+    """One workload instance (the qg_ctx of the C ABI): operands, outputs, golden."""
+
+    SLOT_OUT, SLOT_GOLDEN, SLOT_CKSUM = 5, 6, 7
+
+    def __init__(self, fmt: int = QG_FMT_INT8, m: int = 0, n: int = 0, k: int = 0, copies: int = 1,
+                 seed: int = 1, out_type: int = QG_OUT_BF16, device: int = 0):
+        self.lib = load_library()
+        self.device = device
+        self.cfg = QGCfg(fmt, m, n, k, out_type, copies, seed)
+        h = C.c_void_p()
+        code = self.lib.qg_create(C.byref(h), device, C.byref(self.cfg))
+        if code != 0:
+            raise QGError("qg_create", code, last_error(None))
+        self.ctx = h
+
+    def _check(self, where, code):
+        return check(where, code, self.ctx)
+
+    def close(self):
+        if getattr(self, "ctx", None):
+            self.lib.qg_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def ops_per_launch(self) -> float:
+        return self.lib.qg_ops_per_launch(self.ctx)
+
+    @property
+    def bytes_per_launch(self) -> float:
+        return self.lib.qg_bytes_per_launch(self.ctx)
+
+    def fill(self, seed: int):
+        self._check("qg_fill", self.lib.qg_fill(self.ctx, seed))
+
+    def golden(self):
+        self._check("qg_golden", self.lib.qg_golden(self.ctx))
+
+    def run(self, iters: int = 1, stream=None):
+        s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)
+        self._check("qg_run", self.lib.qg_run(self.ctx, iters, s))
+
+    def run_copy(self, copy: int, stream=None):
+        s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)
+        self._check("qg_run_copy", self.lib.qg_run_copy(self.ctx, copy, s))
+
+    def synchronize(self):
+        self._check("qg_synchronize", self.lib.qg_synchronize(self.ctx))
+
+    def verify(self) -> int:
+        mm = C.c_uint64()
+        self._check("qg_verify", self.lib.qg_verify(self.ctx, C.byref(mm)))
+        return mm.value
+
+    def mismatch_log(self, cap: int = 16):
+        arr = (QGMismatch * cap)()
+        n = self.lib.qg_mismatch_log(self.ctx, arr, cap)
+        if n < 0:
+            self._check("qg_mismatch_log", n)
+        return [(arr[i].index, arr[i].expected, arr[i].actual) for i in range(n)]
+
+    def inject(self):
+        self._check("qg_inject", self.lib.qg_inject(self.ctx))
+
+    def tensor_ptr(self, copy: int, slot: int):
+        p = C.c_void_p()
+        b = C.c_uint64()
+        self._check("qg_tensor", self.lib.qg_tensor(self.ctx, copy, slot, C.byref(p), C.byref(b)))
+        return p.value, b.value
+
+    def tensor(self, copy: int, slot: int, dtype=torch.uint8) -> torch.Tensor:
+        """Copy a device tensor of the context to a new CUDA tensor (raw bytes viewed as dtype)."""
+        ptr, nbytes = self.tensor_ptr(copy, slot)
+        torch.cuda.synchronize(self.device)
+        view = torch.as_tensor(_DeviceBytes(ptr, nbytes), device=f"cuda:{self.device}")
+        return view.clone().view(dtype)
+
+    def upload(self, copy: int, host_tensors, stream=None):
+        arr = (C.c_void_p * len(host_tensors))(*[t.data_ptr() for t in host_tensors])
+        s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)
+        self._check("qg_upload", self.lib.qg_upload(self.ctx, copy, arr, s))
+
+    def download(self, copy: int, host_out, stream=None):
+        s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)
+        self._check("qg_download", self.lib.qg_download(self.ctx, copy, C.c_void_p(host_out.data_ptr()), s))

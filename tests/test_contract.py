@@ -1,0 +1,104 @@
+"""The drop-in boundary, checked without a GPU.
+
+* The C-ABI library loads on a machine without a driver and exports every
+  function include/pantheon_qgemm.h declares.
+* The quantized_gemm binary keeps the reference's argv contract
+  (ai_workload_template.h:352: fewer than 3 arguments -> exit 1) and, with no
+  usable GPU, fails loudly: a reason on stderr, a non-zero exit, and no
+  Throughput line (common.h:444-465) -- never a silent CPU fallback.
+* The output parser restated from the runner reads the reference's own MOCK
+  binary (built from its sources into oracle/_ref) the way the runner does,
+  so the GPU tests can hold our binary to the same reader.
+"""
+import subprocess
+
+import pytest
+
+from tests.contract_parse import parse_kernel_output
+
+
+def _gpu_visible() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+def test_library_exports_every_header_symbol(qglib):
+    from pantheon_b200 import _lib
+    declared = _lib.header_symbols()
+    assert len(declared) >= 20
+    missing = [s for s in declared if not hasattr(qglib, s)]
+    assert missing == [], f"declared in include/pantheon_qgemm.h but not exported: {missing}"
+    assert qglib.qg_abi_version() == 1
+
+
+def test_binary_needs_three_arguments(qglib):
+    from pantheon_b200 import BIN_PATH
+    for args in ([], ["0"], ["0", "1"]):
+        proc = subprocess.run([str(BIN_PATH), *args], capture_output=True, text=True, timeout=60)
+        assert proc.returncode == 1
+        assert "Throughput:" not in proc.stdout
+
+
+@pytest.mark.skipif(_gpu_visible(), reason="checks the no-GPU failure path")
+def test_binary_without_gpu_fails_loudly(qglib):
+    from pantheon_b200 import BIN_PATH
+    proc = subprocess.run([str(BIN_PATH), "0", "1", "5", "--verify"], capture_output=True, text=True, timeout=60)
+    assert proc.returncode != 0
+    assert "[PANTHEON ERROR]" in proc.stderr
+    assert "Throughput:" not in proc.stdout
+    assert "Verification: PASS" not in proc.stdout
+    status = parse_kernel_output(proc.stdout, proc.stderr, proc.returncode, "quantized_gemm")[2]
+    assert status == "FAIL"
+
+
+@pytest.mark.skipif(_gpu_visible(), reason="checks the no-GPU failure path")
+def test_python_entry_points_have_no_cpu_fallback(qglib):
+    import ctypes as C
+    import pantheon_b200 as pb
+    h = C.c_void_p()
+    cfg = pb._lib.QGCfg(pb.QG_FMT_INT8, 128, 256, 128, 0, 1, 0)
+    rc = qglib.qg_create(C.byref(h), 0, C.byref(cfg))
+    assert rc == pb._lib.QG_ERR_CUDA
+    with pytest.raises(pb.QGError):
+        pb.Workload(pb.QG_FMT_INT8, 128, 256, 128)
+
+
+def test_library_rejects_bad_shapes_before_touching_a_device(qglib):
+    import ctypes as C
+    import pantheon_b200 as pb
+    rc = qglib.qg_gemm_i8(None, None, None, None, None, 0, None, 128, 128, 128, None)
+    assert rc == pb._lib.QG_ERR_ARG
+    cfg = pb._lib.QGCfg(pb.QG_FMT_INT8, 128, 128, 100, 0, 1, 0)   # K % 16 != 0
+    b = C.c_uint64()
+    assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == pb._lib.QG_ERR_ARG
+    cfg = pb._lib.QGCfg(pb.QG_FMT_INT8, 8192, 8192, 8192, 0, 1, 0)
+    assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == 0
+    # A, B, sa, sb, C and golden (bf16), row checksums and golden checksums
+    assert b.value == 8192 * 8192 * 2 + 8 * 8192 + 2 * 8192 * 8192 * 2 + 2 * 4 * 8192 + 4096
+
+
+def test_runner_parser_on_reference_mock_binary():
+    from pathlib import Path
+    ref = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "quantized_gemm_mock"
+    if not ref.exists():
+        pytest.skip("reference MOCK binary not built (oracle/Makefile needs the reference tree)")
+    clean = subprocess.run([str(ref), "0", "1", "5", "--verify"], capture_output=True, text=True, timeout=120)
+    t, unit, status, err, kept = parse_kernel_output(clean.stdout, clean.stderr, clean.returncode, "quantized_gemm")
+    assert status == "PASS" and unit == "ai-ops/s" and t > 0
+    bad = subprocess.run([str(ref), "0", "1", "5", "--verify", "--inject_error"], capture_output=True, text=True,
+                         timeout=120)
+    assert bad.returncode == 1
+    assert parse_kernel_output(bad.stdout, bad.stderr, bad.returncode, "quantized_gemm")[2] == "FAIL"
+
+
+def test_parser_rules():
+    assert parse_kernel_output("Throughput:\t12.5   TOPS\n", "", 0, "quantized_gemm")[:3] == (12.5, "TOPS", "PASS")
+    assert parse_kernel_output("Throughput: 1 TOPS\nVerification: FAIL (3 mismatches)\n", "", 0)[2] == "FAIL"
+    assert parse_kernel_output("Throughput: 1 TOPS\n[SDC FAULT][X] bad\n", "", 0)[2] == "FAIL"
+    assert parse_kernel_output("Throughput: nan TOPS\n", "", 0)[2] == "FAIL"
+    assert parse_kernel_output("Throughput: 0.0 TOPS\n", "", 0, "quantized_gemm")[2] == "FAIL"
+    assert parse_kernel_output("Skipping: no B200\n", "", 0, "quantized_gemm")[2] == "SKIP"
+    assert parse_kernel_output("Throughput: 5 TOPS\n", "boom", 1)[2] == "FAIL"

@@ -1,0 +1,51 @@
+"""The quantized_gemm drop-in binary on a B200, read the way the runner reads it.
+
+Mirrors the reference CI's clean/inject pair (.github/workflows/ci.yml:81-101;
+tests/test_kernel_contract.py:174-183): a clean `--verify` run must print
+`Verification: PASS` and exit 0; `--inject_error` must print FAIL (plus an
+[SDC FAULT] line) and exit non-zero; output goes through the runner's parse rules.
+"""
+import subprocess
+
+import pytest
+
+from tests.contract_parse import parse_kernel_output
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(*args, timeout=600):
+    from pantheon_b200 import BIN_PATH
+    return subprocess.run([str(BIN_PATH), *map(str, args)], capture_output=True, text=True, timeout=timeout)
+
+
+def test_clean_verify_passes(cuda_device):
+    p = _run(0, 2, 50, "--verify", "--m", 2048, "--n", 2048, "--k", 2048)
+    assert p.returncode == 0, p.stdout + p.stderr
+    t, unit, status, err, kept = parse_kernel_output(p.stdout, p.stderr, p.returncode, "quantized_gemm")
+    assert status == "PASS" and unit == "TOPS" and t > 0
+    assert "Verification: PASS (0 mismatches)" in p.stdout
+    assert any(line.startswith("-> Mismatches:") for line in kept)
+
+
+def test_injected_fault_fails(cuda_device):
+    p = _run(0, 1, 50, "--verify", "--inject_error", "--m", 1024, "--n", 1024, "--k", 1024)
+    assert p.returncode != 0
+    assert "Verification: FAIL" in p.stdout
+    assert "[SDC FAULT]" in p.stdout
+    assert parse_kernel_output(p.stdout, p.stderr, p.returncode, "quantized_gemm")[2] == "FAIL"
+
+
+def test_default_configuration_runs(cuda_device):
+    """No shape flags: configs[1] (INT8 8192^3, bf16 out), as the runner launches it."""
+    p = _run(0, 2, 99, "--verify")
+    assert p.returncode == 0, p.stdout + p.stderr
+    t, unit, status, _, _ = parse_kernel_output(p.stdout, p.stderr, p.returncode, "quantized_gemm")
+    assert status == "PASS" and unit == "TOPS" and t > 100.0
+
+
+def test_unknown_flags_are_ignored(cuda_device):
+    p = _run(0, 1, 50, "--verify", "--block_size", 128, "--grid_size", 7, "--sync_mode", 1, "--frobnicate",
+             "--m", 512, "--n", 512, "--k", 512, "--kernel_loops", 5, "--warmup_iters", 1)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "Verification: PASS" in p.stdout
