@@ -59,14 +59,32 @@ def _peaks():
     return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def _traffic():
+def _traffic(key: str):
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
     p = ROOT / "profiles" / "traffic.json"
     if p.exists():
         try:
-            return json.loads(p.read_text()).get("gemm_i8_8192")
+            return json.loads(p.read_text()).get(key)
         except Exception:
             return None
     return None
+
+
+def workload_spec(args, pb):
+    """What one step runs.  Default: configs[1] (INT8 8192^3), the metric's headline workload."""
+    if args.workload == "w4a16":
+        m = args.m or 1
+        return {"name": "w4a16", "fmt": pb.QG_FMT_W4A16, "shape": (m, 28672, 8192), "copies": 4, "seed": 3,
+                "unit": "GB/s", "bound": "hbm", "dtype": "bf16 x int4 (fp32 acc)", "launches_per_step": (m + 15) // 16,
+                "traffic_key": f"gemv_w4a16_m{m}",
+                "config": {"workload": f"configs[3] W4A16 group-128 GEMV M={m} K=8192 N=28672, bf16 out",
+                           "M": m, "N": 28672, "K": 8192, "seed": 3, "operand_sets": 4,
+                           "l2": "inputs larger than L2: 4 rotating weight sets of 125 MB each"}}
+    return {"name": "int8", "fmt": pb.QG_FMT_INT8, "shape": (M, N, K), "copies": 2, "seed": 1, "unit": "TOPS",
+            "bound": "tensor", "dtype": "int8", "launches_per_step": 1, "traffic_key": "gemm_i8_8192",
+            "config": {"workload": "configs[1] INT8 W8A8 GEMM 8192x8192x8192, bf16 out, fp32 row/col scales",
+                       "M": M, "N": N, "K": K, "seed": 1, "operand_sets": 2,
+                       "l2": "inputs larger than L2: 2 rotating operand sets of 128 MiB each"}}
 
 
 class ClockSampler:
@@ -206,13 +224,15 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     steps = max(1, args.steps)
     warm = max(3, args.warmup)
-    w = pb.Workload(pb.QG_FMT_INT8, M, N, K, copies=2, seed=1, device=local_rank)
-    w.fill(1)
+    wl = workload_spec(args, pb)
+    w = pb.Workload(wl["fmt"], *wl["shape"], copies=wl["copies"], seed=wl["seed"], device=local_rank)
+    w.fill(wl["seed"])
     w.golden()
     stream = torch.cuda.current_stream(dev)
     ops = w.ops_per_launch
+    nbytes = w.bytes_per_launch
 
-    # ---------------- device-timed region: K GEMMs, operands resident in HBM
+    # ---------------- device-timed region: K launches, operands resident in HBM
     w.run(warm)
     torch.cuda.synchronize(dev)
     uuid = None
@@ -235,7 +255,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     mismatches = w.verify()
     status = pb.device_status(local_rank)
 
-    # ---------------- end-to-end: host operands -> GEMM -> host result, through the C ABI
+    # ---------------- end-to-end: host operands -> kernel -> host result, through the C ABI
     host_ops = []
     for slot in range(4):
         t = w.tensor(0, slot).cpu().pin_memory()
@@ -271,31 +291,36 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if rank == 0:
         peaks = _peaks()
         per_launch_s = ms / 1e3 / steps
-        achieved = ops / per_launch_s / 1e12
-        peak = 2.0 * peaks["bf16_tflops"]
-        value = ops * steps * world / (ms_max / 1e3) / 1e12
-        e2e_value = ops * e2e_steps * world / (e2e_max / 1e3) / 1e12
-        traffic = _traffic()
+        if wl["unit"] == "TOPS":
+            work = ops / 1e12
+            peak = 2.0 * peaks["bf16_tflops"]
+            peak_src = f"2 x {peaks['source']} bf16 dense burst ({peaks['bf16_tflops']} TFLOP/s)"
+            extra = {"frac_of_datasheet_4500": work / per_launch_s / DATASHEET_INT8_TOPS}
+        else:
+            work = nbytes / 1e9
+            peak = peaks["hbm_gbs"]
+            peak_src = f"{peaks['source']} HBM copy bandwidth"
+            extra = {"frac_of_datasheet_8000": work / per_launch_s / 8000.0}
+        achieved = work / per_launch_s
+        value = work * steps * world / (ms_max / 1e3)
+        e2e_value = work * e2e_steps * world / (e2e_max / 1e3)
+        roof = {"bound": wl["bound"], "achieved": achieved, "peak": peak, "unit": wl["unit"],
+                "frac": achieved / peak, "traffic": _traffic(wl["traffic_key"]), "peak_source": peak_src}
+        roof.update(extra)
         result = {
-            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": steps, "warmup": warm,
+            "metric": METRIC, "value": value, "unit": wl["unit"], "n_gpus": world, "steps": steps, "warmup": warm,
             "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "configs[1] INT8 W8A8 GEMM 8192x8192x8192, bf16 out, fp32 row/col scales",
-                       "M": M, "N": N, "K": K, "seed": 1, "operand_sets": 2,
-                       "l2": "inputs larger than L2: 2 rotating operand sets of 128 MiB each",
-                       "parallelism": f"replicas x{world} (independent instance per GPU)"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"2 x {peaks['source']} bf16 dense burst ({peaks['bf16_tflops']} TFLOP/s)",
-                         "frac_of_datasheet_4500": achieved / DATASHEET_INT8_TOPS},
-            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_bytes,
+            "dtype": wl["dtype"], "data": "synthetic",
+            "config": dict(wl["config"], parallelism=f"replicas x{world} (independent instance per GPU)"),
+            "roofline": roof,
+            "e2e": {"value": e2e_value, "unit": wl["unit"], "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_bytes,
                     "path": "qg_upload + qg_run_copy + qg_download (pinned host buffers)", "steps": e2e_steps},
             "clocks": clocks,
-            "gpu_launches": steps,
+            "gpu_launches": steps * wl["launches_per_step"],
             "mismatches": int(mm_max),
             "device_timeouts": int(bad),
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and wl["name"] == "int8":
             result["cpu_baseline"] = cpu_baseline()
     w.close()
     if world > 1:
@@ -312,6 +337,9 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["int8", "w4a16"], default="int8",
+                    help="int8 = configs[1] (default, the headline); w4a16 = configs[3] GEMV")
+    ap.add_argument("--m", type=int, default=0, help="rows of the W4A16 activations (1, 8 or 16)")
     args = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -173,6 +173,22 @@ QG_API int  qg_gemm_i8(const void* A, const void* B, const void* sa, const void*
                 void* C, int out_type, void* row_checksums,
                 int M, int N, int K, void* stream);
 
+/* W4A16 group-128 decode GEMV / skinny GEMM on the CUDA cores:
+ *   Y[m,n] = sum_k X[m,k] * (q[k,n] - Z[k/128,n]) * S[k/128,n],  q = u - 8
+ *   X bf16 [M,K]; W uint32 [K/8, N] with nibble j of word (k8, n) = u(8*k8+j, n)
+ *   in [0,15]; S, Z fp16 [K/128, N]; Y bf16 or fp32 [M,N] (out_type).
+ *   K % 128 == 0, N % 4 == 0; X, W, Y 16-byte and S, Z 8-byte aligned.
+ *   `workspace` (qg_gemv_w4a16_workspace_bytes) holds the split-K partials and
+ *   per-column-block tickets: it must be zero-filled before its first use, and
+ *   every call leaves it ready for the next (calls sharing one workspace must
+ *   not overlap on the GPU).
+ * Replaces: the decode kernel of the llm_decode path
+ *   (kernels/llm_decode/llm_decode.cpp:28-46, a KV gather + FMA chain). */
+QG_API int  qg_gemv_w4a16_workspace_bytes(int M, int N, int K, uint64_t* bytes);
+QG_API int  qg_gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y,
+                          int out_type, int M, int N, int K,
+                          void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* Bounded-wait status of the most recent kernel on this device (QG_OK or
  * QG_ERR_DEVICE_TIMEOUT); clears the flag. Synchronous. */
 QG_API int  qg_device_status(int device);
@@ -194,6 +210,12 @@ QG_API int  qg_gen_uniform_f32(void* out, uint64_t n, float lo, float hi,
                         uint64_t seed, uint32_t tensor_id, void* stream);
 /* out[i] = standard normal deviate (seed, tensor_id, i), fp32. */
 QG_API int  qg_gen_normal_f32(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream);
+/* W4A16 operands of configs[3]: X bf16 [M,K] = bf16(N(0,1)); W packed as in
+ * qg_gemv_w4a16 with u uniform in [0,15] (q uniform in [-8,7]);
+ * S fp16 = f16(U[0.005, 0.02]), Z fp16 = f16(U[-0.5, 0.5]) per (group, n).
+ * Tensor ids: X = tid0, W = tid0+1, S = tid0+2, Z = tid0+3. */
+QG_API int  qg_gen_w4a16(void* X, void* W, void* S, void* Z, int M, int N, int K,
+                         uint64_t seed, uint32_t tid0, void* stream);
 
 #ifdef __cplusplus
 }

@@ -452,6 +452,31 @@ void qgo_gemv_w4a16(const uint16_t* X, const uint32_t* W, const uint16_t* S, con
     }
 }
 
+/* W4A16 operands: X = bf16(N(0,1)); u = top 4 bits of hash(k*N+n)
+ * packed 8 per word along K; S = f16(U[0.005,0.02]); Z = f16(U[-0.5,0.5]). */
+void qgo_gen_w4a16(uint16_t* X, uint32_t* W, uint16_t* S, uint16_t* Z, int M, int N, int K,
+                   uint64_t seed, uint32_t tid0) {
+    uint64_t nx = (uint64_t)M * K, nw = (uint64_t)K / 8 * N, ns = (uint64_t)K / 128 * N;
+    #pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)nx; ++i)
+        X[i] = qgo_f32_to_bf16(qgo_normal_from_hash(qgo_hash64(seed, tid0, (uint64_t)i)));
+    #pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)nw; ++i) {
+        uint64_t k8 = (uint64_t)i / (uint64_t)N, n = (uint64_t)i - k8 * (uint64_t)N;
+        uint32_t w = 0;
+        for (int j = 0; j < 8; ++j) {
+            uint64_t k = k8 * 8 + (uint64_t)j;
+            w |= (uint32_t)(qgo_hash64(seed, tid0 + 1, k * (uint64_t)N + n) >> 60) << (4 * j);
+        }
+        W[i] = w;
+    }
+    #pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)ns; ++i) {
+        S[i] = qgo_f32_to_f16(qgo_uniform_from_hash(qgo_hash64(seed, tid0 + 2, (uint64_t)i), 0.005f, 0.02f));
+        Z[i] = qgo_f32_to_f16(qgo_uniform_from_hash(qgo_hash64(seed, tid0 + 3, (uint64_t)i), -0.5f, 0.5f));
+    }
+}
+
 /* ------------------------------------------------------------------------
  * Verification helpers (word compare as ai_verify_output,
  * kernels/common/ai_workload_template.h:343-349).

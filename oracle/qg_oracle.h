@@ -97,6 +97,8 @@ void  qgo_gemm_nvfp4(const uint8_t* A, const uint8_t* SFA, float GA,
  * X bf16 [M,K]; W packed uint32 [K/8, N] (nibble j of word (k/8, n) is
  * code u(k=8*(k/8)+j, n), value q = u - 8); S, Z fp16 [K/128, N];
  * Y[m,n] = sum_k X[m,k] * (q[k,n] - Z[k/128,n]) * S[k/128,n]. */
+void qgo_gen_w4a16(uint16_t* X, uint32_t* W, uint16_t* S, uint16_t* Z, int M, int N, int K,
+                   uint64_t seed, uint32_t tid0);
 void qgo_gemv_w4a16(const uint16_t* X, const uint32_t* W, const uint16_t* S, const uint16_t* Z,
                     int M, int N, int K, const int32_t* cols, int ncols,
                     int out_type, void* Y);

@@ -63,6 +63,7 @@ def lib() -> C.CDLL:
             "qgo_gemm_nvfp4": (None, [_P, _P, C.c_float, _P, _P, C.c_float, C.c_int, C.c_int, C.c_int, _P,
                                       C.c_int, C.c_int, _P]),
             "qgo_gemv_w4a16": (None, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, _P]),
+            "qgo_gen_w4a16": (None, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint32]),
             "qgo_count_mismatch_u32": (C.c_uint64, [_P, _P, C.c_uint64]),
             "qgo_max_rel_err": (C.c_double, [_P, _P, C.c_uint64, C.c_int]),
             "qgo_threads": (C.c_int, []),
@@ -133,6 +134,45 @@ def gemm_i8(A, B, sa, sb, out_type: int = 0, rows=None, want_acc: bool = False, 
     if want_cksum:
         res.append(ck)
     return res[0] if len(res) == 1 else tuple(res)
+
+
+def w4a16_operands(M: int, N: int, K: int, seed: int, copy: int = 0):
+    """The W4A16 workload's operands of copy `copy` (tensor ids 8*copy + 0..3):
+    X bf16 bits [M,K], W uint32 [K/8,N], S and Z fp16 bits [K/128,N]."""
+    X = np.empty((M, K), dtype=np.uint16)
+    W = np.empty((K // 8, N), dtype=np.uint32)
+    S = np.empty((K // 128, N), dtype=np.uint16)
+    Z = np.empty((K // 128, N), dtype=np.uint16)
+    lib().qgo_gen_w4a16(_p(X), _p(W), _p(S), _p(Z), M, N, K, seed, 8 * copy)
+    return X, W, S, Z
+
+
+def gemv_w4a16(X, W, S, Z, out_type: int = 0, cols=None):
+    """Oracle W4A16 GEMV; returns [M, ncols] (bf16 bits for out_type 0, f32 for 1)."""
+    X = np.ascontiguousarray(X, dtype=np.uint16)
+    W = np.ascontiguousarray(W, dtype=np.uint32)
+    S = np.ascontiguousarray(S, dtype=np.uint16)
+    Z = np.ascontiguousarray(Z, dtype=np.uint16)
+    M, K = X.shape
+    N = W.shape[1]
+    c = None if cols is None else np.ascontiguousarray(cols, dtype=np.int32)
+    nc = N if c is None else len(c)
+    Y = np.empty((M, nc), dtype=np.uint16 if out_type == 0 else np.float32)
+    lib().qgo_gemv_w4a16(_p(X), _p(W), _p(S), _p(Z), M, N, K, _p(c), nc, out_type, _p(Y))
+    return Y
+
+
+def gemv_w4a16_numpy(X, W, S, Z) -> np.ndarray:
+    """Independent float64 numpy evaluation of the W4A16 GEMV (for pinning the oracle)."""
+    x = bf16_bits_to_f32(X).astype(np.float64)
+    K = x.shape[1]
+    N = W.shape[1]
+    shifts = (4 * np.arange(8, dtype=np.uint32))[None, :, None]
+    u = ((W[:, None, :] >> shifts) & np.uint32(0xF)).reshape(K, N).astype(np.float64)
+    s = np.repeat(S.view(np.float16).astype(np.float64), 128, axis=0)
+    z = np.repeat(Z.view(np.float16).astype(np.float64), 128, axis=0)
+    w = (u - 8.0 - z) * s
+    return x @ w
 
 
 # ---------------------------------------------------------------- conversions

@@ -28,7 +28,10 @@ from .ops import (  # noqa: F401
     Workload,
     device_status,
     gemm_i8,
+    gemv_w4a16,
+    gemv_w4a16_workspace_bytes,
     gen_i8,
+    gen_w4a16,
     gen_normal_f32,
     gen_uniform_f32,
     verify_words,
@@ -36,7 +39,7 @@ from .ops import (  # noqa: F401
 
 __all__ = [
     "LIB_PATH", "BIN_PATH", "QGError", "load_library", "Workload", "device_status",
-    "gemm_i8", "gen_i8", "gen_uniform_f32", "gen_normal_f32", "verify_words",
+    "gemm_i8", "gemv_w4a16", "gemv_w4a16_workspace_bytes", "gen_w4a16", "gen_i8", "gen_uniform_f32", "gen_normal_f32", "verify_words",
     "QG_FMT_INT8", "QG_FMT_FP8", "QG_FMT_NVFP4", "QG_FMT_W4A16",
     "QG_OUT_BF16", "QG_OUT_F32", "QG_OUT_S32",
 ]

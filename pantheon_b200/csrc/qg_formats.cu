@@ -33,6 +33,24 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
             l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes + l.cksum_bytes);
             break;
         }
+        case QG_FMT_W4A16: {
+            l.M = cfg.m > 0 ? cfg.m : 1;
+            l.N = cfg.n > 0 ? cfg.n : 28672;
+            l.K = cfg.k > 0 ? cfg.k : 8192;
+            QG_CHECK_ARG(l.K % 128 == 0, "W4A16: K=%d must be a multiple of 128", l.K);
+            QG_CHECK_ARG(l.N % 4 == 0, "W4A16: N=%d must be a multiple of 4", l.N);
+            QG_CHECK_ARG(l.out_type == QG_OUT_BF16 || l.out_type == QG_OUT_F32, "W4A16: bad out_type %d", l.out_type);
+            l.n_ops = 4;
+            l.op_bytes[0] = 2ull * l.M * l.K;                  // X bf16
+            l.op_bytes[1] = (uint64_t)l.K / 8 * l.N * 4;       // W packed int4
+            l.op_bytes[2] = (uint64_t)l.K / 128 * l.N * 2;     // S fp16
+            l.op_bytes[3] = (uint64_t)l.K / 128 * l.N * 2;     // Z fp16
+            l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
+            l.scratch_bytes = gemv_w4a16_workspace_bytes(l.M, l.N, l.K, 148);
+            l.ops = 2.0 * l.M * (double)l.N * l.K;
+            l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes);
+            break;
+        }
         default:
             set_error("format %d is not available in this build", cfg.format);
             return QG_ERR_ARG;
@@ -52,6 +70,9 @@ int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_inde
             if ((rc = gen_uniform(cp.op[2], (uint64_t)L.M, 0.001f, 0.01f, seed, base + 2, s))) return rc;
             if ((rc = gen_uniform(cp.op[3], (uint64_t)L.N, 0.001f, 0.01f, seed, base + 3, s))) return rc;
             return QG_OK;
+        case QG_FMT_W4A16:
+            if (cp.scratch) QG_CUDA(cudaMemsetAsync(cp.scratch, 0, L.scratch_bytes, s));
+            return gen_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], L.M, L.N, L.K, seed, base, s);
         default:
             set_error("format %d is not available in this build", cfg.format);
             return QG_ERR_ARG;
@@ -62,6 +83,9 @@ int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaS
     switch (cfg.format) {
         case QG_FMT_INT8:
             return gemm_i8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, cp.cksum, L.M, L.N, L.K, s);
+        case QG_FMT_W4A16:
+            return gemv_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, cp.scratch,
+                              L.scratch_bytes, s);
         default:
             set_error("format %d is not available in this build", cfg.format);
             return QG_ERR_ARG;

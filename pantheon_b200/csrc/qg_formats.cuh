@@ -44,6 +44,10 @@ int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* 
 int gen_i8(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, cudaStream_t s);
 int gen_uniform(void* out, uint64_t n, float lo, float hi, uint64_t seed, uint32_t tensor_id, cudaStream_t s);
 int gen_normal(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, cudaStream_t s);
+int gen_w4a16(void* X, void* W, void* S, void* Z, int M, int N, int K, uint64_t seed, uint32_t tid0, cudaStream_t s);
+uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int sm_count);
+int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,
+               void* workspace, uint64_t workspace_bytes, cudaStream_t stream);
 int verify_words(const void* actual, const void* expected, uint64_t nwords, void* counters, void* log, int log_cap,
                  cudaStream_t s);
 int flip_bit(void* word, cudaStream_t s);

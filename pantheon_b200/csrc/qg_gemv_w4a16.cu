@@ -230,11 +230,15 @@ gemv_w4a16_kernel(Params p) {
 // Rows per launch template and K split for a given M.
 static int m_template(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16; }
 
-static int choose_splits(int MT, int N, int K, int sm_count) {
+// The split depends only on the shape (sized for the 148 SMs of a B200), so the
+// workspace size is a function of (M, N, K) alone.
+constexpr int kSplitSms = 148;
+
+static int choose_splits(int MT, int N, int K) {
     const int col_blocks = (N + COLS_PER_CTA - 1) / COLS_PER_CTA;
     const int groups = K / GROUP;
     // enough CTAs for several per SM; fewer, longer splits when M makes the CTA compute-heavy
-    const int target_ctas = (MT <= 2 ? 12 : MT <= 4 ? 8 : 4) * sm_count;
+    const int target_ctas = (MT <= 2 ? 12 : MT <= 4 ? 8 : 4) * kSplitSms;
     int splits = (target_ctas + col_blocks - 1) / col_blocks;
     if (splits > groups) splits = groups;
     if (splits < 1) splits = 1;
@@ -249,7 +253,7 @@ uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int sm_count) {
     uint64_t total = 0;
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mt = w4::m_template(M - m0 < w4::MAX_M ? M - m0 : w4::MAX_M);
-        const int splits = w4::choose_splits(mt, N, K, sm_count);
+        const int splits = w4::choose_splits(mt, N, K);
         const uint64_t ws = (uint64_t)splits * mt * N * 4;
         if (ws > total) total = ws;
     }
@@ -280,7 +284,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mrows = (M - m0) < w4::MAX_M ? (M - m0) : w4::MAX_M;
         const int mt = w4::m_template(mrows);
-        const int splits = w4::choose_splits(mt, N, K, info->sm_count);
+        const int splits = w4::choose_splits(mt, N, K);
         w4::Params p;
         p.X = static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K;
         p.W = static_cast<const uint4*>(W);

@@ -65,6 +65,45 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, sa: torch.Tensor | None, sb: torch
     return (out, ck) if row_checksums else out
 
 
+def gemv_w4a16_workspace_bytes(M: int, N: int, K: int) -> int:
+    b = C.c_uint64()
+    check("qg_gemv_w4a16_workspace_bytes", load_library().qg_gemv_w4a16_workspace_bytes(M, N, K, C.byref(b)))
+    return b.value
+
+
+def gemv_w4a16(X: torch.Tensor, W: torch.Tensor, S: torch.Tensor, Z: torch.Tensor, out_type: int = QG_OUT_BF16,
+               workspace: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Y = X @ dequant(W) on the CUDA-core W4A16 path.
+
+    X bf16 [M,K]; W int32/uint32 [K/8,N] packed int4 (nibble j = k offset j);
+    S, Z fp16 [K/128,N]; returns Y [M,N] (bf16 or fp32).  `workspace` (uint8,
+    zero-filled, qg_gemv_w4a16_workspace_bytes) is allocated when not given.
+    """
+    _require_cuda(X, W, S, Z)
+    M, K = X.shape
+    N = W.shape[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=_OUT_DTYPES[out_type], device=X.device)
+    need = gemv_w4a16_workspace_bytes(M, N, K)
+    if workspace is None:
+        workspace = torch.zeros((need,), dtype=torch.uint8, device=X.device)
+    check("qg_gemv_w4a16", load_library().qg_gemv_w4a16(_ptr(X), _ptr(W), _ptr(S), _ptr(Z), _ptr(out), out_type,
+                                                         M, N, K, _ptr(workspace), workspace.numel(),
+                                                         _stream(X.device)))
+    return out
+
+
+def gen_w4a16(M: int, N: int, K: int, seed: int, tid0: int = 0, device="cuda"):
+    """The W4A16 workload's generated operands (X bf16, W int32, S fp16, Z fp16) on the device."""
+    X = torch.empty((M, K), dtype=torch.bfloat16, device=device)
+    W = torch.empty((K // 8, N), dtype=torch.int32, device=device)
+    S = torch.empty((K // 128, N), dtype=torch.float16, device=device)
+    Z = torch.empty((K // 128, N), dtype=torch.float16, device=device)
+    check("qg_gen_w4a16", load_library().qg_gen_w4a16(_ptr(X), _ptr(W), _ptr(S), _ptr(Z), M, N, K, seed, tid0,
+                                                       _stream(X.device)))
+    return X, W, S, Z
+
+
 def gen_i8(n: int, seed: int, tensor_id: int, device="cuda") -> torch.Tensor:
     """Counter-based uniform int8 in [-127, 127] (same bits as the CPU oracle)."""
     out = torch.empty(((n + 15) // 16) * 16, dtype=torch.int8, device=device)

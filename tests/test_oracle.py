@@ -163,3 +163,27 @@ def test_count_mismatch_and_rel_err(oracle):
     r = np.linspace(-1, 1, 101).astype(np.float32)
     y = r * np.float32(1.001)
     assert oracle.max_rel_err(y, r, 1) < 2e-3
+
+
+@pytest.mark.parametrize("shape", [(1, 8, 128), (3, 36, 256), (16, 64, 512)])
+def test_gemv_w4a16_oracle_matches_numpy(oracle, shape):
+    """The oracle's W4A16 GEMV against an independent float64 numpy evaluation."""
+    M, N, K = shape
+    X, W, S, Z = oracle.w4a16_operands(M, N, K, seed=M + N)
+    ref = oracle.gemv_w4a16_numpy(X, W, S, Z).astype(np.float32)
+    y = oracle.gemv_w4a16(X, W, S, Z, out_type=1)
+    np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-5 * float(np.abs(ref).max()))
+    cols = np.array([0, N - 1, N // 2], dtype=np.int32)
+    np.testing.assert_array_equal(oracle.gemv_w4a16(X, W, S, Z, out_type=1, cols=cols), y[:, cols])
+
+
+def test_w4a16_generator_distributions(oracle):
+    X, W, S, Z = oracle.w4a16_operands(4, 1024, 1024, seed=3)
+    x = oracle.bf16_bits_to_f32(X)
+    assert abs(float(x.mean())) < 0.05 and abs(float(x.std()) - 1.0) < 0.05
+    u = ((W[:, None, :] >> (4 * np.arange(8, dtype=np.uint32))[None, :, None]) & 0xF).ravel()
+    assert u.min() == 0 and u.max() == 15 and abs(u.mean() - 7.5) < 0.05
+    s = S.view(np.float16).astype(np.float32)
+    z = Z.view(np.float16).astype(np.float32)
+    # bounds after rounding to fp16
+    assert s.min() >= np.float16(0.005) and s.max() <= np.float16(0.02) and z.min() >= -0.5 and z.max() <= 0.5
