@@ -189,6 +189,22 @@ QG_API int  qg_gemv_w4a16(const void* X, const void* W, const void* S, const voi
                           int out_type, int M, int N, int K,
                           void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* qg_gemv_w4a16 without a caller-provided workspace, for callers that cannot
+ * allocate device memory where they call it (a process whose device-memory
+ * budget is already claimed, or a latency-critical decode path where an
+ * allocation is not acceptable).  No counterpart in the reference.
+ * Scratch comes from a 16 MiB array compiled into the library, which every GPU
+ * that loads the library holds until the process exits; shapes whose
+ * workspace (qg_gemv_w4a16_workspace_bytes) exceeds 16 MiB are rejected with
+ * QG_ERR_ARG (configs[3], M <= 16, K = 8192, N = 28672, fits).  The call
+ * allocates nothing; it clears the part of the array it uses on `stream`
+ * before the kernel runs.  All calls share the one array per device, so calls
+ * that overlap on the GPU (other streams, other threads) race: serialise them.
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture. */
+QG_API int  qg_gemv_w4a16_noalloc(const void* X, const void* W, const void* S, const void* Z, void* Y,
+                                  int out_type, int M, int N, int K, void* stream);
+
 /* Bounded-wait status of the most recent kernel on this device (QG_OK or
  * QG_ERR_DEVICE_TIMEOUT); clears the flag. Synchronous. */
 QG_API int  qg_device_status(int device);

@@ -27,6 +27,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 namespace qg {
 namespace w4 {
 
@@ -337,4 +339,72 @@ extern "C" int qg_gemv_w4a16(const void* X, const void* W, const void* S, const 
                              int N, int K, void* workspace, uint64_t workspace_bytes, void* stream) {
     return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, workspace, workspace_bytes,
                           static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the W4A16 GEMV.
+//
+// qg_gemv_w4a16 needs a caller-provided device workspace for its split-K
+// partial sums and tickets.  Some callers cannot allocate one at the point of
+// the call: a process that has already claimed its device-memory budget up
+// front (the stress harness sizes its working set to --mem percent of free
+// memory, and a host framework's caching allocator may hold the rest, so a
+// fresh cudaMalloc can fail), or a caller on a latency-critical decode path
+// where an allocation, which can synchronize the device, is not acceptable.
+// qg_gemv_w4a16_noalloc serves them from a fixed scratch array compiled into
+// this library instead, and calls no allocating routine.
+//
+// The array lives in every GPU that loads the library, for the life of the
+// process: kNoAllocScratchBytes of device memory per GPU.
+constexpr uint64_t kNoAllocScratchBytes = 16ull << 20;   // 16 MiB
+
+static __device__ __align__(256) uint8_t g_gemv_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace qg {
+namespace w4 {
+
+constexpr int kNoAllocMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[kNoAllocMaxDevices];
+
+// Device address of this device's scratch array.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per
+// device, with that device current, and cached.
+static int noalloc_scratch(void** out) {
+    int dev = 0;
+    QG_CUDA(cudaGetDevice(&dev));
+    QG_CHECK_ARG(dev >= 0 && dev < kNoAllocMaxDevices, "qg_gemv_w4a16_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            set_error("qg_gemv_w4a16_noalloc: cudaGetSymbolAddress failed: %s (%d)", cudaGetErrorString(e), (int)e);
+            return QG_ERR_CUDA;
+        }
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return QG_OK;
+}
+
+} // namespace w4
+} // namespace qg
+
+extern "C" int qg_gemv_w4a16_noalloc(const void* X, const void* W, const void* S, const void* Z, void* Y,
+                                     int out_type, int M, int N, int K, void* stream) {
+    QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemv_w4a16_noalloc: empty shape %dx%dx%d", M, N, K);
+    const uint64_t need = qg::gemv_w4a16_workspace_bytes(M, N, K, 0);
+    QG_CHECK_ARG(need <= kNoAllocScratchBytes,
+                 "qg_gemv_w4a16_noalloc: shape %dx%dx%d needs %llu bytes of scratch, above the built-in maximum of "
+                 "%llu bytes; use qg_gemv_w4a16 with a caller-provided workspace",
+                 M, N, K, (unsigned long long)need, (unsigned long long)kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    int rc = qg::w4::noalloc_scratch(&scratch);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The array keeps whatever the previous call (of any shape) left in it,
+    // and the tickets must start at zero: clear this call's part first.
+    QG_CUDA(cudaMemsetAsync(scratch, 0, (size_t)need, s));
+    return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, scratch, kNoAllocScratchBytes, s);
 }
