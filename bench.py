@@ -80,6 +80,13 @@ def workload_spec(args, pb):
                 "config": {"workload": f"configs[3] W4A16 group-128 GEMV M={m} K=8192 N=28672, bf16 out",
                            "M": m, "N": 28672, "K": 8192, "seed": 3, "operand_sets": 4,
                            "l2": "inputs larger than L2: 4 rotating weight sets of 125 MB each"}}
+    if args.workload == "fp8":
+        return {"name": "fp8", "fmt": pb.QG_FMT_FP8, "shape": (8192, 8192, 16384), "copies": 1, "seed": 2,
+                "unit": "TOPS", "bound": "tensor", "dtype": "e4m3 (fp32 acc, fp32 block scales)", "launches_per_step": 1,
+                "traffic_key": "gemm_fp8_8192_16384",
+                "config": {"workload": "configs[2] FP8 e4m3 GEMM M=N=8192 K=16384, 1x128 / 128x128 fp32 scales, bf16 out",
+                           "M": 8192, "N": 8192, "K": 16384, "seed": 2, "operand_sets": 1,
+                           "l2": "inputs larger than L2: A + B = 256 MiB"}}
     return {"name": "int8", "fmt": pb.QG_FMT_INT8, "shape": (M, N, K), "copies": 2, "seed": 1, "unit": "TOPS",
             "bound": "tensor", "dtype": "int8", "launches_per_step": 1, "traffic_key": "gemm_i8_8192",
             "config": {"workload": "configs[1] INT8 W8A8 GEMM 8192x8192x8192, bf16 out, fp32 row/col scales",
@@ -337,7 +344,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["int8", "w4a16"], default="int8",
+    ap.add_argument("--workload", choices=["int8", "fp8", "w4a16"], default="int8",
                     help="int8 = configs[1] (default, the headline); w4a16 = configs[3] GEMV")
     ap.add_argument("--m", type=int, default=0, help="rows of the W4A16 activations (1, 8 or 16)")
     args = ap.parse_args(argv)

@@ -173,6 +173,19 @@ QG_API int  qg_gemm_i8(const void* A, const void* B, const void* sa, const void*
                 void* C, int out_type, void* row_checksums,
                 int M, int N, int K, void* stream);
 
+/* FP8 e4m3 with fp32 block scales:
+ *   C[m,n] = out( sum_kb P_kb[m,n] * sa[m,kb] * sb[n/128,kb] ),
+ *   P_kb = sum over the 128-deep K block kb of A[m,k] B[n,k] (tensor cores, fp32),
+ *   promoted in fp32 in K-block order as acc = fma(P_kb, sa*sb, acc).
+ *   A e4m3 [M,K], B e4m3 [N,K] (K contiguous, K % 128 == 0); sa fp32 [M, K/128]
+ *   (1x128 blocks), sb fp32 [ceil(N/128), K/128] (128x128 blocks);
+ *   out_type QG_OUT_BF16 or QG_OUT_F32.
+ * Replaces: the per-kind body of ai_workload_kernel (ai_workload_template.h:157-177);
+ *   the reference's only FP8 GEMM is cuBLASLt e4m3 without block scales
+ *   (kernels/common/vendor_gemm.h:311-327). */
+QG_API int  qg_gemm_fp8_b128(const void* A, const void* B, const void* sa, const void* sb,
+                             void* C, int out_type, int M, int N, int K, void* stream);
+
 /* W4A16 group-128 decode GEMV / skinny GEMM on the CUDA cores:
  *   Y[m,n] = sum_k X[m,k] * (q[k,n] - Z[k/128,n]) * S[k/128,n],  q = u - 8
  *   X bf16 [M,K]; W uint32 [K/8, N] with nibble j of word (k8, n) = u(8*k8+j, n)
@@ -226,6 +239,11 @@ QG_API int  qg_gen_uniform_f32(void* out, uint64_t n, float lo, float hi,
                         uint64_t seed, uint32_t tensor_id, void* stream);
 /* out[i] = standard normal deviate (seed, tensor_id, i), fp32. */
 QG_API int  qg_gen_normal_f32(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream);
+/* FP8 operands of configs[2]: values N(0,1) (A: tensor tid0, B: tid0+2), each
+ * block (A 1x128, B 128x128) scaled so its absmax maps to 448:
+ * q = e4m3_rn_satfinite(x * (448/absmax)), scale = absmax/448 (fp32). */
+QG_API int  qg_gen_fp8(void* A, void* sa, void* B, void* sb, int M, int N, int K,
+                       uint64_t seed, uint32_t tid0, void* stream);
 /* W4A16 operands of configs[3]: X bf16 [M,K] = bf16(N(0,1)); W packed as in
  * qg_gemv_w4a16 with u uniform in [0,15] (q uniform in [-8,7]);
  * S fp16 = f16(U[0.005, 0.02]), Z fp16 = f16(U[-0.5, 0.5]) per (group, n).

@@ -303,15 +303,19 @@ void qgo_quant_fp8_rows(const float* X, int R, int K, uint8_t* Q, float* S) {
 }
 
 void qgo_quant_fp8_blocks(const float* X, int R, int K, uint8_t* Q, float* S) {
-    int kb = K / 128, rb = R / 128;
+    int kb = K / 128, rb = (R + 127) / 128;   /* a last partial block of rows is its own block */
     #pragma omp parallel for collapse(2) schedule(static)
     for (int i = 0; i < rb; ++i)
-        for (int b = 0; b < kb; ++b) quant_fp8_block(X, K, i * 128, i * 128 + 128, b * 128, Q, &S[(size_t)i * kb + b]);
+        for (int b = 0; b < kb; ++b) {
+            int r1 = i * 128 + 128 < R ? i * 128 + 128 : R;
+            quant_fp8_block(X, K, i * 128, r1, b * 128, Q, &S[(size_t)i * kb + b]);
+        }
 }
 
 /* Per 128-wide K block: exact partial sum (products of e4m3 values are exact in
  * fp32 and 128 of them sum exactly in double), rounded once to fp32, then
- * acc = acc + partial * (sa[m,kb] * sb[n/128,kb]) in fp32, K blocks in order. */
+ * acc = fma(partial, sa[m,kb] * sb[n/128,kb], acc) in fp32, K blocks in order
+ * (the promotion the GPU epilogue performs per K block). */
 void qgo_gemm_fp8_b128(const uint8_t* A, const uint8_t* B, const float* sa, const float* sb,
                        int M, int N, int K, const int32_t* rows, int nrows,
                        int out_type, void* C) {
@@ -331,8 +335,7 @@ void qgo_gemm_fp8_b128(const uint8_t* A, const uint8_t* B, const float* sa, cons
                 for (int k = j * 128; k < j * 128 + 128; ++k) p += (double)(lut[a[k]] * lut[b[k]]);
                 float pf = (float)p;
                 float sc = sa[(size_t)m * kb + j] * sb[(size_t)(n / 128) * kb + j];
-                float t = pf * sc;
-                acc = acc + t;
+                acc = fmaf(pf, sc, acc);
             }
             size_t o = (size_t)r * N + n;
             if (out_type == 1) ((float*)C)[o] = acc;

@@ -136,6 +136,41 @@ def gemm_i8(A, B, sa, sb, out_type: int = 0, rows=None, want_acc: bool = False, 
     return res[0] if len(res) == 1 else tuple(res)
 
 
+def fp8_operands(M: int, N: int, K: int, seed: int, copy: int = 0):
+    """The FP8 block-128 workload's operands of copy `copy`: A e4m3 [M,K] with sa [M,K/128]
+    (values: tensor id 8*copy+0), B e4m3 [N,K] with sb [ceil(N/128),K/128] (tensor id 8*copy+2)."""
+    b = 8 * copy
+    xa = gen_normal_f32(M * K, seed, b + 0)
+    xb = gen_normal_f32(N * K, seed, b + 2)
+    A = np.empty((M, K), dtype=np.uint8)
+    B = np.empty((N, K), dtype=np.uint8)
+    sa = np.empty((M, K // 128), dtype=np.float32)
+    sb = np.empty(((N + 127) // 128, K // 128), dtype=np.float32)
+    lib().qgo_quant_fp8_rows(_p(xa), M, K, _p(A), _p(sa))
+    lib().qgo_quant_fp8_blocks(_p(xb), N, K, _p(B), _p(sb))
+    return A, B, sa, sb
+
+
+def gemm_fp8(A, B, sa, sb, out_type: int = 0, rows=None):
+    """Oracle FP8 block-128 GEMM (bf16 bits for out_type 0, f32 for 1)."""
+    A = np.ascontiguousarray(A, dtype=np.uint8)
+    B = np.ascontiguousarray(B, dtype=np.uint8)
+    sa = np.ascontiguousarray(sa, dtype=np.float32)
+    sb = np.ascontiguousarray(sb, dtype=np.float32)
+    M, K = A.shape
+    N = B.shape[0]
+    r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int32)
+    nr = M if r is None else len(r)
+    C_ = np.empty((nr, N), dtype=np.uint16 if out_type == 0 else np.float32)
+    lib().qgo_gemm_fp8_b128(_p(A), _p(B), _p(sa), _p(sb), M, N, K, _p(r), nr, out_type, _p(C_))
+    return C_
+
+
+def e4m3_to_f32(q: np.ndarray) -> np.ndarray:
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(q, dtype=np.uint8)).view(torch.float8_e4m3fn).float().numpy()
+
+
 def w4a16_operands(M: int, N: int, K: int, seed: int, copy: int = 0):
     """The W4A16 workload's operands of copy `copy` (tensor ids 8*copy + 0..3):
     X bf16 bits [M,K], W uint32 [K/8,N], S and Z fp16 bits [K/128,N]."""

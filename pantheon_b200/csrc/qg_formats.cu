@@ -33,6 +33,22 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
             l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes + l.cksum_bytes);
             break;
         }
+        case QG_FMT_FP8: {
+            l.M = cfg.m > 0 ? cfg.m : 8192;
+            l.N = cfg.n > 0 ? cfg.n : 8192;
+            l.K = cfg.k > 0 ? cfg.k : 16384;
+            QG_CHECK_ARG(l.K % 128 == 0, "FP8: K=%d must be a multiple of 128", l.K);
+            QG_CHECK_ARG(l.out_type == QG_OUT_BF16 || l.out_type == QG_OUT_F32, "FP8: bad out_type %d", l.out_type);
+            l.n_ops = 4;                                                   // A, B, sa, sb
+            l.op_bytes[0] = (uint64_t)l.M * l.K;
+            l.op_bytes[1] = (uint64_t)l.N * l.K;
+            l.op_bytes[2] = 4ull * l.M * (l.K / 128);
+            l.op_bytes[3] = 4ull * ((l.N + 127) / 128) * (l.K / 128);
+            l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
+            l.ops = 2.0 * l.M * (double)l.N * l.K;
+            l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes);
+            break;
+        }
         case QG_FMT_W4A16: {
             l.M = cfg.m > 0 ? cfg.m : 1;
             l.N = cfg.n > 0 ? cfg.n : 28672;
@@ -70,6 +86,8 @@ int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_inde
             if ((rc = gen_uniform(cp.op[2], (uint64_t)L.M, 0.001f, 0.01f, seed, base + 2, s))) return rc;
             if ((rc = gen_uniform(cp.op[3], (uint64_t)L.N, 0.001f, 0.01f, seed, base + 3, s))) return rc;
             return QG_OK;
+        case QG_FMT_FP8:
+            return gen_fp8(cp.op[0], cp.op[2], cp.op[1], cp.op[3], L.M, L.N, L.K, seed, base, s);
         case QG_FMT_W4A16:
             if (cp.scratch) QG_CUDA(cudaMemsetAsync(cp.scratch, 0, L.scratch_bytes, s));
             return gen_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], L.M, L.N, L.K, seed, base, s);
@@ -83,6 +101,8 @@ int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaS
     switch (cfg.format) {
         case QG_FMT_INT8:
             return gemm_i8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, cp.cksum, L.M, L.N, L.K, s);
+        case QG_FMT_FP8:
+            return gemm_fp8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, s);
         case QG_FMT_W4A16:
             return gemv_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, cp.scratch,
                               L.scratch_bytes, s);

@@ -6,6 +6,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 namespace qg {
 namespace gen {
@@ -73,6 +74,79 @@ __global__ void gen_w4_kernel(uint32_t* out, uint64_t words, uint32_t N, uint64_
     }
 }
 
+// FP8 e4m3 operands: values N(0,1), each block scaled so that its
+// absmax maps to 448: q = e4m3_rn_satfinite(x * (448 / amax)), scale = amax / 448.
+__device__ __forceinline__ uint8_t to_e4m3(float v) {
+    return (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+}
+
+// A: 1 x 128 blocks along K, one warp per block (lane l holds k = 4l .. 4l+3).
+__global__ void gen_fp8_rows_kernel(uint8_t* Q, float* S, int R, int K, uint64_t key) {
+    const int kb_count = K / 128;
+    const uint64_t blocks = (uint64_t)R * kb_count;
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+    for (uint64_t b = (uint64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); b < blocks; b += warps) {
+        const uint64_t r = b / kb_count, kb = b - r * kb_count;
+        const uint64_t base = r * (uint64_t)K + kb * 128 + (uint64_t)lane * 4;
+        float x[4];
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            x[i] = normal_from_hash(hash_at(key, base + i));
+            amax = fmaxf(amax, fabsf(x[i]));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float inv = amax > 0.0f ? __fdiv_rn(448.0f, amax) : 1.0f;
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w |= (uint32_t)to_e4m3(__fmul_rn(x[i], inv)) << (8 * i);
+        *reinterpret_cast<uint32_t*>(Q + base) = w;
+        if (lane == 0) S[b] = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+    }
+}
+
+// B: 128 x 128 blocks, one 256-thread CTA per block (thread t: row t/2, 64 k).
+__global__ void gen_fp8_blocks_kernel(uint8_t* Q, float* S, int R, int K, uint64_t key) {
+    const int kb_count = K / 128;
+    const int rb = blockIdx.x / kb_count, kb = blockIdx.x - rb * kb_count;
+    const int r = rb * 128 + (threadIdx.x >> 1);
+    const uint64_t base = (uint64_t)r * K + (uint64_t)kb * 128 + (threadIdx.x & 1) * 64;
+    const bool live = r < R;
+    float x[64];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+        x[i] = live ? normal_from_hash(hash_at(key, base + i)) : 0.0f;
+        amax = fmaxf(amax, fabsf(x[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    __shared__ float warp_max[8];
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, warp_max[i]);
+    const float inv = amax > 0.0f ? __fdiv_rn(448.0f, amax) : 1.0f;
+    if (live) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) word |= (uint32_t)to_e4m3(__fmul_rn(x[v * 16 + j * 4 + b], inv)) << (8 * b);
+                w[j] = word;
+            }
+            *reinterpret_cast<uint4*>(Q + base + v * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    if (threadIdx.x == 0) S[blockIdx.x] = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+}
+
 static int grid_for(uint64_t work) {
     DeviceInfo* info = nullptr;
     int blocks = 148 * 8;
@@ -125,7 +199,25 @@ int gen_w4a16(void* X, void* W, void* S, void* Z, int M, int N, int K, uint64_t 
     return QG_OK;
 }
 
+int gen_fp8(void* A, void* SA, void* B, void* SB, int M, int N, int K, uint64_t seed, uint32_t tid0, cudaStream_t s) {
+    QG_CHECK_ARG(A && SA && B && SB, "qg_gen_fp8: null output");
+    QG_CHECK_ARG(M > 0 && N > 0 && K > 0 && K % 128 == 0, "qg_gen_fp8: bad shape %dx%dx%d (K %% 128 == 0)", M, N, K);
+    const uint64_t warps_needed = (uint64_t)M * (K / 128);
+    gen::gen_fp8_rows_kernel<<<gen::grid_for(warps_needed * 32), 256, 0, s>>>(
+        static_cast<uint8_t*>(A), static_cast<float*>(SA), M, K, gen::stream_key(seed, tid0));
+    const int bblocks = ((N + 127) / 128) * (K / 128);
+    gen::gen_fp8_blocks_kernel<<<bblocks, 256, 0, s>>>(static_cast<uint8_t*>(B), static_cast<float*>(SB), N, K,
+                                                       gen::stream_key(seed, tid0 + 2));
+    QG_CUDA(cudaGetLastError());
+    return QG_OK;
+}
+
 } // namespace qg
+
+extern "C" int qg_gen_fp8(void* A, void* SA, void* B, void* SB, int M, int N, int K, uint64_t seed, uint32_t tid0,
+                          void* stream) {
+    return qg::gen_fp8(A, SA, B, SB, M, N, K, seed, tid0, static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int qg_gen_w4a16(void* X, void* W, void* S, void* Z, int M, int N, int K, uint64_t seed, uint32_t tid0,
                             void* stream) {

@@ -65,6 +65,34 @@ def gemm_i8(A: torch.Tensor, B: torch.Tensor, sa: torch.Tensor | None, sb: torch
     return (out, ck) if row_checksums else out
 
 
+def gemm_fp8_b128(A: torch.Tensor, B: torch.Tensor, sa: torch.Tensor, sb: torch.Tensor,
+                  out_type: int = QG_OUT_BF16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = sum_kb (A_kb @ B_kb^T) * sa[:, kb] * sb[n/128, kb] on the tcgen05 FP8 path.
+
+    A, B e4m3 bytes (uint8 or float8_e4m3fn) [M,K] / [N,K]; sa fp32 [M,K/128];
+    sb fp32 [ceil(N/128),K/128].  Asynchronous on the current stream.
+    """
+    _require_cuda(A, B, sa, sb)
+    M, K = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=_OUT_DTYPES[out_type], device=A.device)
+    check("qg_gemm_fp8_b128", load_library().qg_gemm_fp8_b128(_ptr(A), _ptr(B), _ptr(sa), _ptr(sb), _ptr(out),
+                                                               out_type, M, N, K, _stream(A.device)))
+    return out
+
+
+def gen_fp8(M: int, N: int, K: int, seed: int, tid0: int = 0, device="cuda"):
+    """The FP8 workload's generated operands (A, B as uint8 e4m3 bytes; sa, sb fp32)."""
+    A = torch.empty((M, K), dtype=torch.uint8, device=device)
+    B = torch.empty((N, K), dtype=torch.uint8, device=device)
+    sa = torch.empty((M, K // 128), dtype=torch.float32, device=device)
+    sb = torch.empty(((N + 127) // 128, K // 128), dtype=torch.float32, device=device)
+    check("qg_gen_fp8", load_library().qg_gen_fp8(_ptr(A), _ptr(sa), _ptr(B), _ptr(sb), M, N, K, seed, tid0,
+                                                   _stream(A.device)))
+    return A, B, sa, sb
+
+
 def gemv_w4a16_workspace_bytes(M: int, N: int, K: int) -> int:
     b = C.c_uint64()
     check("qg_gemv_w4a16_workspace_bytes", load_library().qg_gemv_w4a16_workspace_bytes(M, N, K, C.byref(b)))
