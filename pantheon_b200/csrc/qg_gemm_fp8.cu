@@ -78,16 +78,6 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
     nt = r / gm;
 }
 
-__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-}
-
 template <int OUT>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
@@ -107,7 +97,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&bars->full[s], 1); mbar_init(&bars->empty[s], 1); }
-        for (int a = 0; a < 2; ++a) { mbar_init(&bars->part_full[a], 1); mbar_init(&bars->part_empty[a], EPI_THREADS); }
+        for (int a = 0; a < 2; ++a) { mbar_init(&bars->part_full[a], 1); mbar_init(&bars->part_empty[a], EPI_THREADS / 32); }
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
         fence_barrier_init();
@@ -195,26 +185,44 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             float acc[COLS_PER_EPI];
 #pragma unroll
             for (int i = 0; i < COLS_PER_EPI; ++i) acc[i] = 0.0f;
+            // scales of the first K block; later ones are fetched a block ahead
+            float sa_next = row_ok ? __ldg(sa_row) : 0.0f;
+            float sb_next = nb_ok ? __ldg(sb_row) : 0.0f;
             for (int kb = 0; kb < nk; ++kb, ++pcount) {
                 const uint32_t buf = pcount & 1u;
                 const uint32_t pph = (pcount >> 1) & 1u;
-                const float scale = __fmul_rn(row_ok ? __ldg(sa_row + kb) : 0.0f, nb_ok ? __ldg(sb_row + kb) : 0.0f);
+                const float scale = __fmul_rn(sa_next, sb_next);
+                if (kb + 1 < nk) {
+                    sa_next = row_ok ? __ldg(sa_row + kb + 1) : 0.0f;
+                    sb_next = nb_ok ? __ldg(sb_row + kb + 1) : 0.0f;
+                }
                 int w_ok = 1;
                 if (lane == 0) w_ok = mbar_wait(&bars->part_full[buf], pph, abort_flag, p.status, SITE_EPI) ? 1 : 0;
                 w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
                 if (!w_ok) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t t_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * PART_COLS + half * COLS_PER_EPI;
+                // two 16-column loads in flight: the next chunk loads while this one is promoted
+                uint32_t ra[16], rb[16];
+                tmem_ld_32x32b_x16(t_addr, ra);
+                tmem_ld_wait_regs(ra);
 #pragma unroll
-                for (int c = 0; c < COLS_PER_EPI; c += 16) {
-                    uint32_t r[16];
-                    tmem_ld_32x32b_x16(t_addr + c, r);
-                    tmem_ld_wait();
+                for (int c = 0; c < COLS_PER_EPI; c += 32) {
+                    tmem_ld_32x32b_x16(t_addr + c + 16, rb);
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) acc[c + i] = fmaf(__uint_as_float(r[i]), scale, acc[c + i]);
+                    for (int i = 0; i < 16; i += 2)
+                        fma2_scalar(acc[c + i], acc[c + i + 1], __uint_as_float(ra[i]), __uint_as_float(ra[i + 1]), scale);
+                    tmem_ld_wait_regs(rb);
+                    if (c + 32 < COLS_PER_EPI) tmem_ld_32x32b_x16(t_addr + c + 32, ra);
+#pragma unroll
+                    for (int i = 0; i < 16; i += 2)
+                        fma2_scalar(acc[c + 16 + i], acc[c + 17 + i], __uint_as_float(rb[i]), __uint_as_float(rb[i + 1]), scale);
+                    if (c + 32 < COLS_PER_EPI) tmem_ld_wait_regs(ra);
                 }
+                // release the partial buffer: one arrival per warp
                 tc_fence_before();
-                mbar_arrive(&bars->part_empty[buf]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->part_empty[buf]);
             }
             if (!ok) break;
             // store this row's 128-column segment

@@ -203,7 +203,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 uint32_t r[32];
                 __syncwarp();
                 tmem_ld_32x32b_x32(t_row + c, r);
-                tmem_ld_wait();
+                tmem_ld_wait_regs(r);
                 const int n0 = nt * BN + c;
                 if (!row_ok || n0 >= p.N) continue;
                 const bool full_chunk = (n0 + 32 <= p.N);

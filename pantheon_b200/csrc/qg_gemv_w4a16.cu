@@ -7,17 +7,34 @@
 // S, Z fp16 [K/128, N]; Y bf16 or fp32 [M, N].
 //
 // The weights are read once per call, so the kernel is a stream over W: each
-// thread owns 4 adjacent columns and issues 128-bit non-allocating loads of
-// W (4 columns x 8 k per load), 8 loads deep, coalesced across the warp.  The
-// int4 -> bf16 unpack is done in registers: one LOP3 turns two nibbles into a
-// bf16 pair 128 + u (exact), and fma.rn.f32.bf16 multiplies it by the bf16
-// activation exactly and accumulates in fp32.  Per group of 128 the offset and
-// zero point come out algebraically:
-//     sum_k x (u - 8 - z) s = s * (sum_k x (128 + u) - (136 + z) * sum_k x),
-// with sum_k x computed once per CTA and group.  K is split over CTAs for
-// parallelism; each CTA writes its fp32 partial to a workspace and the last
-// CTA of a column block (atomic ticket) sums the partials in split order and
-// writes Y, so the result is bit-for-bit reproducible run to run.
+// thread owns CPT adjacent columns and issues non-allocating 64/128-bit loads
+// of W (CPT columns x 8 k per load), coalesced across the warp, software-
+// pipelined so the loads of the next batch are in flight while the current
+// batch is unpacked.  Per group of 128 the group's dot product is folded with
+// its scale and zero point:  sum_k x (u - 8 - z) s = s * (sum_k x u - (8 + z) sum_k x).
+//
+// The inner product sum_k x u, two ways:
+//   M <= 2   integer: the word's nibbles become bytes with one shift and two
+//            masks (u0 u2 u4 u6 | u1 u3 u5 u7), the activations of each
+//            (row, group) are staged as int16 fixed point with a shared power-
+//            of-two scale (the group's absmax maps below 2^14), and dp2a
+//            forms two 16x8-bit products per instruction into an exact int32
+//            group accumulator.  The only rounding is the activation's, at
+//            most 2^-15 of the group absmax per element.
+//   M >= 4   floating point: masking nibble j in place (w & (15 << s)) leaves
+//            the fp32 denormal u * 2^(s - 149), exact; with activations staged
+//            as x * 2^(109 - s) each product is u * x * 2^-40 exactly, and one
+//            unpacked weight pair serves every row through packed
+//            fma.rn.f32x2 into fp32 accumulators.
+// The sum of the activations of each group is exact fp32 from bf16.
+//
+// Work split: the K/8 packed rows of a column block are cut into `splits`
+// contiguous ranges of (almost) equal length, so the grid is one wave of
+// equally sized CTAs; a range may begin or end inside a group, and each group
+// segment is folded with its own scale and zero point.  Each CTA writes its
+// fp32 partial to the workspace; the last CTA of a column block (atomic
+// ticket) sums the partials in split order and writes Y, so the result is
+// bit-for-bit reproducible run to run.
 //
 // The path it sits on in the reference: llm_decode (kernels/llm_decode/
 // llm_decode.cpp:28-46, a KV gather + FMA chain with no weights) is the decode
@@ -33,31 +50,53 @@ namespace qg {
 namespace w4 {
 
 constexpr int THREADS = 128;
-constexpr int COLS_PER_THREAD = 4;
-constexpr int COLS_PER_CTA = THREADS * COLS_PER_THREAD;   // 512
 constexpr int GROUP = 128;
-constexpr int CHUNKS_PER_GROUP = GROUP / 8;               // 16 uint4 loads per group per thread
+constexpr int CHUNKS_PER_GROUP = GROUP / 8;
 constexpr int MAX_M = 16;
+// The split depends only on the shape (sized for the 148 SMs of a B200), so the
+// workspace size is a function of (M, N, K) alone.
+constexpr int kSplitSms = 148;
+// Floating path: products are accumulated as u * x * 2^-40; 2^40 undoes it.
+constexpr float kUnscale = 1099511627776.0f;
+
+// Per row-count template: integer or floating inner product, columns per
+// thread, resident CTAs per SM (register budget), loads per pipeline half.
+__host__ __device__ constexpr bool int_path(int mt) { return mt <= 2; }
+__host__ __device__ constexpr int cols_per_thread(int mt) { return mt >= 8 ? 2 : 4; }
+__host__ __device__ constexpr int blocks_per_sm(int mt) { return mt == 1 ? 7 : mt == 2 ? 5 : mt <= 8 ? 3 : 2; }
+__host__ __device__ constexpr int load_depth(int mt) { return mt <= 2 ? 4 : 2; }
+__host__ __device__ constexpr int cols_per_cta(int mt) { return THREADS * cols_per_thread(mt); }
 
 struct Params {
     const __nv_bfloat16* X;
-    const uint4* W;          // viewed as uint4 = 4 columns of one k8 row
+    const uint32_t* W;
     const __half* S;
     const __half* Z;
     void* Y;
-    float* ws;               // [splits][Mpad][N] fp32 partials
-    unsigned int* tickets;   // [col_blocks], zero between calls
+    float* ws;               // [splits][MT][N] fp32 partials
+    unsigned int* tickets;   // [column blocks], zero between calls
     int M, N, K;
-    int splits;              // K is cut into `splits` ranges of k_per_split
-    int k_per_split;         // multiple of GROUP
+    int splits;
     int out_type;
 };
 
-__device__ __forceinline__ float fma_bf16(uint16_t a, uint16_t b, float c) {
-    float d;
-    asm("fma.rn.f32.bf16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
-    return d;
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float p0, float p1, float x0, float x1) {
+    asm("{\n\t.reg .b64 a, p, x;\n\t"
+        "mov.b64 a, {%0, %1};\n\t"
+        "mov.b64 p, {%2, %3};\n\t"
+        "mov.b64 x, {%4, %5};\n\t"
+        "fma.rn.f32x2 a, p, x, a;\n\t"
+        "mov.b64 {%0, %1}, a;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(p0), "f"(p1), "f"(x0), "f"(x1));
 }
+
+template <int CPT>
+struct WVec;
+template <>
+struct WVec<4> { using T = uint4; };
+template <>
+struct WVec<2> { using T = uint2; };
 
 __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
     uint4 v;
@@ -65,142 +104,296 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
+__device__ __forceinline__ uint2 ld_stream(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int c) { return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w; }
+__device__ __forceinline__ uint32_t word_of(const uint2& v, int c) { return c == 0 ? v.x : v.y; }
 
-// acc[m][c] += sum over the 8 k of one packed word w (column c) of x[m][k] * (128 + u_k).
-template <int MT>
-__device__ __forceinline__ void accumulate_word(uint32_t w, const uint16_t (*xs)[8], float (&acc)[MT]) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        // nibbles j (k = j) and j + 4 (k = j + 4) -> bf16 pair (128 + u_j, 128 + u_{j+4})
-        const uint32_t pair = ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
-        const uint16_t lo = (uint16_t)(pair & 0xFFFFu);
-        const uint16_t hi = (uint16_t)(pair >> 16);
-#pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            acc[m] = fma_bf16(xs[m][j], lo, acc[m]);
-            acc[m] = fma_bf16(xs[m][j + 4], hi, acc[m]);
-        }
-    }
+// Floating path: the eight weights of one packed word as exact fp32 denormals u_k * 2^(s_k - 149).
+__device__ __forceinline__ void unpack_denormal(uint32_t w, float (&v)[8]) {
+    const uint32_t h = w >> 12;
+    v[0] = __uint_as_float(w & 0x0000000Fu);   // s = 0
+    v[1] = __uint_as_float(w & 0x000000F0u);   // s = 4
+    v[2] = __uint_as_float(w & 0x00000F00u);   // s = 8
+    v[3] = __uint_as_float(w & 0x0000F000u);   // s = 12
+    v[4] = __uint_as_float(w & 0x000F0000u);   // s = 16
+    v[5] = __uint_as_float(h & 0x00000F00u);   // nibble 5 -> s = 8
+    v[6] = __uint_as_float(h & 0x0000F000u);   // nibble 6 -> s = 12
+    v[7] = __uint_as_float(h & 0x000F0000u);   // nibble 7 -> s = 16
 }
 
-template <int MT>
-__global__ void __launch_bounds__(THREADS)
-gemv_w4a16_kernel(Params p) {
-    // X slice of this CTA's k range (bf16 bits) and its per-group sums.
-    extern __shared__ uint16_t smem16[];
-    const int k0 = blockIdx.y * p.k_per_split;
-    const int klen = min(p.k_per_split, p.K - k0);
-    const int ngroups = klen / GROUP;
-    uint16_t* xs = smem16;                                               // [MT][k_per_split]
-    float* xsum = reinterpret_cast<float*>(smem16 + MT * p.k_per_split); // [MT][groups]
+// Floating path: 2^(109 - s_k) for the nibble positions above.
+__device__ __forceinline__ float prescale(int k) {
+    const int s = k < 5 ? 4 * k : 4 * (k - 3);
+    return __uint_as_float((uint32_t)(127 + 109 - s) << 23);
+}
 
-    // Stage X (rows >= M read as zero) and the group sums.
-    for (int i = threadIdx.x; i < MT * klen / 8; i += THREADS) {
-        const int m = i / (klen / 8);
-        const int c = i - m * (klen / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (m < p.M) v = *reinterpret_cast<const uint4*>(p.X + (size_t)m * p.K + k0 + c * 8);
-        *reinterpret_cast<uint4*>(xs + m * p.k_per_split + c * 8) = v;
+__device__ __forceinline__ float pow2(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
+template <int MT>
+__global__ void __launch_bounds__(THREADS, blocks_per_sm(MT))
+gemv_w4a16_kernel(Params p) {
+    constexpr bool INT = int_path(MT);
+    constexpr int CPT = cols_per_thread(MT);
+    constexpr int DEPTH = load_depth(MT);
+    constexpr int CPC = cols_per_cta(MT);
+    using VT = typename WVec<CPT>::T;
+
+    const int nchunks = p.K / 8;
+    const int c0 = (int)(((long long)blockIdx.y * nchunks) / p.splits);
+    const int c1 = (int)(((long long)(blockIdx.y + 1) * nchunks) / p.splits);
+    const int len = c1 - c0;
+    const int g_first = c0 / CHUNKS_PER_GROUP;
+    const int n_groups = (c1 - 1) / CHUNKS_PER_GROUP - g_first + 1;
+    const int col0 = blockIdx.x * CPC;
+
+    // Shared memory for this CTA's k range (g = group index within the range):
+    //   gsum  fp32  [groups][MT]     sum of the activations of the group segment
+    //   gpow  fp32  [groups][MT]     integer path: 2^e of the segment's fixed point
+    //   sz    half2 [groups][CPC]    (scale, zero) of each column
+    //   xdat  integer path: int32 [len][MT][4]  int16 pairs (x0,x2) (x4,x6) (x1,x3) (x5,x7)
+    //         floating path: fp32 [len][MT][8]  x * 2^(109 - s_k)
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int gmax = (len + CHUNKS_PER_GROUP - 1) / CHUNKS_PER_GROUP + 1;
+    float* gsum = reinterpret_cast<float*>(smem);
+    float* gpow = gsum + gmax * MT;
+    __half2* sz = reinterpret_cast<__half2*>(gpow + gmax * MT);
+    // 16-byte aligned for the int4 / float4 accesses (the tables above end on a
+    // 4-byte boundary; the size computation reserves the padding).
+    uint8_t* xdat = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sz + (size_t)gmax * CPC) + 15) &
+                                               ~static_cast<uintptr_t>(15));
+    int4* xi = reinterpret_cast<int4*>(xdat);
+    float* xq = reinterpret_cast<float*>(xdat);
+
+    // The first two batches of weights are requested before anything else, so
+    // they stream in while the prologue below stages activations and scales.
+    const int n0 = col0 + threadIdx.x * CPT;
+    const bool active = n0 < p.N;   // N % 4 == 0, so a thread's columns are wholly in or out
+    const size_t row_stride = (size_t)p.N / CPT;                         // VT per packed row
+    const VT* wp = reinterpret_cast<const VT*>(p.W) + (size_t)c0 * row_stride + (active ? n0 / CPT : 0);
+    VT wa[DEPTH], wb[DEPTH];
+    auto load_batch = [&](VT (&dst)[DEPTH], int base) {
+#pragma unroll
+        for (int d = 0; d < DEPTH; ++d)
+            if (base + d < len) dst[d] = ld_stream(wp + (size_t)(base + d) * row_stride);
+    };
+    if (active) {
+        load_batch(wa, 0);
+        if (DEPTH < len) load_batch(wb, DEPTH);
     }
-    __syncthreads();
+
+    // Scales and zero points of this CTA's groups, staged once with 64-bit
+    // loads (rows of S and Z are 8-byte aligned because N % 4 == 0): the group
+    // folds never wait on a global load mid-stream.
+    for (int t = threadIdx.x; t < n_groups * (CPC / 4); t += THREADS) {
+        const int g = t / (CPC / 4), c4 = (t - g * (CPC / 4)) * 4;
+        const int n = col0 + c4;
+        uint2 s4 = make_uint2(0, 0), z4 = make_uint2(0, 0);
+        if (n < p.N) {
+            s4 = __ldg(reinterpret_cast<const uint2*>(p.S + (size_t)(g_first + g) * p.N + n));
+            z4 = __ldg(reinterpret_cast<const uint2*>(p.Z + (size_t)(g_first + g) * p.N + n));
+        }
+        const __half* sh = reinterpret_cast<const __half*>(&s4);
+        const __half* zh = reinterpret_cast<const __half*>(&z4);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sz[g * CPC + c4 + j] = __halves2half2(sh[j], zh[j]);
+    }
+    // Per (group segment, row): exact fp32 sum and absmax of the activations (one warp each).
     {
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        for (int t = warp; t < MT * ngroups; t += THREADS / 32) {
-            const int m = t / ngroups, g = t - m * ngroups;
-            float s = 0.0f;
-            for (int k = lane; k < GROUP; k += 32)
-                s += __uint_as_float((uint32_t)xs[m * p.k_per_split + g * GROUP + k] << 16);
+        for (int t = warp; t < n_groups * MT; t += THREADS / 32) {
+            const int g = t / MT, m = t - g * MT;
+            const int ca = max(c0, (g_first + g) * CHUNKS_PER_GROUP);
+            const int cb = min(c1, (g_first + g + 1) * CHUNKS_PER_GROUP);
+            float s = 0.0f, a = 0.0f;
+            if (m < p.M && lane < cb - ca) {   // one packed row (8 activations) per lane, <= 16 rows
+                const uint4 raw = *reinterpret_cast<const uint4*>(p.X + (size_t)m * p.K + (size_t)(ca + lane) * 8);
+                const uint32_t r4[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            if (lane == 0) xsum[m * ngroups + g] = s;
+                for (int i = 0; i < 4; ++i) {
+                    const float v0 = __uint_as_float(r4[i] << 16), v1 = __uint_as_float(r4[i] & 0xFFFF0000u);
+                    s += v0 + v1;
+                    a = fmaxf(a, fmaxf(fabsf(v0), fabsf(v1)));
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                s += __shfl_xor_sync(0xffffffffu, s, o);
+                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+            }
+            if (lane == 0) {
+                gsum[g * MT + m] = s;
+                // fixed point: the absmax of the segment maps below 2^14 (fits int16 with margin)
+                int e = 0;
+                if (a > 0.0f) {
+                    const int E = (int)((__float_as_uint(a) >> 23) & 0xFF) - 127;
+                    e = 13 - E;
+                    e = e > 126 ? 126 : (e < -126 ? -126 : e);
+                }
+                gpow[g * MT + m] = pow2(e);
+            }
+        }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < len * MT; t += THREADS) {
+        const int ch = t / MT, m = t - ch * MT;
+        float v[8];
+        if (m < p.M) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(p.X + (size_t)m * p.K + (size_t)(c0 + ch) * 8);
+            const uint32_t r4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[2 * i] = __uint_as_float(r4[i] << 16);
+                v[2 * i + 1] = __uint_as_float(r4[i] & 0xFFFF0000u);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        }
+        if (INT) {
+            const float sc = gpow[((c0 + ch) / CHUNKS_PER_GROUP - g_first) * MT + m];
+            int q[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[i] = __float2int_rn(v[i] * sc);
+            auto pk = [](int lo, int hi) { return (int)(((uint32_t)lo & 0xFFFFu) | ((uint32_t)hi << 16)); };
+            xi[(size_t)ch * MT + m] = make_int4(pk(q[0], q[2]), pk(q[4], q[6]), pk(q[1], q[3]), pk(q[5], q[7]));
+        } else {
+            float* dst = xq + ((size_t)ch * MT + m) * 8;
+            *reinterpret_cast<float4*>(dst) =
+                make_float4(v[0] * prescale(0), v[1] * prescale(1), v[2] * prescale(2), v[3] * prescale(3));
+            *reinterpret_cast<float4*>(dst + 4) =
+                make_float4(v[4] * prescale(4), v[5] * prescale(5), v[6] * prescale(6), v[7] * prescale(7));
         }
     }
     __syncthreads();
 
-    const int n0 = blockIdx.x * COLS_PER_CTA + threadIdx.x * COLS_PER_THREAD;
-    const bool active = n0 < p.N;   // N % 4 == 0, so a thread is wholly in or out
-    float y[MT][COLS_PER_THREAD];
+    float y[MT][CPT];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
-        for (int c = 0; c < COLS_PER_THREAD; ++c) y[m][c] = 0.0f;
+        for (int c = 0; c < CPT; ++c) y[m][c] = 0.0f;
 
     if (active) {
-        const size_t row_stride = (size_t)p.N / 4;                   // uint4 per k8 row
-        const uint4* wp = p.W + (size_t)(k0 / 8) * row_stride + n0 / 4;
-        for (int g = 0; g < ngroups; ++g) {
-            float acc[COLS_PER_THREAD][MT];
+        int iacc[CPT][MT];           // integer path
+        float facc[CPT][MT][2];      // floating path
 #pragma unroll
-            for (int c = 0; c < COLS_PER_THREAD; ++c)
+        for (int c = 0; c < CPT; ++c)
 #pragma unroll
-                for (int m = 0; m < MT; ++m) acc[c][m] = 0.0f;
+            for (int m = 0; m < MT; ++m) { iacc[c][m] = 0; facc[c][m][0] = facc[c][m][1] = 0.0f; }
+
+        // End of a group segment at packed row i: fold with its scale and zero point.
+        auto fold = [&](int i) {
+            const int g = (c0 + i) / CHUNKS_PER_GROUP - g_first;
 #pragma unroll
-            for (int half = 0; half < CHUNKS_PER_GROUP; half += 8) {
-                uint4 wv[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) wv[i] = ld_stream(wp + (size_t)(g * CHUNKS_PER_GROUP + half + i) * row_stride);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int kk = g * GROUP + (half + i) * 8;   // k offset inside this CTA's slice
-                    uint16_t xv[MT][8];
-#pragma unroll
-                    for (int m = 0; m < MT; ++m) {
-                        const uint4 x4 = *reinterpret_cast<const uint4*>(xs + m * p.k_per_split + kk);
-                        xv[m][0] = (uint16_t)(x4.x & 0xFFFF); xv[m][1] = (uint16_t)(x4.x >> 16);
-                        xv[m][2] = (uint16_t)(x4.y & 0xFFFF); xv[m][3] = (uint16_t)(x4.y >> 16);
-                        xv[m][4] = (uint16_t)(x4.z & 0xFFFF); xv[m][5] = (uint16_t)(x4.z >> 16);
-                        xv[m][6] = (uint16_t)(x4.w & 0xFFFF); xv[m][7] = (uint16_t)(x4.w >> 16);
-                    }
-                    accumulate_word<MT>(wv[i].x, xv, acc[0]);
-                    accumulate_word<MT>(wv[i].y, xv, acc[1]);
-                    accumulate_word<MT>(wv[i].z, xv, acc[2]);
-                    accumulate_word<MT>(wv[i].w, xv, acc[3]);
-                }
-            }
-            // fold in scale and zero point of this group
-            const int gg = (k0 / GROUP) + g;
-            const uint2 s2 = *reinterpret_cast<const uint2*>(p.S + (size_t)gg * p.N + n0);
-            const uint2 z2 = *reinterpret_cast<const uint2*>(p.Z + (size_t)gg * p.N + n0);
-            const __half* sh = reinterpret_cast<const __half*>(&s2);
-            const __half* zh = reinterpret_cast<const __half*>(&z2);
-#pragma unroll
-            for (int c = 0; c < COLS_PER_THREAD; ++c) {
-                const float sc = __half2float(sh[c]);
-                const float off = 136.0f + __half2float(zh[c]);
+            for (int c = 0; c < CPT; ++c) {
+                const float2 f = __half22float2(sz[g * CPC + threadIdx.x * CPT + c]);
 #pragma unroll
                 for (int m = 0; m < MT; ++m) {
-                    const float t = fmaf(-off, xsum[m * ngroups + g], acc[c][m]);
-                    y[m][c] = fmaf(sc, t, y[m][c]);
+                    const float corr = -(8.0f + f.y) * gsum[g * MT + m];
+                    float t;
+                    if (INT) {
+                        t = fmaf((float)iacc[c][m], 1.0f / gpow[g * MT + m], corr);
+                        iacc[c][m] = 0;
+                    } else {
+                        t = fmaf(facc[c][m][0] + facc[c][m][1], kUnscale, corr);
+                        facc[c][m][0] = facc[c][m][1] = 0.0f;
+                    }
+                    y[m][c] = fmaf(f.x, t, y[m][c]);
                 }
             }
+        };
+
+        // One packed row of the CTA's range.
+        auto chunk = [&](int i, const VT& wvd) {
+            if (INT) {
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    const int4 xw = xi[(size_t)i * MT + m];
+#pragma unroll
+                    for (int c = 0; c < CPT; ++c) {
+                        const uint32_t w = word_of(wvd, c);
+                        const int b0 = (int)(w & 0x0F0F0F0Fu);          // u0 u2 u4 u6
+                        const int b1 = (int)((w >> 4) & 0x0F0F0F0Fu);   // u1 u3 u5 u7
+                        int a = iacc[c][m];
+                        a = __dp2a_lo(xw.x, b0, a);
+                        a = __dp2a_hi(xw.y, b0, a);
+                        a = __dp2a_lo(xw.z, b1, a);
+                        a = __dp2a_hi(xw.w, b1, a);
+                        iacc[c][m] = a;
+                    }
+                }
+            } else {
+                float wf[CPT][8];
+#pragma unroll
+                for (int c = 0; c < CPT; ++c) unpack_denormal(word_of(wvd, c), wf[c]);
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    const float4 xa = *reinterpret_cast<const float4*>(xq + ((size_t)i * MT + m) * 8);
+                    const float4 xb = *reinterpret_cast<const float4*>(xq + ((size_t)i * MT + m) * 8 + 4);
+#pragma unroll
+                    for (int c = 0; c < CPT; ++c) {
+                        ffma2(facc[c][m][0], facc[c][m][1], wf[c][0], wf[c][1], xa.x, xa.y);
+                        ffma2(facc[c][m][0], facc[c][m][1], wf[c][2], wf[c][3], xa.z, xa.w);
+                        ffma2(facc[c][m][0], facc[c][m][1], wf[c][4], wf[c][5], xb.x, xb.y);
+                        ffma2(facc[c][m][0], facc[c][m][1], wf[c][6], wf[c][7], xb.z, xb.w);
+                    }
+                }
+            }
+            if (((c0 + i + 1) % CHUNKS_PER_GROUP) == 0 || i + 1 == len) fold(i);
+        };
+
+        // Software pipeline: the loads of batch b + 1 are in flight while batch
+        // b is unpacked, so each warp keeps DRAM requests outstanding through
+        // its compute phase (ping-pong register buffers, no copies).
+        // (batches 0 and 1 were requested before the prologue)
+        auto run_batch = [&](const VT (&src)[DEPTH], int base) {
+#pragma unroll
+            for (int d = 0; d < DEPTH; ++d)
+                if (base + d < len) chunk(base + d, src[d]);
+        };
+        for (int base = 0; base < len; base += 2 * DEPTH) {
+            if (base > 0 && base + DEPTH < len) load_batch(wb, base + DEPTH);
+            run_batch(wa, base);
+            if (base + DEPTH >= len) break;
+            if (base + 2 * DEPTH < len) load_batch(wa, base + 2 * DEPTH);
+            run_batch(wb, base + DEPTH);
         }
     }
 
-    // ---- split-K: publish the partial; the last CTA of this column block reduces.
-    const int mpad = MT;
-    if (p.splits == 1) {
-        if (active) {
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                if (m >= p.M) break;
-                if (p.out_type == QG_OUT_F32) {
-                    *reinterpret_cast<float4*>(static_cast<float*>(p.Y) + (size_t)m * p.N + n0) =
-                        make_float4(y[m][0], y[m][1], y[m][2], y[m][3]);
-                } else {
-                    __nv_bfloat162 a = __floats2bfloat162_rn(y[m][0], y[m][1]);
-                    __nv_bfloat162 b = __floats2bfloat162_rn(y[m][2], y[m][3]);
-                    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.Y) + (size_t)m * p.N + n0) =
-                        make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-                }
+    // ---- publish: directly when K is not split, else partial + ticket
+    auto store_row = [&](int m, const float* v) {
+        if (p.out_type == QG_OUT_F32) {
+            float* dst = static_cast<float*>(p.Y) + (size_t)m * p.N + n0;
+            if (CPT == 4) *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+            else *reinterpret_cast<float2*>(dst) = make_float2(v[0], v[1]);
+        } else {
+            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.Y) + (size_t)m * p.N + n0;
+            __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+            if (CPT == 4) {
+                __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+                *reinterpret_cast<uint2*>(dst) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+            } else {
+                *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<uint32_t*>(&a);
             }
         }
+    };
+    if (p.splits == 1) {
+        if (active)
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+                if (m < p.M) store_row(m, y[m]);
         return;
     }
     if (active) {
 #pragma unroll
-        for (int m = 0; m < MT; ++m)
-            *reinterpret_cast<float4*>(p.ws + ((size_t)blockIdx.y * mpad + m) * p.N + n0) =
-                make_float4(y[m][0], y[m][1], y[m][2], y[m][3]);
+        for (int m = 0; m < MT; ++m) {
+            float* dst = p.ws + ((size_t)blockIdx.y * MT + m) * p.N + n0;
+            if (CPT == 4) *reinterpret_cast<float4*>(dst) = make_float4(y[m][0], y[m][1], y[m][2], y[m][3]);
+            else *reinterpret_cast<float2*>(dst) = make_float2(y[m][0], y[m][1]);
+        }
     }
     __threadfence();
     __syncthreads();
@@ -210,57 +403,67 @@ gemv_w4a16_kernel(Params p) {
     if (ticket != (unsigned int)p.splits - 1) return;
     __threadfence();
     if (active) {
-        for (int m = 0; m < p.M && m < MT; ++m) {
-            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int m = 0; m < MT && m < p.M; ++m) {
+            float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             for (int sp = 0; sp < p.splits; ++sp) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(p.ws + ((size_t)sp * mpad + m) * p.N + n0));
-                s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+                const float* src = p.ws + ((size_t)sp * MT + m) * p.N + n0;
+                if (CPT == 4) {
+                    const float4 v = __ldcg(reinterpret_cast<const float4*>(src));
+                    s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
+                } else {
+                    const float2 v = __ldcg(reinterpret_cast<const float2*>(src));
+                    s[0] += v.x; s[1] += v.y;
+                }
             }
-            if (p.out_type == QG_OUT_F32) {
-                *reinterpret_cast<float4*>(static_cast<float*>(p.Y) + (size_t)m * p.N + n0) = s;
-            } else {
-                __nv_bfloat162 a = __floats2bfloat162_rn(s.x, s.y);
-                __nv_bfloat162 b = __floats2bfloat162_rn(s.z, s.w);
-                *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.Y) + (size_t)m * p.N + n0) =
-                    make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-            }
+            store_row(m, s);
         }
     }
     if (threadIdx.x == 0) p.tickets[blockIdx.x] = 0;   // ready for the next call
 }
 
-// Rows per launch template and K split for a given M.
 static int m_template(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16; }
 
-// The split depends only on the shape (sized for the 148 SMs of a B200), so the
-// workspace size is a function of (M, N, K) alone.
-constexpr int kSplitSms = 148;
+static int col_blocks_for(int mt, int N) { return (N + cols_per_cta(mt) - 1) / cols_per_cta(mt); }
 
-static int choose_splits(int MT, int N, int K) {
-    const int col_blocks = (N + COLS_PER_CTA - 1) / COLS_PER_CTA;
-    const int groups = K / GROUP;
-    // enough CTAs for several per SM; fewer, longer splits when M makes the CTA compute-heavy
-    const int target_ctas = (MT <= 2 ? 12 : MT <= 4 ? 8 : 4) * kSplitSms;
-    int splits = (target_ctas + col_blocks - 1) / col_blocks;
-    if (splits > groups) splits = groups;
+// Shared-memory bytes for a K range of `len` packed rows (see the kernel's layout).
+static size_t smem_bytes_len(int mt, int len) {
+    const size_t gmax = (size_t)(len + CHUNKS_PER_GROUP - 1) / CHUNKS_PER_GROUP + 1;
+    const size_t per_chunk = int_path(mt) ? (size_t)mt * 16 : (size_t)mt * 32;
+    return gmax * mt * 8 + gmax * cols_per_cta(mt) * 4 + (size_t)len * per_chunk + 16;
+}
+constexpr size_t kSmemBudget = 180 * 1024;
+
+// Equal contiguous K ranges per column block, as many as fill one wave of the
+// resident CTAs (at least two packed rows each), and never fewer than keep the
+// staged activations within the shared-memory budget.
+static int choose_splits(int mt, int N, int K) {
+    const int nchunks = K / 8;
+    const int slots = kSplitSms * blocks_per_sm(mt);
+    int splits = slots / col_blocks_for(mt, N);
+    const int max_splits = nchunks / 2;
+    if (splits > max_splits) splits = max_splits;
     if (splits < 1) splits = 1;
-    while (groups % splits) --splits;   // equal k ranges, each a whole number of groups
+    while (splits < max_splits && smem_bytes_len(mt, (nchunks + splits - 1) / splits) > kSmemBudget) ++splits;
     return splits;
 }
 
+static size_t smem_bytes(int mt, int K, int splits) { return smem_bytes_len(mt, (K / 8 + splits - 1) / splits); }
+
 } // namespace w4
 
-uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int sm_count) {
+// Workspace: fp32 partials for the largest row chunk, then one ticket per
+// column block of the narrowest column-block width (256 columns).
+uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int /*sm_count*/) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    uint64_t total = 0;
+    uint64_t partials = 0;
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mt = w4::m_template(M - m0 < w4::MAX_M ? M - m0 : w4::MAX_M);
         const int splits = w4::choose_splits(mt, N, K);
         const uint64_t ws = (uint64_t)splits * mt * N * 4;
-        if (ws > total) total = ws;
+        if (ws > partials) partials = ws;
     }
-    const uint64_t col_blocks = (uint64_t)(N + w4::COLS_PER_CTA - 1) / w4::COLS_PER_CTA;
-    return ((total + 255) & ~255ull) + col_blocks * 4;
+    const uint64_t tickets = (uint64_t)((N + 255) / 256) * 4;
+    return ((partials + 255) & ~255ull) + tickets;
 }
 
 int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,
@@ -280,37 +483,35 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
     QG_CHECK_ARG(workspace && workspace_bytes >= need,
                  "qg_gemv_w4a16: workspace of %llu bytes needed (got %llu)", (unsigned long long)need,
                  (unsigned long long)workspace_bytes);
-    const int col_blocks = (N + w4::COLS_PER_CTA - 1) / w4::COLS_PER_CTA;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const uint64_t ws_floats_bytes = need - (uint64_t)col_blocks * 4;
+    const uint64_t tickets_off = need - (uint64_t)((N + 255) / 256) * 4;
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mrows = (M - m0) < w4::MAX_M ? (M - m0) : w4::MAX_M;
         const int mt = w4::m_template(mrows);
         const int splits = w4::choose_splits(mt, N, K);
         w4::Params p;
         p.X = static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K;
-        p.W = static_cast<const uint4*>(W);
+        p.W = static_cast<const uint32_t*>(W);
         p.S = static_cast<const __half*>(S);
         p.Z = static_cast<const __half*>(Z);
         p.Y = static_cast<uint8_t*>(Y) + (size_t)m0 * N * (out_type == QG_OUT_F32 ? 4 : 2);
         p.ws = reinterpret_cast<float*>(ws);
-        p.tickets = reinterpret_cast<unsigned int*>(ws + ws_floats_bytes);
+        p.tickets = reinterpret_cast<unsigned int*>(ws + tickets_off);
         p.M = mrows;
         p.N = N;
         p.K = K;
         p.splits = splits;
-        p.k_per_split = K / splits;
         p.out_type = out_type;
-        const size_t smem = (size_t)mt * p.k_per_split * 2 + (size_t)mt * (p.k_per_split / w4::GROUP) * 4;
+        const size_t smem = w4::smem_bytes(mt, K, splits);
         QG_CHECK_ARG(smem <= 200 * 1024, "qg_gemv_w4a16: K slice too large for shared memory");
-        dim3 grid(col_blocks, splits);
+        dim3 grid(w4::col_blocks_for(mt, N), splits);
         switch (mt) {
-#define QG_W4_LAUNCH(MTV)                                                                                   \
-    case MTV:                                                                                               \
-        if (smem > 48 * 1024)                                                                               \
-            QG_CUDA(cudaFuncSetAttribute(w4::gemv_w4a16_kernel<MTV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                         (int)smem));                                                       \
-        w4::gemv_w4a16_kernel<MTV><<<grid, w4::THREADS, smem, stream>>>(p);                                 \
+#define QG_W4_LAUNCH(MTV)                                                                                        \
+    case MTV:                                                                                                    \
+        if (smem > 48 * 1024)                                                                                    \
+            QG_CUDA(cudaFuncSetAttribute(w4::gemv_w4a16_kernel<MTV>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                         (int)smem));                                                            \
+        w4::gemv_w4a16_kernel<MTV><<<grid, w4::THREADS, smem, stream>>>(p);                                      \
         break;
             QG_W4_LAUNCH(1)
             QG_W4_LAUNCH(2)
@@ -328,10 +529,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
 
 extern "C" int qg_gemv_w4a16_workspace_bytes(int M, int N, int K, uint64_t* bytes) {
     QG_CHECK_ARG(bytes, "qg_gemv_w4a16_workspace_bytes: null argument");
-    qg::DeviceInfo* info = nullptr;
-    int sm = 148;
-    if (qg::current_device_info(&info) == QG_OK) sm = info->sm_count;
-    *bytes = qg::gemv_w4a16_workspace_bytes(M, N, K, sm);
+    *bytes = qg::gemv_w4a16_workspace_bytes(M, N, K, 0);
     return QG_OK;
 }
 

@@ -221,6 +221,50 @@ __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// TMEM -> registers: 32 lanes x 16 columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+// tcgen05.wait::ld that also names the registers of the loads it waits for, so
+// the compiler cannot move a use of those registers above the wait (the
+// tcgen05.ld asm statement is otherwise all it sees as their producer).
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                   "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
+// Two fp32 FMAs in one instruction: (a0, a1) = (p0, p1) * s + (a0, a1).
+__device__ __forceinline__ void fma2_scalar(float& a0, float& a1, float p0, float p1, float s) {
+    asm("{\n\t.reg .b64 a, p, s;\n\t"
+        "mov.b64 a, {%0, %1};\n\t"
+        "mov.b64 p, {%2, %3};\n\t"
+        "mov.b64 s, {%4, %4};\n\t"
+        "fma.rn.f32x2 a, p, s, a;\n\t"
+        "mov.b64 {%0, %1}, a;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(p0), "f"(p1), "f"(s));
+}
+
 // Shared-memory matrix descriptor (tcgen05 format): K-major operand tile whose
 // rows are 128 bytes long, stored with the 128-byte swizzle that TMA's
 // SWIZZLE_128B writes.  Eight-row groups are SBO = 1024 bytes apart; LBO is
