@@ -87,6 +87,13 @@ def workload_spec(args, pb):
                 "config": {"workload": "configs[2] FP8 e4m3 GEMM M=N=8192 K=16384, 1x128 / 128x128 fp32 scales, bf16 out",
                            "M": 8192, "N": 8192, "K": 16384, "seed": 2, "operand_sets": 1,
                            "l2": "inputs larger than L2: A + B = 256 MiB"}}
+    if args.workload == "nvfp4":
+        return {"name": "nvfp4", "fmt": pb.QG_FMT_NVFP4, "shape": (16384, 16384, 16384), "copies": 1, "seed": 4,
+                "unit": "TOPS", "bound": "tensor", "dtype": "e2m1 x ue4m3/16 (fp32 acc)", "launches_per_step": 1,
+                "traffic_key": "gemm_nvfp4_16384", "peak_mult": 4.0,
+                "config": {"workload": "configs[4] NVFP4 GEMM M=N=K=16384, ue4m3 scale per 16 + fp32 per-tensor, bf16 out",
+                           "M": 16384, "N": 16384, "K": 16384, "seed": 4, "operand_sets": 1,
+                           "l2": "inputs larger than L2: A + B = 256 MiB"}}
     return {"name": "int8", "fmt": pb.QG_FMT_INT8, "shape": (M, N, K), "copies": 2, "seed": 1, "unit": "TOPS",
             "bound": "tensor", "dtype": "int8", "launches_per_step": 1, "traffic_key": "gemm_i8_8192",
             "config": {"workload": "configs[1] INT8 W8A8 GEMM 8192x8192x8192, bf16 out, fp32 row/col scales",
@@ -300,9 +307,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         per_launch_s = ms / 1e3 / steps
         if wl["unit"] == "TOPS":
             work = ops / 1e12
-            peak = 2.0 * peaks["bf16_tflops"]
-            peak_src = f"2 x {peaks['source']} bf16 dense burst ({peaks['bf16_tflops']} TFLOP/s)"
-            extra = {"frac_of_datasheet_4500": work / per_launch_s / DATASHEET_INT8_TOPS}
+            mult = wl.get("peak_mult", 2.0)   # dense INT8/FP8 = 2x bf16, FP4 = 4x bf16 on this part
+            peak = mult * peaks["bf16_tflops"]
+            peak_src = f"{mult:g} x {peaks['source']} bf16 dense burst ({peaks['bf16_tflops']} TFLOP/s)"
+            datasheet = mult / 2.0 * DATASHEET_INT8_TOPS
+            extra = {f"frac_of_datasheet_{datasheet:g}": work / per_launch_s / datasheet,
+                     "frac_of_measured_sustained": work / per_launch_s / (mult * peaks["bf16_tflops_sustained"])}
         else:
             work = nbytes / 1e9
             peak = peaks["hbm_gbs"]
@@ -344,7 +354,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["int8", "fp8", "w4a16"], default="int8",
+    ap.add_argument("--workload", choices=["int8", "fp8", "nvfp4", "w4a16"], default="int8",
                     help="int8 = configs[1] (default, the headline); w4a16 = configs[3] GEMV")
     ap.add_argument("--m", type=int, default=0, help="rows of the W4A16 activations (1, 8 or 16)")
     args = ap.parse_args(argv)

@@ -186,6 +186,21 @@ QG_API int  qg_gemm_i8(const void* A, const void* B, const void* sa, const void*
 QG_API int  qg_gemm_fp8_b128(const void* A, const void* B, const void* sa, const void* sb,
                              void* C, int out_type, int M, int N, int K, void* stream);
 
+/* NVFP4: C[m,n] = out( ga*gb * sum_k (qa[m,k] sfa[m,k/16]) (qb[n,k] sfb[n,k/16]) ),
+ *   tensor cores (tcgen05.mma kind::mxf4nvf4, block 16), fp32 accumulate.
+ *   A, B: e2m1 codes packed two per byte along K (low nibble = even k),
+ *   [M, K/2] and [N, K/2] bytes, K % 256 == 0.
+ *   sfa, sfb: ue4m3 scale bytes (one per 16 elements along K) in the atom
+ *   layout: one 512-byte atom per (128-row block, 64-element K chunk), atoms
+ *   ordered [row block][K/64]; inside an atom row r's four scales are bytes
+ *   (r%32)*16 + ((r/32)%4)*4 + 0..3 (qg_nvfp4_sf_bytes gives the size).
+ *   ga, gb: per-tensor fp32 scales.  out_type QG_OUT_BF16 or QG_OUT_F32.
+ * Replaces: the per-kind body of ai_workload_kernel (ai_workload_template.h:157-177)
+ *   for configs[4]; the reference has no FP4 GEMM. */
+QG_API int  qg_gemm_nvfp4(const void* A, const void* sfa, const void* B, const void* sfb,
+                          float ga, float gb, void* C, int out_type, int M, int N, int K, void* stream);
+QG_API int  qg_nvfp4_sf_bytes(int rows, int K, uint64_t* bytes);
+
 /* W4A16 group-128 decode GEMV / skinny GEMM on the CUDA cores:
  *   Y[m,n] = sum_k X[m,k] * (q[k,n] - Z[k/128,n]) * S[k/128,n],  q = u - 8
  *   X bf16 [M,K]; W uint32 [K/8, N] with nibble j of word (k8, n) = u(8*k8+j, n)
@@ -244,6 +259,12 @@ QG_API int  qg_gen_normal_f32(void* out, uint64_t n, uint64_t seed, uint32_t ten
  * q = e4m3_rn_satfinite(x * (448/absmax)), scale = absmax/448 (fp32). */
 QG_API int  qg_gen_fp8(void* A, void* sa, void* B, void* sb, int M, int N, int K,
                        uint64_t seed, uint32_t tid0, void* stream);
+/* NVFP4 operands of configs[4]: values N(0,1) (A: tensor tid0, B: tid0+2);
+ * per-tensor scale g = absmax/(448*6) -> gscales[0..1] (device fp32);
+ * per 16 along K an ue4m3 scale sf = e4m3(blockmax/6/g); codes
+ * q = e2m1(x / (sf*g)).  `work` is 8 bytes of device scratch. */
+QG_API int  qg_gen_nvfp4(void* A, void* sfa, void* B, void* sfb, void* gscales, void* work,
+                         int M, int N, int K, uint64_t seed, uint32_t tid0, void* stream);
 /* W4A16 operands of configs[3]: X bf16 [M,K] = bf16(N(0,1)); W packed as in
  * qg_gemv_w4a16 with u uniform in [0,15] (q uniform in [-8,7]);
  * S fp16 = f16(U[0.005, 0.02]), Z fp16 = f16(U[-0.5, 0.5]) per (group, n).

@@ -166,6 +166,62 @@ def gemm_fp8(A, B, sa, sb, out_type: int = 0, rows=None):
     return C_
 
 
+def nvfp4_operands(M: int, N: int, K: int, seed: int, copy: int = 0):
+    """The NVFP4 workload's operands of copy `copy`: A, B packed e2m1 [R, K/2] (low nibble =
+    even k), scales ue4m3 in the PLAIN layout [R, K/16], per-tensor scales GA, GB
+    (values: tensor ids 8*copy+0 and 8*copy+2)."""
+    b = 8 * copy
+    out = []
+    for R, tid in ((M, b + 0), (N, b + 2)):
+        x = gen_normal_f32(R * K, seed, tid)
+        g = lib().qgo_nvfp4_global_scale(_p(x), x.size)
+        q = np.empty((R, K // 2), dtype=np.uint8)
+        sf = np.empty((R, K // 16), dtype=np.uint8)
+        lib().qgo_quant_nvfp4(_p(x), R, K, g, _p(q), _p(sf))
+        out.append((q, sf, np.float32(g)))
+    (A, SFA, GA), (B, SFB, GB) = out
+    return A, SFA, GA, B, SFB, GB
+
+
+def sf_to_atoms(sf: np.ndarray) -> np.ndarray:
+    """Plain scales [R, K/16] -> the tcgen05 atom layout (512-byte atom per 128 rows x 64 K;
+    row r's 4 scales at (r%32)*16 + ((r/32)%4)*4), atoms ordered [row block][K/64]."""
+    R, nb = sf.shape
+    rb = (R + 127) // 128
+    kc = nb // 4
+    out = np.zeros((rb, kc, 512), dtype=np.uint8)
+    r = np.arange(R)
+    for j in range(nb):
+        out[r // 128, j // 4, (r % 32) * 16 + ((r // 32) % 4) * 4 + (j % 4)] = sf[:, j]
+    return out.reshape(-1)
+
+
+def gemm_nvfp4(A, SFA, GA, B, SFB, GB, out_type: int = 0, rows=None):
+    """Oracle NVFP4 GEMM (plain-layout scales). bf16 bits for out_type 0, f32 for 1."""
+    A = np.ascontiguousarray(A, dtype=np.uint8)
+    B = np.ascontiguousarray(B, dtype=np.uint8)
+    SFA = np.ascontiguousarray(SFA, dtype=np.uint8)
+    SFB = np.ascontiguousarray(SFB, dtype=np.uint8)
+    M, K = A.shape[0], A.shape[1] * 2
+    N = B.shape[0]
+    r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int32)
+    nr = M if r is None else len(r)
+    C_ = np.empty((nr, N), dtype=np.uint16 if out_type == 0 else np.float32)
+    lib().qgo_gemm_nvfp4(_p(A), _p(SFA), float(GA), _p(B), _p(SFB), float(GB), M, N, K, _p(r), nr, out_type, _p(C_))
+    return C_
+
+
+def nvfp4_dequant(Q: np.ndarray, SF: np.ndarray, G: float) -> np.ndarray:
+    """float64 values q * sf * G of packed codes and plain scales (independent numpy decode)."""
+    grid = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+    lo = Q & 0xF
+    hi = Q >> 4
+    codes = np.stack([lo, hi], axis=-1).reshape(Q.shape[0], -1)
+    vals = grid[codes & 7] * np.where(codes & 8, -1.0, 1.0)
+    sf = e4m3_to_f32(SF).astype(np.float64)
+    return vals * np.repeat(sf, 16, axis=1) * float(G)
+
+
 def e4m3_to_f32(q: np.ndarray) -> np.ndarray:
     import torch
     return torch.from_numpy(np.ascontiguousarray(q, dtype=np.uint8)).view(torch.float8_e4m3fn).float().numpy()

@@ -61,6 +61,9 @@ _SIGNATURES = {
     "qg_gemm_i8": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, _V, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gemm_fp8_b128": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gen_fp8": (C.c_int, [_V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint32, _V]),
+    "qg_gemm_nvfp4": (C.c_int, [_V, _V, _V, _V, C.c_float, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
+    "qg_nvfp4_sf_bytes": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_uint64)]),
+    "qg_gen_nvfp4": (C.c_int, [_V, _V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint32, _V]),
     "qg_gemv_w4a16_workspace_bytes": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_uint64)]),
     "qg_gemv_w4a16": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V, C.c_uint64, _V]),
     "qg_gemv_w4a16_noalloc": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),

@@ -49,6 +49,24 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
             l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes);
             break;
         }
+        case QG_FMT_NVFP4: {
+            l.M = cfg.m > 0 ? cfg.m : 16384;
+            l.N = cfg.n > 0 ? cfg.n : 16384;
+            l.K = cfg.k > 0 ? cfg.k : 16384;
+            QG_CHECK_ARG(l.K % 256 == 0, "NVFP4: K=%d must be a multiple of 256", l.K);
+            QG_CHECK_ARG(l.out_type == QG_OUT_BF16 || l.out_type == QG_OUT_F32, "NVFP4: bad out_type %d", l.out_type);
+            l.n_ops = 5;                                                   // A, sfa, B, sfb, global scales
+            l.op_bytes[0] = (uint64_t)l.M * l.K / 2;
+            l.op_bytes[1] = nvfp4_sf_bytes(l.M, l.K);
+            l.op_bytes[2] = (uint64_t)l.N * l.K / 2;
+            l.op_bytes[3] = nvfp4_sf_bytes(l.N, l.K);
+            l.op_bytes[4] = 16;
+            l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
+            l.scratch_bytes = 16;
+            l.ops = 2.0 * l.M * (double)l.N * l.K;
+            l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes);
+            break;
+        }
         case QG_FMT_W4A16: {
             l.M = cfg.m > 0 ? cfg.m : 1;
             l.N = cfg.n > 0 ? cfg.n : 28672;
@@ -88,6 +106,17 @@ int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_inde
             return QG_OK;
         case QG_FMT_FP8:
             return gen_fp8(cp.op[0], cp.op[2], cp.op[1], cp.op[3], L.M, L.N, L.K, seed, base, s);
+        case QG_FMT_NVFP4: {
+            float* g = static_cast<float*>(cp.op[4]);
+            if ((rc = gen_nvfp4(cp.op[0], cp.op[1], cp.op[2], cp.op[3], g, cp.scratch, L.M, L.N, L.K, seed, base, s)))
+                return rc;
+            float h[2] = {1.0f, 1.0f};
+            QG_CUDA(cudaMemcpyAsync(h, g, sizeof(h), cudaMemcpyDeviceToHost, s));
+            QG_CUDA(cudaStreamSynchronize(s));
+            cp.global_a = h[0];
+            cp.global_b = h[1];
+            return QG_OK;
+        }
         case QG_FMT_W4A16:
             if (cp.scratch) QG_CUDA(cudaMemsetAsync(cp.scratch, 0, L.scratch_bytes, s));
             return gen_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], L.M, L.N, L.K, seed, base, s);
@@ -103,6 +132,9 @@ int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaS
             return gemm_i8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, cp.cksum, L.M, L.N, L.K, s);
         case QG_FMT_FP8:
             return gemm_fp8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, s);
+        case QG_FMT_NVFP4:
+            return gemm_nvfp4(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.global_a, cp.global_b, cp.out, L.out_type,
+                              L.M, L.N, L.K, s);
         case QG_FMT_W4A16:
             return gemv_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, cp.scratch,
                               L.scratch_bytes, s);

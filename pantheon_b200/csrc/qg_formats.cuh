@@ -47,6 +47,11 @@ int gen_normal(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, cudaStr
 int gen_fp8(void* A, void* SA, void* B, void* SB, int M, int N, int K, uint64_t seed, uint32_t tid0, cudaStream_t s);
 int gemm_fp8(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type, int M, int N, int K,
              cudaStream_t stream);
+uint64_t nvfp4_sf_bytes(int R, int K);
+int gen_nvfp4(void* A, void* SFA, void* B, void* SFB, float* gscales, void* work, int M, int N, int K, uint64_t seed,
+              uint32_t tid0, cudaStream_t s);
+int gemm_nvfp4(const void* A, const void* SFA, const void* B, const void* SFB, float ga, float gb, void* C,
+               int out_type, int M, int N, int K, cudaStream_t stream);
 int gen_w4a16(void* X, void* W, void* S, void* Z, int M, int N, int K, uint64_t seed, uint32_t tid0, cudaStream_t s);
 uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int sm_count);
 int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,

@@ -1,0 +1,334 @@
+// qg_gemm_nvfp4.cu -- NVFP4 GEMM on the sm_100a tensor cores:
+// tcgen05.mma kind::mxf4nvf4 with ue4m3 block scales per 16 elements along K.
+//
+//   C[m,n] = out( (GA * GB) * sum_k (qa[m,k] * sfa[m,k/16]) * (qb[n,k] * sfb[n,k/16]) )
+//
+// A, B: e2m1 codes packed two per byte along K (low nibble = even k), [M, K/2]
+// and [N, K/2]; sfa, sfb: ue4m3 bytes in the scale-factor atom layout the MMA
+// reads (one 512-byte atom per 128 rows x 64 K: row r's four scales at
+// (r%32)*16 + ((r/32)%4)*4 + 0..3; atoms ordered [row block][K/64]); GA, GB:
+// per-tensor fp32 scales applied in the epilogue.
+//
+// One persistent CTA per SM, 384 threads:
+//   warp 0      producer: per 256-element K block, TMA loads of the A (128 rows)
+//               and B (256 rows) code tiles (128-byte swizzle) and bulk copies
+//               of the matching scale atoms (2 KB + 4 KB), 4-stage ring.
+//   warp 1      TMEM allocator and MMA issuer: copies the stage's scales from
+//               shared memory into TMEM (tcgen05.cp 32x128b.warpx4, which
+//               broadcasts each atom to the four lane quarters) and issues 4 x
+//               tcgen05.mma M=128 N=256 K=64 into a 256-column accumulator.
+//               tcgen05.cp and tcgen05.mma from one thread execute in issue
+//               order, so one scale region serves every K block.
+//   warps 4-11  epilogue: TMEM lane quarter warp % 4, column half (warp-4)/4;
+//               scale by GA*GB, round, store.
+// All barrier waits are bounded (qg_ptx.cuh).
+#include "qg_common.cuh"
+
+#include <cuda_bf16.h>
+
+namespace qg {
+namespace f4 {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 256;                       // fp4 elements per K block = 128 bytes per row
+constexpr int BK_BYTES = BK / 2;
+constexpr int UMMA_K = 64;                    // elements per tcgen05.mma kind::mxf4nvf4
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK_BYTES;        // 16 KB
+constexpr int B_BYTES = BN * BK_BYTES;        // 32 KB
+constexpr int SFA_BYTES = (BM / 128) * (BK / 64) * 512;   // 2 KB
+constexpr int SFB_BYTES = (BN / 128) * (BK / 64) * 512;   // 4 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+constexpr int ACC_COLS = BN;
+constexpr int SFA_COL = ACC_COLS;             // 4 MMAs x 4 columns
+constexpr int SFB_COL = ACC_COLS + 16;        // 4 MMAs x (BN/128) x 4 columns
+constexpr int TMEM_COLS = 512;                // 256 accumulator + 48 scale columns, rounded up
+constexpr int THREADS = 384;
+constexpr int EPI_WARP0 = 4;
+constexpr int EPI_THREADS = 256;
+constexpr int GROUP_M = 16;
+
+struct Barriers {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t tmem_full;
+    uint64_t tmem_empty;
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+constexpr uint32_t SITE_PRODUCER = 0x00030001u;
+constexpr uint32_t SITE_MMA_FULL = 0x00030002u;
+constexpr uint32_t SITE_MMA_TMEM = 0x00030003u;
+constexpr uint32_t SITE_EPI = 0x00030004u;
+
+struct Params {
+    int M, N, K;
+    const uint8_t* sfa;
+    const uint8_t* sfb;
+    float gab;            // GA * GB
+    void* C;
+    DeviceStatus* status;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
+    const int group = GROUP_M * tiles_n;
+    const int g = t / group;
+    const int first_m = g * GROUP_M;
+    const int gm = min(tiles_m - first_m, GROUP_M);
+    const int r = t - g * group;
+    mt = first_m + r % gm;
+    nt = r / gm;
+}
+
+template <int OUT>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t* sA = smem;
+    uint8_t* sB = sA + STAGES * A_BYTES;
+    uint8_t* sSFA = sB + STAGES * B_BYTES;
+    uint8_t* sSFB = sSFA + STAGES * SFA_BYTES;
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tiles_m = (p.M + BM - 1) / BM;
+    const int tiles_n = (p.N + BN - 1) / BN;
+    const int tiles = tiles_m * tiles_n;
+    const int nk = p.K / BK;
+    const int kchunks = p.K / 64;                 // scale atoms per 128-row block
+    const int n_row_blocks = (p.N + 127) / 128;   // 128-row blocks of B's scales
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&bars->full[s], 1); mbar_init(&bars->empty[s], 1); }
+        mbar_init(&bars->tmem_full, 1);
+        mbar_init(&bars->tmem_empty, EPI_THREADS / 32);
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(&bars->tmem_base, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+    volatile int* abort_flag = &bars->abort;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------ producer
+        uint32_t stage = 0, phase = 0, armed = 0, armed_phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            int mt, nt;
+            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER)) { ok = false; break; }
+                mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
+                tma_load_2d(sA + stage * A_BYTES, &tmA, &bars->full[stage], kb * BK_BYTES, mt * BM);
+                tma_load_2d(sB + stage * B_BYTES, &tmB, &bars->full[stage], kb * BK_BYTES, nt * BN);
+                // scale atoms of this K block: 4 consecutive atoms per 128-row block
+                bulk_load(sSFA + stage * SFA_BYTES, p.sfa + ((size_t)mt * kchunks + kb * 4) * 512, SFA_BYTES / (BM / 128),
+                          &bars->full[stage]);
+                // (a 128-row block past the end of B exists only in a ragged last
+                // tile; its columns are never stored, so block 0 stands in for it)
+#pragma unroll
+                for (int h = 0; h < BN / 128; ++h) {
+                    const int blk = nt * (BN / 128) + h < n_row_blocks ? nt * (BN / 128) + h : 0;
+                    bulk_load(sSFB + stage * SFB_BYTES + h * (SFB_BYTES / (BN / 128)),
+                              p.sfb + ((size_t)blk * kchunks + kb * 4) * 512, SFB_BYTES / (BN / 128),
+                              &bars->full[stage]);
+                }
+                armed |= 1u << stage;
+                armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        if (!ok)
+            for (int s = 0; s < STAGES; ++s)
+                if (armed & (1u << s)) mbar_wait(&bars->full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------------ scale copies + MMA issuer
+        constexpr uint32_t IDESC = make_idesc_bs(/*e2m1*/ 1, /*e2m1*/ 1, /*ue4m3*/ 0, BM, BN);
+        uint32_t stage = 0, phase = 0;
+        bool ok = true, issued = false;
+        int iter = 0;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++iter) {
+            if (!mbar_wait(&bars->tmem_empty, (iter & 1) ^ 1u, abort_flag, p.status, SITE_MMA_TMEM)) { ok = false; break; }
+            tc_fence_after();
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_MMA_FULL)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sfa_addr = smem_u32(sSFA + stage * SFA_BYTES);
+                const uint32_t sfb_addr = smem_u32(sSFB + stage * SFB_BYTES);
+#pragma unroll
+                for (int k = 0; k < BK / UMMA_K; ++k) {
+                    utccp_32x128b_warpx4(tmem_base + SFA_COL + 4 * k, make_sdesc_sf(sfa_addr + k * 512));
+#pragma unroll
+                    for (int h = 0; h < BN / 128; ++h)
+                        utccp_32x128b_warpx4(tmem_base + SFB_COL + (BN / 128) * 4 * k + 4 * h,
+                                             make_sdesc_sf(sfb_addr + h * (SFB_BYTES / (BN / 128)) + k * 512));
+                }
+                const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+                const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                for (int k = 0; k < BK / UMMA_K; ++k)
+                    umma_nvf4(tmem_base, make_sdesc_kmajor_sw128(a_addr + k * (UMMA_K / 2)),
+                              make_sdesc_kmajor_sw128(b_addr + k * (UMMA_K / 2)), IDESC,
+                              tmem_base + SFA_COL + 4 * k, tmem_base + SFB_COL + (BN / 128) * 4 * k,
+                              (kb | k) != 0 ? 1u : 0u);
+                issued = true;
+                umma_commit(&bars->empty[stage]);
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (ok) umma_commit(&bars->tmem_full);
+        }
+        if (!ok && issued) {
+            umma_commit(&bars->drain);
+            mbar_wait(&bars->drain, 0, nullptr, nullptr, 0);
+        }
+    } else if (warp >= EPI_WARP0) {
+        // ------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;
+        const int half = (warp - EPI_WARP0) >> 2;
+        const int row = quarter * 32 + lane;
+        int iter = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
+            int mt, nt;
+            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&bars->tmem_full, iter & 1, abort_flag, p.status, SITE_EPI) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const int m = mt * BM + row;
+            const bool row_ok = m < p.M;
+            const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * (BN / 2);
+#pragma unroll 1
+            for (int c = 0; c < BN / 2; c += 32) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(t_row + c, r);
+                tmem_ld_wait_regs(r);
+                const int n0 = nt * BN + half * (BN / 2) + c;
+                if (!row_ok || n0 >= p.N) continue;
+                const bool full_chunk = (n0 + 32 <= p.N);
+                float f[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) f[i] = __fmul_rn(__uint_as_float(r[i]), p.gab);
+                if (OUT == QG_OUT_F32) {
+                    float* dst = static_cast<float*>(p.C) + (size_t)m * p.N + n0;
+                    if (full_chunk && (p.N % 4) == 0) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (n0 + i < p.N) dst[i] = f[i];
+                    }
+                } else {
+                    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
+                    if (full_chunk && (p.N % 8) == 0) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 8) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                __nv_bfloat162 h = __floats2bfloat162_rn(f[i + 2 * j], f[i + 2 * j + 1]);
+                                w[j] = *reinterpret_cast<uint32_t*>(&h);
+                            }
+                            *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (n0 + i < p.N) dst[i] = __float2bfloat16_rn(f[i]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->tmem_empty);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+template <int OUT>
+static int launch(const void* A, const void* SFA, const void* B, const void* SFB, float gab, void* C, int M, int N,
+                  int K, cudaStream_t stream) {
+    DeviceInfo* info = nullptr;
+    int rc = current_device_info(&info);
+    if (rc) return rc;
+    DeviceStatus* status = nullptr;
+    if ((rc = device_status_ptr(&status))) return rc;
+    CUtensorMap tmA, tmB;
+    if ((rc = make_tmap_2d(&tmA, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K / 2, (uint64_t)M, (uint64_t)K / 2,
+                           BK_BYTES, BM, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    if ((rc = make_tmap_2d(&tmB, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2,
+                           BK_BYTES, BN, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    QG_CUDA(cudaGetDevice(&dev));
+    if (!attr_set[dev & 63]) {
+        QG_CUDA(cudaFuncSetAttribute(gemm_nvfp4_kernel<QG_OUT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(gemm_nvfp4_kernel<QG_OUT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        attr_set[dev & 63] = true;
+    }
+    Params p{M, N, K, static_cast<const uint8_t*>(SFA), static_cast<const uint8_t*>(SFB), gab, C, status};
+    const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
+    const int grid = tiles < info->sm_count ? tiles : info->sm_count;
+    gemm_nvfp4_kernel<OUT><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, p);
+    QG_CUDA(cudaGetLastError());
+    return QG_OK;
+}
+
+} // namespace f4
+
+uint64_t nvfp4_sf_bytes(int R, int K) { return (uint64_t)((R + 127) / 128) * (uint64_t)(K / 64) * 512; }
+
+int gemm_nvfp4(const void* A, const void* SFA, const void* B, const void* SFB, float ga, float gb, void* C,
+               int out_type, int M, int N, int K, cudaStream_t stream) {
+    QG_CHECK_ARG(A && SFA && B && SFB && C, "qg_gemm_nvfp4: null operand");
+    QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemm_nvfp4: empty shape %dx%dx%d", M, N, K);
+    QG_CHECK_ARG(K % 256 == 0, "qg_gemm_nvfp4: K=%d must be a multiple of 256", K);
+    QG_CHECK_ARG(((uintptr_t)SFA & 15) == 0 && ((uintptr_t)SFB & 15) == 0, "qg_gemm_nvfp4: scale tensors must be 16-byte aligned");
+    const float gab = ga * gb;
+    switch (out_type) {
+        case QG_OUT_BF16: return f4::launch<QG_OUT_BF16>(A, SFA, B, SFB, gab, C, M, N, K, stream);
+        case QG_OUT_F32: return f4::launch<QG_OUT_F32>(A, SFA, B, SFB, gab, C, M, N, K, stream);
+        default: set_error("qg_gemm_nvfp4: bad out_type %d", out_type); return QG_ERR_ARG;
+    }
+}
+
+} // namespace qg
+
+extern "C" int qg_gemm_nvfp4(const void* A, const void* SFA, const void* B, const void* SFB, float ga, float gb,
+                             void* C, int out_type, int M, int N, int K, void* stream) {
+    return qg::gemm_nvfp4(A, SFA, B, SFB, ga, gb, C, out_type, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qg_nvfp4_sf_bytes(int rows, int K, uint64_t* bytes) {
+    QG_CHECK_ARG(bytes && rows > 0 && K > 0 && K % 64 == 0, "qg_nvfp4_sf_bytes: bad argument");
+    *bytes = qg::nvfp4_sf_bytes(rows, K);
+    return QG_OK;
+}

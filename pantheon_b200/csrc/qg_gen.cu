@@ -147,6 +147,85 @@ __global__ void gen_fp8_blocks_kernel(uint8_t* Q, float* S, int R, int K, uint64
     if (threadIdx.x == 0) S[blockIdx.x] = amax > 0.0f ? __fdiv_rn(amax, 448.0f) : 1.0f;
 }
 
+// NVFP4 operands: values N(0,1); per-tensor scale G = amax/(448*6);
+// per 16 along K an ue4m3 scale sf = e4m3(bmax/6/G); codes q = e2m1(x/(dec(sf)*G)).
+__global__ void absmax_normal_kernel(uint64_t n, uint64_t key, unsigned int* amax_bits) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    float a = 0.0f;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        a = fmaxf(a, fabsf(normal_from_hash(hash_at(key, i))));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(a));   // non-negative floats order as integers
+}
+
+__global__ void global_scale_kernel(const unsigned int* amax_bits, float* g) {
+    const float amax = __uint_as_float(*amax_bits);
+    *g = amax > 0.0f ? __fdiv_rn(amax, 448.0f * 6.0f) : 1.0f;
+}
+
+__device__ __forceinline__ float e4m3_decode(uint8_t v) {
+    const int e = (v >> 3) & 0xF, m = v & 7;
+    const float r = (e == 0) ? (float)m * 0.001953125f : ldexpf((float)(8 + m), e - 10);
+    return (v & 0x80) ? -r : r;
+}
+
+// e2m1 code of x (round to nearest, ties to the even code, saturating at 6).
+__device__ __forceinline__ uint32_t e2m1_code(float x) {
+    const uint32_t sign = (__float_as_uint(x) >> 28) & 0x8u;
+    const float a = fabsf(x);
+    uint32_t c;
+    if (a <= 0.25f) c = 0;
+    else if (a < 0.75f) c = 1;
+    else if (a <= 1.25f) c = 2;
+    else if (a < 1.75f) c = 3;
+    else if (a <= 2.5f) c = 4;
+    else if (a < 3.5f) c = 5;
+    else if (a <= 5.0f) c = 6;
+    else c = 7;
+    return sign | c;
+}
+
+// One thread per (row, 16-element block): codes (8 bytes) and the scale byte,
+// written straight into the tcgen05 scale-factor atom layout:
+//   atom (row block r/128, K chunk k/64) is 512 bytes at ((r/128) * (K/64) + k/64) * 512;
+//   inside it, row r's 4 scales of the chunk are bytes (r%32)*16 + ((r/32)%4)*4 + 0..3.
+__global__ void quant_nvfp4_kernel(uint8_t* Q, uint8_t* SF, int R, int K, uint64_t key, const float* gscale) {
+    const int nb = K / 16;
+    const uint64_t total = (uint64_t)R * nb;
+    const float G = *gscale;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; b < total; b += stride) {
+        const int r = (int)(b / nb), kb = (int)(b - (uint64_t)r * nb);
+        const uint64_t base = (uint64_t)r * K + (uint64_t)kb * 16;
+        float x[16];
+        float bmax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            x[i] = normal_from_hash(hash_at(key, base + i));
+            bmax = fmaxf(bmax, fabsf(x[i]));
+        }
+        float t = __fdiv_rn(bmax, 6.0f);
+        t = __fdiv_rn(t, G);
+        const uint8_t sf = (uint8_t)(__nv_cvt_float_to_fp8(t, __NV_SATFINITE, __NV_E4M3) & 0x7F);
+        const float d = __fmul_rn(e4m3_decode(sf), G);
+        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t c = d > 0.0f ? e2m1_code(__fdiv_rn(x[i], d)) : 0u;
+            w0 |= c << (4 * i);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t c = d > 0.0f ? e2m1_code(__fdiv_rn(x[8 + i], d)) : 0u;
+            w1 |= c << (4 * i);
+        }
+        *reinterpret_cast<uint2*>(Q + base / 2) = make_uint2(w0, w1);
+        const size_t atom = (size_t)(r / 128) * (K / 64) + kb / 4;
+        SF[atom * 512 + (r % 32) * 16 + ((r / 32) % 4) * 4 + (kb % 4)] = sf;
+    }
+}
+
 static int grid_for(uint64_t work) {
     DeviceInfo* info = nullptr;
     int blocks = 148 * 8;
@@ -212,7 +291,42 @@ int gen_fp8(void* A, void* SA, void* B, void* SB, int M, int N, int K, uint64_t 
     return QG_OK;
 }
 
+// NVFP4 operand set: A codes/scales from tensor tid0, B from tid0 + 2.  The two
+// per-tensor scales are written to gscales[0..1] (device) and also returned
+// through `host_gscales` when non-null (synchronizes `s`).  `work` is 8 bytes
+// of device scratch for the absmax reductions.
+int gen_nvfp4(void* A, void* SFA, void* B, void* SFB, float* gscales, void* work, int M, int N, int K, uint64_t seed,
+              uint32_t tid0, cudaStream_t s) {
+    QG_CHECK_ARG(A && SFA && B && SFB && gscales && work, "qg_gen_nvfp4: null output");
+    QG_CHECK_ARG(M > 0 && N > 0 && K > 0 && K % 256 == 0, "qg_gen_nvfp4: bad shape %dx%dx%d (K %% 256 == 0)", M, N, K);
+    unsigned int* amax = static_cast<unsigned int*>(work);
+    QG_CUDA(cudaMemsetAsync(amax, 0, 8, s));
+    const uint64_t keyA = gen::stream_key(seed, tid0), keyB = gen::stream_key(seed, tid0 + 2);
+    const uint64_t na = (uint64_t)M * K, nbv = (uint64_t)N * K;
+    gen::absmax_normal_kernel<<<gen::grid_for(na), 256, 0, s>>>(na, keyA, amax);
+    gen::absmax_normal_kernel<<<gen::grid_for(nbv), 256, 0, s>>>(nbv, keyB, amax + 1);
+    gen::global_scale_kernel<<<1, 1, 0, s>>>(amax, gscales);
+    gen::global_scale_kernel<<<1, 1, 0, s>>>(amax + 1, gscales + 1);
+    // scale atoms of rows past M / N (the last partial 128-row block) stay zero
+    const size_t sfa_bytes = (size_t)((M + 127) / 128) * (K / 64) * 512;
+    const size_t sfb_bytes = (size_t)((N + 127) / 128) * (K / 64) * 512;
+    QG_CUDA(cudaMemsetAsync(SFA, 0, sfa_bytes, s));
+    QG_CUDA(cudaMemsetAsync(SFB, 0, sfb_bytes, s));
+    gen::quant_nvfp4_kernel<<<gen::grid_for((uint64_t)M * (K / 16)), 256, 0, s>>>(
+        static_cast<uint8_t*>(A), static_cast<uint8_t*>(SFA), M, K, keyA, gscales);
+    gen::quant_nvfp4_kernel<<<gen::grid_for((uint64_t)N * (K / 16)), 256, 0, s>>>(
+        static_cast<uint8_t*>(B), static_cast<uint8_t*>(SFB), N, K, keyB, gscales + 1);
+    QG_CUDA(cudaGetLastError());
+    return QG_OK;
+}
+
 } // namespace qg
+
+extern "C" int qg_gen_nvfp4(void* A, void* SFA, void* B, void* SFB, void* gscales, void* work, int M, int N, int K,
+                            uint64_t seed, uint32_t tid0, void* stream) {
+    return qg::gen_nvfp4(A, SFA, B, SFB, static_cast<float*>(gscales), work, M, N, K, seed, tid0,
+                         static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int qg_gen_fp8(void* A, void* SA, void* B, void* SB, int M, int N, int K, uint64_t seed, uint32_t tid0,
                           void* stream) {

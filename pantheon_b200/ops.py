@@ -93,6 +93,42 @@ def gen_fp8(M: int, N: int, K: int, seed: int, tid0: int = 0, device="cuda"):
     return A, B, sa, sb
 
 
+def nvfp4_sf_bytes(rows: int, K: int) -> int:
+    b = C.c_uint64()
+    check("qg_nvfp4_sf_bytes", load_library().qg_nvfp4_sf_bytes(rows, K, C.byref(b)))
+    return b.value
+
+
+def gemm_nvfp4(A: torch.Tensor, sfa: torch.Tensor, B: torch.Tensor, sfb: torch.Tensor, ga: float, gb: float,
+               out_type: int = QG_OUT_BF16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = ga*gb * (A .* sfa) @ (B .* sfb)^T on the tcgen05 NVFP4 path.
+
+    A [M, K/2], B [N, K/2] uint8 (two e2m1 codes per byte, low nibble = even k);
+    sfa, sfb uint8 ue4m3 scales in the atom layout (see include/pantheon_qgemm.h).
+    """
+    _require_cuda(A, sfa, B, sfb)
+    M, K2 = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=_OUT_DTYPES[out_type], device=A.device)
+    check("qg_gemm_nvfp4", load_library().qg_gemm_nvfp4(_ptr(A), _ptr(sfa), _ptr(B), _ptr(sfb), ga, gb, _ptr(out),
+                                                         out_type, M, N, 2 * K2, _stream(A.device)))
+    return out
+
+
+def gen_nvfp4(M: int, N: int, K: int, seed: int, tid0: int = 0, device="cuda"):
+    """The NVFP4 workload's generated operands: (A, sfa, B, sfb, gscales[2]) on the device."""
+    A = torch.empty((M, K // 2), dtype=torch.uint8, device=device)
+    B = torch.empty((N, K // 2), dtype=torch.uint8, device=device)
+    sfa = torch.empty((nvfp4_sf_bytes(M, K),), dtype=torch.uint8, device=device)
+    sfb = torch.empty((nvfp4_sf_bytes(N, K),), dtype=torch.uint8, device=device)
+    g = torch.empty((2,), dtype=torch.float32, device=device)
+    work = torch.empty((2,), dtype=torch.int32, device=device)
+    check("qg_gen_nvfp4", load_library().qg_gen_nvfp4(_ptr(A), _ptr(sfa), _ptr(B), _ptr(sfb), _ptr(g), _ptr(work),
+                                                       M, N, K, seed, tid0, _stream(A.device)))
+    return A, sfa, B, sfb, g
+
+
 def gemv_w4a16_workspace_bytes(M: int, N: int, K: int) -> int:
     b = C.c_uint64()
     check("qg_gemv_w4a16_workspace_bytes", load_library().qg_gemv_w4a16_workspace_bytes(M, N, K, C.byref(b)))
