@@ -154,17 +154,27 @@ class ClockSampler:
                 "reasons": reasons, "power_w_max": max(power) if power else None, "samples": len(rows)}
 
 
-def cpu_baseline(target_s: float = 10.0):
-    """The oracle's INT8 GEMM on a bounded sample of rows of the 8192^3 GEMM (all host threads)."""
+def _oracle_row_rate(O, A, B, sa, sb, nrows=64):
+    """Seconds per output row of the 8192^3 INT8 GEMM for the oracle on all host threads."""
     import numpy as np
-    from oracle import qg_oracle as O
-    # rows 0..255 of A (the first rows of the full A's stream), the full B
-    A, B, sa, sb = O.int8_operands(256, N, K, seed=1)
-    rows = np.arange(1, dtype=np.int32)
+    rows = np.arange(nrows, dtype=np.int32)
+    O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows[:8])
     t0 = time.perf_counter()
     O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
-    t1 = time.perf_counter() - t0
-    nrows = int(max(1, min(256, target_s / max(t1, 1e-6))))
+    return (time.perf_counter() - t0) / nrows
+
+
+def cpu_baseline(target_s: float = 15.0):
+    """The oracle's INT8 GEMM on a bounded sample of rows of the 8192^3 GEMM (all host threads).
+
+    The sample is as many leading output rows as fit in about `target_s` seconds
+    (the whole GEMM on a host fast enough), calibrated on 64 rows first.
+    """
+    import numpy as np
+    from oracle import qg_oracle as O
+    A, B, sa, sb = O.int8_operands(M, N, K, seed=1)
+    per_row = _oracle_row_rate(O, A, B, sa, sb)
+    nrows = int(max(64, min(M, target_s / max(per_row, 1e-9))))
     rows = np.arange(nrows, dtype=np.int32)
     t0 = time.perf_counter()
     O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
@@ -197,10 +207,13 @@ def run_reference(args, rank: int):
     warm = max(0, args.warmup)
     import numpy as np
     from oracle import qg_oracle as O
-    A, B, sa, sb = O.int8_operands(64, N, K, seed=1)
-    rows = np.arange(4, dtype=np.int32)   # bounded sample per step: 4 rows of the GEMM
-    for _ in range(min(warm, 1)):
-        O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows[:1])
+    A, B, sa, sb = O.int8_operands(M, N, K, seed=1)
+    # bounded sample per step: the leading rows that keep the whole run near a minute
+    per_row = _oracle_row_rate(O, A, B, sa, sb)
+    nrows = int(max(1, min(M, 60.0 / (steps + warm) / max(per_row, 1e-9))))
+    rows = np.arange(nrows, dtype=np.int32)
+    for _ in range(warm):
+        O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
     t0 = time.perf_counter()
     for s in range(steps):
         O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
@@ -210,7 +223,8 @@ def run_reference(args, rank: int):
         "impl": "reference", "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": args.gpus,
         "steps": steps, "warmup": warm, "ms_per_step": dt / steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "configs[1] INT8 W8A8 GEMM 8192x8192x8192, bf16 out (CPU: 4 rows per step)"},
+        "config": {"workload": "configs[1] INT8 W8A8 GEMM 8192x8192x8192, bf16 out, fp32 row/col scales",
+                   "M": M, "N": N, "K": K, "seed": 1, "cpu_rows_per_step": nrows},
         "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": O.threads(), "kind": "port",
                          "sample": f"{len(rows)} of 8192 output rows per step, {steps} steps"},
         "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -251,12 +251,20 @@ void qgo_gemm_i8(const int8_t* A, const int8_t* B, const float* sa, const float*
                  int M, int N, int K, const int32_t* rows, int nrows,
                  int out_type, void* C, int32_t* acc, uint32_t* row_cksum) {
     if (!rows) nrows = M;
+    /* work items are (row, 256-column tile) so that a sample of a few rows
+     * still spreads over every host thread; the row checksum is a wrapping
+     * u32 sum, so adding the tiles' parts in any order gives the same bits */
+    const int TN = 256;
+    int ntn = (N + TN - 1) / TN;
+    if (row_cksum) for (int r = 0; r < nrows; ++r) row_cksum[r] = 0;
     #pragma omp parallel for schedule(dynamic, 1)
-    for (int r = 0; r < nrows; ++r) {
+    for (long it = 0; it < (long)nrows * ntn; ++it) {
+        int r = (int)(it / ntn);
+        int n0 = (int)(it % ntn) * TN, n1 = n0 + TN < N ? n0 + TN : N;
         int m = rows ? rows[r] : r;
         const int8_t* a = A + (size_t)m * K;
         uint32_t ck = 0;
-        for (int n = 0; n < N; ++n) {
+        for (int n = n0; n < n1; ++n) {
             const int8_t* b = B + (size_t)n * K;
             int32_t s = 0;
             for (int k = 0; k < K; ++k) s += (int32_t)a[k] * (int32_t)b[k];
@@ -272,7 +280,10 @@ void qgo_gemm_i8(const int8_t* A, const int8_t* B, const float* sa, const float*
                 else ((uint16_t*)C)[o] = qgo_f32_to_bf16(f);
             }
         }
-        if (row_cksum) row_cksum[r] = ck;
+        if (row_cksum) {
+            #pragma omp atomic
+            row_cksum[r] += ck;
+        }
     }
 }
 

@@ -9,16 +9,25 @@
 // (r%32)*16 + ((r/32)%4)*4 + 0..3; atoms ordered [row block][K/64]); GA, GB:
 // per-tensor fp32 scales applied in the epilogue.
 //
-// One persistent CTA per SM, 384 threads:
+// One persistent CTA per SM, 448 threads:
 //   warp 0      producer: per 256-element K block, TMA loads of the A (128 rows)
 //               and B (256 rows) code tiles (128-byte swizzle) and bulk copies
 //               of the matching scale atoms (2 KB + 4 KB), 4-stage ring.
-//   warp 1      TMEM allocator and MMA issuer: copies the stage's scales from
-//               shared memory into TMEM (tcgen05.cp 32x128b.warpx4, which
-//               broadcasts each atom to the four lane quarters) and issues 4 x
-//               tcgen05.mma M=128 N=256 K=64 into a 256-column accumulator.
-//               tcgen05.cp and tcgen05.mma from one thread execute in issue
-//               order, so one scale region serves every K block.
+//   warps 2, 3, 12, 13   scale writers, one per TMEM lane quarter: each lane
+//               reads its 16 bytes of every atom of the stage from shared
+//               memory and writes them to TMEM with tcgen05.st, giving the
+//               layout tcgen05.cp 32x128b.warpx4 would (each atom broadcast to
+//               the four lane quarters, 4 columns per MMA).  tcgen05.cp runs
+//               in the tensor pipe in order with the MMAs (12 copies per K
+//               block cost ~40 % of the MMA time when measured); tcgen05.st
+//               does not occupy that pipe.
+//   warp 1      TMEM allocator and MMA issuer: 4 x tcgen05.mma M=128 N=256
+//               K=64 per K block into a 256-column accumulator, once the
+//               stage's operands have landed and its scales are in TMEM.
+//               Each ring stage has its own 48-column scale region in TMEM,
+//               free again exactly when the stage's shared memory is (the
+//               producer refills a stage only after the commit of the MMAs
+//               that read it, and the writers wait for that refill).
 //   warps 4-11  epilogue: TMEM lane quarter warp % 4, column half (warp-4)/4;
 //               scale by GA*GB, round, store.
 // All barrier waits are bounded (qg_ptx.cuh).
@@ -41,17 +50,22 @@ constexpr int SFA_BYTES = (BM / 128) * (BK / 64) * 512;   // 2 KB
 constexpr int SFB_BYTES = (BN / 128) * (BK / 64) * 512;   // 4 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
 constexpr int ACC_COLS = BN;
-constexpr int SFA_COL = ACC_COLS;             // 4 MMAs x 4 columns
-constexpr int SFB_COL = ACC_COLS + 16;        // 4 MMAs x (BN/128) x 4 columns
-constexpr int TMEM_COLS = 512;                // 256 accumulator + 48 scale columns, rounded up
-constexpr int THREADS = 384;
+constexpr int SFA_COLS = (BK / UMMA_K) * 4;                  // 16: 4 MMAs x 4 columns
+constexpr int SFB_COLS = (BK / UMMA_K) * (BN / 128) * 4;     // 32
+constexpr int SF_STAGE_COLS = SFA_COLS + SFB_COLS;           // 48 per ring stage
+constexpr int TMEM_COLS = 512;                // 256 accumulator + 4 x 48 scale columns, rounded up
+static_assert(ACC_COLS + STAGES * SF_STAGE_COLS <= TMEM_COLS, "TMEM budget");
+constexpr int THREADS = 448;
 constexpr int EPI_WARP0 = 4;
+constexpr int EPI_WARP_END = 12;
+constexpr int SF_WRITERS = 4;                 // warps 2, 3, 12, 13: lane quarters 2, 3, 0, 1
 constexpr int EPI_THREADS = 256;
 constexpr int GROUP_M = 16;
 
 struct Barriers {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
+    uint64_t sf_ready[STAGES];
     uint64_t tmem_full;
     uint64_t tmem_empty;
     uint64_t drain;
@@ -65,6 +79,8 @@ constexpr uint32_t SITE_PRODUCER = 0x00030001u;
 constexpr uint32_t SITE_MMA_FULL = 0x00030002u;
 constexpr uint32_t SITE_MMA_TMEM = 0x00030003u;
 constexpr uint32_t SITE_EPI = 0x00030004u;
+constexpr uint32_t SITE_SF = 0x00030005u;
+constexpr uint32_t SITE_MMA_SF = 0x00030006u;
 
 struct Params {
     int M, N, K;
@@ -107,7 +123,11 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
     const int n_row_blocks = (p.N + 127) / 128;   // 128-row blocks of B's scales
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) { mbar_init(&bars->full[s], 1); mbar_init(&bars->empty[s], 1); }
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+            mbar_init(&bars->sf_ready[s], SF_WRITERS);
+        }
         mbar_init(&bars->tmem_full, 1);
         mbar_init(&bars->tmem_empty, EPI_THREADS / 32);
         mbar_init(&bars->drain, 1);
@@ -169,24 +189,17 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             tc_fence_after();
             for (int kb = 0; kb < nk; ++kb) {
                 if (!mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_MMA_FULL)) { ok = false; break; }
+                if (!mbar_wait(&bars->sf_ready[stage], phase, abort_flag, p.status, SITE_MMA_SF)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t sfa_addr = smem_u32(sSFA + stage * SFA_BYTES);
-                const uint32_t sfb_addr = smem_u32(sSFB + stage * SFB_BYTES);
-#pragma unroll
-                for (int k = 0; k < BK / UMMA_K; ++k) {
-                    utccp_32x128b_warpx4(tmem_base + SFA_COL + 4 * k, make_sdesc_sf(sfa_addr + k * 512));
-#pragma unroll
-                    for (int h = 0; h < BN / 128; ++h)
-                        utccp_32x128b_warpx4(tmem_base + SFB_COL + (BN / 128) * 4 * k + 4 * h,
-                                             make_sdesc_sf(sfb_addr + h * (SFB_BYTES / (BN / 128)) + k * 512));
-                }
+                const uint32_t sfa_col = tmem_base + ACC_COLS + stage * SF_STAGE_COLS;
+                const uint32_t sfb_col = sfa_col + SFA_COLS;
                 const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
                 const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
                 for (int k = 0; k < BK / UMMA_K; ++k)
                     umma_nvf4(tmem_base, make_sdesc_kmajor_sw128(a_addr + k * (UMMA_K / 2)),
                               make_sdesc_kmajor_sw128(b_addr + k * (UMMA_K / 2)), IDESC,
-                              tmem_base + SFA_COL + 4 * k, tmem_base + SFB_COL + (BN / 128) * 4 * k,
+                              sfa_col + 4 * k, sfb_col + (BN / 128) * 4 * k,
                               (kb | k) != 0 ? 1u : 0u);
                 issued = true;
                 umma_commit(&bars->empty[stage]);
@@ -197,6 +210,47 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         if (!ok && issued) {
             umma_commit(&bars->drain);
             mbar_wait(&bars->drain, 0, nullptr, nullptr, 0);
+        }
+    } else if (warp == 2 || warp == 3 || warp >= EPI_WARP_END) {
+        // ------------------------------------------------------------ scale writers
+        const int quarter = warp & 3;
+        const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16) + ACC_COLS;
+        uint32_t stage = 0, phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            for (int kb = 0; kb < nk; ++kb) {
+                int got = 1;
+                if (lane == 0) got = mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_SF) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
+                // lane i takes bytes [16 i, 16 i + 16) of each atom: TMEM columns
+                // 4k..4k+3 (A) and 16 + 8k + 4h .. +3 (B) of this stage's region
+                const uint4* sfa = reinterpret_cast<const uint4*>(sSFA + stage * SFA_BYTES) + lane;
+                const uint4* sfb = reinterpret_cast<const uint4*>(sSFB + stage * SFB_BYTES) + lane;
+                uint32_t va[16], vb0[16], vb1[16];
+#pragma unroll
+                for (int k = 0; k < BK / UMMA_K; ++k) {
+                    const uint4 a = sfa[k * 32];
+                    va[4 * k] = a.x; va[4 * k + 1] = a.y; va[4 * k + 2] = a.z; va[4 * k + 3] = a.w;
+                }
+#pragma unroll
+                for (int k = 0; k < BK / UMMA_K; ++k) {
+#pragma unroll
+                    for (int h = 0; h < BN / 128; ++h) {
+                        const uint4 b = sfb[h * (SFB_BYTES / (BN / 128) / 16) + k * 32];
+                        uint32_t* d = (2 * k + h) < 4 ? &vb0[4 * (2 * k + h)] : &vb1[4 * (2 * k + h - 4)];
+                        d[0] = b.x; d[1] = b.y; d[2] = b.z; d[3] = b.w;
+                    }
+                }
+                const uint32_t col = t_lane + stage * SF_STAGE_COLS;
+                tmem_st_32x32b_x16(col, va);
+                tmem_st_32x32b_x16(col + SFA_COLS, vb0);
+                tmem_st_32x32b_x16(col + SFA_COLS + 16, vb1);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->sf_ready[stage]);
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
         }
     } else if (warp >= EPI_WARP0) {
         // ------------------------------------------------------------ epilogue
