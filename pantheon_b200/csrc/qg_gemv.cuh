@@ -1,0 +1,23 @@
+// qg_gemv.cuh -- what the two W4A16 GEMV kernels share: the SM count their
+// work split is sized for, and the tensor-core kernel's entry (used by the
+// C entry points in qg_gemv_w4a16.cu for 3..16 activation rows).
+#pragma once
+
+#include "qg_common.cuh"
+
+namespace qg {
+
+// The split of the work depends only on the shape (sized for the 148 SMs of a
+// B200), so workspace sizes are functions of (M, N, K) alone.
+constexpr int kGemvSms = 148;
+
+// fp32 partial-sum bytes and ticket count of the tensor-core GEMV for N x K.
+uint64_t gemv_w4a16_tc_partial_bytes(int N, int K);
+uint64_t gemv_w4a16_tc_ticket_count(int N);
+
+// One launch for `mrows` (1..16) activation rows; `partials` and `tickets`
+// come from the caller's workspace, tickets zero on entry (and on return).
+int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
+                  int K, float* partials, unsigned int* tickets, cudaStream_t stream);
+
+} // namespace qg

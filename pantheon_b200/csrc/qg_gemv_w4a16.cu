@@ -1,5 +1,7 @@
-// qg_gemv_w4a16.cu -- weight-only W4A16 group-128 decode GEMV / skinny GEMM
-// on the CUDA cores (no tensor cores), bandwidth-bound at M = 1.
+// qg_gemv_w4a16.cu -- weight-only W4A16 group-128 decode GEMV: the C entry
+// points, and the CUDA-core kernel for 1-2 activation rows (bandwidth-bound at
+// M = 1).  3-16 rows run on the tensor cores (qg_gemv_w4a16_tc.cu); larger M
+// is processed 16 rows at a time.
 //
 //   Y[m, n] = sum_k X[m, k] * (q[k, n] - Z[k/128, n]) * S[k/128, n],  q = u - 8
 //
@@ -13,19 +15,12 @@
 // batch is unpacked.  Per group of 128 the group's dot product is folded with
 // its scale and zero point:  sum_k x (u - 8 - z) s = s * (sum_k x u - (8 + z) sum_k x).
 //
-// The inner product sum_k x u, two ways:
-//   M <= 2   integer: the word's nibbles become bytes with one shift and two
-//            masks (u0 u2 u4 u6 | u1 u3 u5 u7), the activations of each
-//            (row, group) are staged as int16 fixed point with a shared power-
-//            of-two scale (the group's absmax maps below 2^14), and dp2a
-//            forms two 16x8-bit products per instruction into an exact int32
-//            group accumulator.  The only rounding is the activation's, at
-//            most 2^-15 of the group absmax per element.
-//   M >= 4   floating point: masking nibble j in place (w & (15 << s)) leaves
-//            the fp32 denormal u * 2^(s - 149), exact; with activations staged
-//            as x * 2^(109 - s) each product is u * x * 2^-40 exactly, and one
-//            unpacked weight pair serves every row through packed
-//            fma.rn.f32x2 into fp32 accumulators.
+// The inner product sum_k x u is integer: the word's nibbles become bytes with
+// one shift and two masks (u0 u2 u4 u6 | u1 u3 u5 u7), the activations of each
+// (row, group) are staged as int16 fixed point with a shared power-of-two scale
+// (the group's absmax maps below 2^14), and dp2a forms two 16x8-bit products
+// per instruction into an exact int32 group accumulator.  The only rounding is
+// the activation's, at most 2^-15 of the group absmax per element.
 // The sum of the activations of each group is exact fp32 from bf16.
 //
 // Work split: the K/8 packed rows of a column block are cut into `splits`
@@ -40,6 +35,7 @@
 // llm_decode.cpp:28-46, a KV gather + FMA chain with no weights) is the decode
 // workload; this kernel is the weight-only quantized projection it is named for.
 #include "qg_common.cuh"
+#include "qg_gemv.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -52,20 +48,15 @@ namespace w4 {
 constexpr int THREADS = 128;
 constexpr int GROUP = 128;
 constexpr int CHUNKS_PER_GROUP = GROUP / 8;
-constexpr int MAX_M = 16;
-// The split depends only on the shape (sized for the 148 SMs of a B200), so the
-// workspace size is a function of (M, N, K) alone.
-constexpr int kSplitSms = 148;
-// Floating path: products are accumulated as u * x * 2^-40; 2^40 undoes it.
-constexpr float kUnscale = 1099511627776.0f;
+constexpr int MAX_M = 16;    // rows per launch (either kernel)
+constexpr int kSplitSms = kGemvSms;
+constexpr int CPT = 4;       // columns per thread: one 128-bit load = 4 columns x 8 k
 
-// Per row-count template: integer or floating inner product, columns per
-// thread, resident CTAs per SM (register budget), loads per pipeline half.
-__host__ __device__ constexpr bool int_path(int mt) { return mt <= 2; }
-__host__ __device__ constexpr int cols_per_thread(int mt) { return mt >= 8 ? 2 : 4; }
-__host__ __device__ constexpr int blocks_per_sm(int mt) { return mt == 1 ? 7 : mt == 2 ? 5 : mt <= 8 ? 3 : 2; }
-__host__ __device__ constexpr int load_depth(int mt) { return mt <= 2 ? 4 : 2; }
-__host__ __device__ constexpr int cols_per_cta(int mt) { return THREADS * cols_per_thread(mt); }
+// Per row-count template (1 or 2): resident CTAs per SM (register budget) and
+// loads per pipeline half.
+__host__ __device__ constexpr int blocks_per_sm(int mt) { return mt == 1 ? 7 : 5; }
+__host__ __device__ constexpr int load_depth(int) { return 4; }
+__host__ __device__ constexpr int cols_per_cta(int) { return THREADS * CPT; }
 
 struct Params {
     const __nv_bfloat16* X;
@@ -80,67 +71,23 @@ struct Params {
     int out_type;
 };
 
-__device__ __forceinline__ void ffma2(float& a0, float& a1, float p0, float p1, float x0, float x1) {
-    asm("{\n\t.reg .b64 a, p, x;\n\t"
-        "mov.b64 a, {%0, %1};\n\t"
-        "mov.b64 p, {%2, %3};\n\t"
-        "mov.b64 x, {%4, %5};\n\t"
-        "fma.rn.f32x2 a, p, x, a;\n\t"
-        "mov.b64 {%0, %1}, a;\n\t}"
-        : "+f"(a0), "+f"(a1)
-        : "f"(p0), "f"(p1), "f"(x0), "f"(x1));
-}
-
-template <int CPT>
-struct WVec;
-template <>
-struct WVec<4> { using T = uint4; };
-template <>
-struct WVec<2> { using T = uint2; };
-
 __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
     uint4 v;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
-__device__ __forceinline__ uint2 ld_stream(const uint2* p) {
-    uint2 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
-}
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int c) { return c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w; }
-__device__ __forceinline__ uint32_t word_of(const uint2& v, int c) { return c == 0 ? v.x : v.y; }
-
-// Floating path: the eight weights of one packed word as exact fp32 denormals u_k * 2^(s_k - 149).
-__device__ __forceinline__ void unpack_denormal(uint32_t w, float (&v)[8]) {
-    const uint32_t h = w >> 12;
-    v[0] = __uint_as_float(w & 0x0000000Fu);   // s = 0
-    v[1] = __uint_as_float(w & 0x000000F0u);   // s = 4
-    v[2] = __uint_as_float(w & 0x00000F00u);   // s = 8
-    v[3] = __uint_as_float(w & 0x0000F000u);   // s = 12
-    v[4] = __uint_as_float(w & 0x000F0000u);   // s = 16
-    v[5] = __uint_as_float(h & 0x00000F00u);   // nibble 5 -> s = 8
-    v[6] = __uint_as_float(h & 0x0000F000u);   // nibble 6 -> s = 12
-    v[7] = __uint_as_float(h & 0x000F0000u);   // nibble 7 -> s = 16
-}
-
-// Floating path: 2^(109 - s_k) for the nibble positions above.
-__device__ __forceinline__ float prescale(int k) {
-    const int s = k < 5 ? 4 * k : 4 * (k - 3);
-    return __uint_as_float((uint32_t)(127 + 109 - s) << 23);
-}
 
 __device__ __forceinline__ float pow2(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 
 template <int MT>
 __global__ void __launch_bounds__(THREADS, blocks_per_sm(MT))
 gemv_w4a16_kernel(Params p) {
-    constexpr bool INT = int_path(MT);
-    constexpr int CPT = cols_per_thread(MT);
+    static_assert(MT == 1 || MT == 2, "the CUDA-core kernel serves 1-2 rows");
     constexpr int DEPTH = load_depth(MT);
     constexpr int CPC = cols_per_cta(MT);
-    using VT = typename WVec<CPT>::T;
+    using VT = uint4;
 
     const int nchunks = p.K / 8;
     const int c0 = (int)(((long long)blockIdx.y * nchunks) / p.splits);
@@ -152,10 +99,9 @@ gemv_w4a16_kernel(Params p) {
 
     // Shared memory for this CTA's k range (g = group index within the range):
     //   gsum  fp32  [groups][MT]     sum of the activations of the group segment
-    //   gpow  fp32  [groups][MT]     integer path: 2^e of the segment's fixed point
+    //   gpow  fp32  [groups][MT]     2^e of the segment's fixed point
     //   sz    half2 [groups][CPC]    (scale, zero) of each column
-    //   xdat  integer path: int32 [len][MT][4]  int16 pairs (x0,x2) (x4,x6) (x1,x3) (x5,x7)
-    //         floating path: fp32 [len][MT][8]  x * 2^(109 - s_k)
+    //   xdat  int32 [len][MT][4]     int16 pairs (x0,x2) (x4,x6) (x1,x3) (x5,x7)
     extern __shared__ __align__(16) uint8_t smem[];
     const int gmax = (len + CHUNKS_PER_GROUP - 1) / CHUNKS_PER_GROUP + 1;
     float* gsum = reinterpret_cast<float*>(smem);
@@ -166,7 +112,6 @@ gemv_w4a16_kernel(Params p) {
     uint8_t* xdat = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sz + (size_t)gmax * CPC) + 15) &
                                                ~static_cast<uintptr_t>(15));
     int4* xi = reinterpret_cast<int4*>(xdat);
-    float* xq = reinterpret_cast<float*>(xdat);
 
     // The first two batches of weights are requested before anything else, so
     // they stream in while the prologue below stages activations and scales.
@@ -253,20 +198,12 @@ gemv_w4a16_kernel(Params p) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = 0.0f;
         }
-        if (INT) {
-            const float sc = gpow[((c0 + ch) / CHUNKS_PER_GROUP - g_first) * MT + m];
-            int q[8];
+        const float sc = gpow[((c0 + ch) / CHUNKS_PER_GROUP - g_first) * MT + m];
+        int q[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) q[i] = __float2int_rn(v[i] * sc);
-            auto pk = [](int lo, int hi) { return (int)(((uint32_t)lo & 0xFFFFu) | ((uint32_t)hi << 16)); };
-            xi[(size_t)ch * MT + m] = make_int4(pk(q[0], q[2]), pk(q[4], q[6]), pk(q[1], q[3]), pk(q[5], q[7]));
-        } else {
-            float* dst = xq + ((size_t)ch * MT + m) * 8;
-            *reinterpret_cast<float4*>(dst) =
-                make_float4(v[0] * prescale(0), v[1] * prescale(1), v[2] * prescale(2), v[3] * prescale(3));
-            *reinterpret_cast<float4*>(dst + 4) =
-                make_float4(v[4] * prescale(4), v[5] * prescale(5), v[6] * prescale(6), v[7] * prescale(7));
-        }
+        for (int i = 0; i < 8; ++i) q[i] = __float2int_rn(v[i] * sc);
+        auto pk = [](int lo, int hi) { return (int)(((uint32_t)lo & 0xFFFFu) | ((uint32_t)hi << 16)); };
+        xi[(size_t)ch * MT + m] = make_int4(pk(q[0], q[2]), pk(q[4], q[6]), pk(q[1], q[3]), pk(q[5], q[7]));
     }
     __syncthreads();
 
@@ -277,12 +214,11 @@ gemv_w4a16_kernel(Params p) {
         for (int c = 0; c < CPT; ++c) y[m][c] = 0.0f;
 
     if (active) {
-        int iacc[CPT][MT];           // integer path
-        float facc[CPT][MT][2];      // floating path
+        int iacc[CPT][MT];
 #pragma unroll
         for (int c = 0; c < CPT; ++c)
 #pragma unroll
-            for (int m = 0; m < MT; ++m) { iacc[c][m] = 0; facc[c][m][0] = facc[c][m][1] = 0.0f; }
+            for (int m = 0; m < MT; ++m) iacc[c][m] = 0;
 
         // End of a group segment at packed row i: fold with its scale and zero point.
         auto fold = [&](int i) {
@@ -293,14 +229,8 @@ gemv_w4a16_kernel(Params p) {
 #pragma unroll
                 for (int m = 0; m < MT; ++m) {
                     const float corr = -(8.0f + f.y) * gsum[g * MT + m];
-                    float t;
-                    if (INT) {
-                        t = fmaf((float)iacc[c][m], 1.0f / gpow[g * MT + m], corr);
-                        iacc[c][m] = 0;
-                    } else {
-                        t = fmaf(facc[c][m][0] + facc[c][m][1], kUnscale, corr);
-                        facc[c][m][0] = facc[c][m][1] = 0.0f;
-                    }
+                    const float t = fmaf((float)iacc[c][m], 1.0f / gpow[g * MT + m], corr);
+                    iacc[c][m] = 0;
                     y[m][c] = fmaf(f.x, t, y[m][c]);
                 }
             }
@@ -308,38 +238,20 @@ gemv_w4a16_kernel(Params p) {
 
         // One packed row of the CTA's range.
         auto chunk = [&](int i, const VT& wvd) {
-            if (INT) {
 #pragma unroll
-                for (int m = 0; m < MT; ++m) {
-                    const int4 xw = xi[(size_t)i * MT + m];
+            for (int m = 0; m < MT; ++m) {
+                const int4 xw = xi[(size_t)i * MT + m];
 #pragma unroll
-                    for (int c = 0; c < CPT; ++c) {
-                        const uint32_t w = word_of(wvd, c);
-                        const int b0 = (int)(w & 0x0F0F0F0Fu);          // u0 u2 u4 u6
-                        const int b1 = (int)((w >> 4) & 0x0F0F0F0Fu);   // u1 u3 u5 u7
-                        int a = iacc[c][m];
-                        a = __dp2a_lo(xw.x, b0, a);
-                        a = __dp2a_hi(xw.y, b0, a);
-                        a = __dp2a_lo(xw.z, b1, a);
-                        a = __dp2a_hi(xw.w, b1, a);
-                        iacc[c][m] = a;
-                    }
-                }
-            } else {
-                float wf[CPT][8];
-#pragma unroll
-                for (int c = 0; c < CPT; ++c) unpack_denormal(word_of(wvd, c), wf[c]);
-#pragma unroll
-                for (int m = 0; m < MT; ++m) {
-                    const float4 xa = *reinterpret_cast<const float4*>(xq + ((size_t)i * MT + m) * 8);
-                    const float4 xb = *reinterpret_cast<const float4*>(xq + ((size_t)i * MT + m) * 8 + 4);
-#pragma unroll
-                    for (int c = 0; c < CPT; ++c) {
-                        ffma2(facc[c][m][0], facc[c][m][1], wf[c][0], wf[c][1], xa.x, xa.y);
-                        ffma2(facc[c][m][0], facc[c][m][1], wf[c][2], wf[c][3], xa.z, xa.w);
-                        ffma2(facc[c][m][0], facc[c][m][1], wf[c][4], wf[c][5], xb.x, xb.y);
-                        ffma2(facc[c][m][0], facc[c][m][1], wf[c][6], wf[c][7], xb.z, xb.w);
-                    }
+                for (int c = 0; c < CPT; ++c) {
+                    const uint32_t w = word_of(wvd, c);
+                    const int b0 = (int)(w & 0x0F0F0F0Fu);          // u0 u2 u4 u6
+                    const int b1 = (int)((w >> 4) & 0x0F0F0F0Fu);   // u1 u3 u5 u7
+                    int a = iacc[c][m];
+                    a = __dp2a_lo(xw.x, b0, a);
+                    a = __dp2a_hi(xw.y, b0, a);
+                    a = __dp2a_lo(xw.z, b1, a);
+                    a = __dp2a_hi(xw.w, b1, a);
+                    iacc[c][m] = a;
                 }
             }
             if (((c0 + i + 1) % CHUNKS_PER_GROUP) == 0 || i + 1 == len) fold(i);
@@ -367,17 +279,12 @@ gemv_w4a16_kernel(Params p) {
     auto store_row = [&](int m, const float* v) {
         if (p.out_type == QG_OUT_F32) {
             float* dst = static_cast<float*>(p.Y) + (size_t)m * p.N + n0;
-            if (CPT == 4) *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-            else *reinterpret_cast<float2*>(dst) = make_float2(v[0], v[1]);
+            *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
         } else {
             __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.Y) + (size_t)m * p.N + n0;
             __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
-            if (CPT == 4) {
-                __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
-                *reinterpret_cast<uint2*>(dst) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-            } else {
-                *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<uint32_t*>(&a);
-            }
+            __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+            *reinterpret_cast<uint2*>(dst) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
         }
     };
     if (p.splits == 1) {
@@ -391,8 +298,7 @@ gemv_w4a16_kernel(Params p) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
             float* dst = p.ws + ((size_t)blockIdx.y * MT + m) * p.N + n0;
-            if (CPT == 4) *reinterpret_cast<float4*>(dst) = make_float4(y[m][0], y[m][1], y[m][2], y[m][3]);
-            else *reinterpret_cast<float2*>(dst) = make_float2(y[m][0], y[m][1]);
+            *reinterpret_cast<float4*>(dst) = make_float4(y[m][0], y[m][1], y[m][2], y[m][3]);
         }
     }
     __threadfence();
@@ -407,13 +313,8 @@ gemv_w4a16_kernel(Params p) {
             float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             for (int sp = 0; sp < p.splits; ++sp) {
                 const float* src = p.ws + ((size_t)sp * MT + m) * p.N + n0;
-                if (CPT == 4) {
-                    const float4 v = __ldcg(reinterpret_cast<const float4*>(src));
-                    s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
-                } else {
-                    const float2 v = __ldcg(reinterpret_cast<const float2*>(src));
-                    s[0] += v.x; s[1] += v.y;
-                }
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(src));
+                s[0] += v.x; s[1] += v.y; s[2] += v.z; s[3] += v.w;
             }
             store_row(m, s);
         }
@@ -421,14 +322,14 @@ gemv_w4a16_kernel(Params p) {
     if (threadIdx.x == 0) p.tickets[blockIdx.x] = 0;   // ready for the next call
 }
 
-static int m_template(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16; }
+static int m_template(int M) { return M <= 1 ? 1 : 2; }
 
 static int col_blocks_for(int mt, int N) { return (N + cols_per_cta(mt) - 1) / cols_per_cta(mt); }
 
 // Shared-memory bytes for a K range of `len` packed rows (see the kernel's layout).
 static size_t smem_bytes_len(int mt, int len) {
     const size_t gmax = (size_t)(len + CHUNKS_PER_GROUP - 1) / CHUNKS_PER_GROUP + 1;
-    const size_t per_chunk = int_path(mt) ? (size_t)mt * 16 : (size_t)mt * 32;
+    const size_t per_chunk = (size_t)mt * 16;
     return gmax * mt * 8 + gmax * cols_per_cta(mt) * 4 + (size_t)len * per_chunk + 16;
 }
 constexpr size_t kSmemBudget = 180 * 1024;
@@ -451,19 +352,32 @@ static size_t smem_bytes(int mt, int K, int splits) { return smem_bytes_len(mt, 
 
 } // namespace w4
 
-// Workspace: fp32 partials for the largest row chunk, then one ticket per
-// column block of the narrowest column-block width (256 columns).
+// Row chunks of up to 16 rows: 1-2 rows run on the CUDA cores (this file),
+// 3-16 on the tensor cores (qg_gemv_w4a16_tc.cu).
+constexpr int kTensorMinRows = 3;
+
+static uint64_t ticket_bytes(int N) {
+    const uint64_t a = (uint64_t)((N + 255) / 256), b = gemv_w4a16_tc_ticket_count(N);
+    return (a > b ? a : b) * 4;
+}
+
+// Workspace: fp32 partials for the largest row chunk, then the tickets (shared
+// by both kernels: each leaves them zero).
 uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int /*sm_count*/) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     uint64_t partials = 0;
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
-        const int mt = w4::m_template(M - m0 < w4::MAX_M ? M - m0 : w4::MAX_M);
-        const int splits = w4::choose_splits(mt, N, K);
-        const uint64_t ws = (uint64_t)splits * mt * N * 4;
+        const int mrows = M - m0 < w4::MAX_M ? M - m0 : w4::MAX_M;
+        uint64_t ws;
+        if (mrows >= kTensorMinRows) {
+            ws = gemv_w4a16_tc_partial_bytes(N, K);
+        } else {
+            const int mt = w4::m_template(mrows);
+            ws = (uint64_t)w4::choose_splits(mt, N, K) * mt * N * 4;
+        }
         if (ws > partials) partials = ws;
     }
-    const uint64_t tickets = (uint64_t)((N + 255) / 256) * 4;
-    return ((partials + 255) & ~255ull) + tickets;
+    return ((partials + 255) & ~255ull) + ticket_bytes(N);
 }
 
 int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,
@@ -484,9 +398,17 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
                  "qg_gemv_w4a16: workspace of %llu bytes needed (got %llu)", (unsigned long long)need,
                  (unsigned long long)workspace_bytes);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const uint64_t tickets_off = need - (uint64_t)((N + 255) / 256) * 4;
+    const uint64_t tickets_off = need - ticket_bytes(N);
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mrows = (M - m0) < w4::MAX_M ? (M - m0) : w4::MAX_M;
+        if (mrows >= kTensorMinRows) {
+            rc = gemv_w4a16_tc(static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K, W, S, Z,
+                               static_cast<uint8_t*>(Y) + (size_t)m0 * N * (out_type == QG_OUT_F32 ? 4 : 2), out_type,
+                               mrows, N, K, reinterpret_cast<float*>(ws),
+                               reinterpret_cast<unsigned int*>(ws + tickets_off), stream);
+            if (rc) return rc;
+            continue;
+        }
         const int mt = w4::m_template(mrows);
         const int splits = w4::choose_splits(mt, N, K);
         w4::Params p;
@@ -515,9 +437,6 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         break;
             QG_W4_LAUNCH(1)
             QG_W4_LAUNCH(2)
-            QG_W4_LAUNCH(4)
-            QG_W4_LAUNCH(8)
-            QG_W4_LAUNCH(16)
 #undef QG_W4_LAUNCH
         }
         QG_CUDA(cudaGetLastError());

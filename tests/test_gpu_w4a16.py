@@ -39,8 +39,10 @@ def test_generator_matches_oracle(cuda_device, oracle):
     np.testing.assert_array_equal(_np(Z.view(torch.int16)).view(np.uint16), rZ)
 
 
+# 1-2 rows run on the CUDA cores, 3-16 on the tensor cores, more in chunks of 16
 SHAPES = [(1, 512, 128), (1, 1028, 1024), (3, 2048, 2048), (8, 4096, 1024), (16, 1536, 4096),
-          (17, 516, 256), (5, 28672, 256)]
+          (17, 516, 256), (5, 28672, 256), (4, 300, 384), (12, 1028, 1024), (8, 128, 8192), (16, 36, 128),
+          (34, 260, 512)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
@@ -76,8 +78,9 @@ def test_full_size_config3(cuda_device, oracle, M):
         assert pb.device_status(0) == 0
 
 
-def test_workspace_reusable_and_checked(cuda_device, oracle):
-    M, N, K = 2, 2048, 2048
+@pytest.mark.parametrize("M", [2, 8])
+def test_workspace_reusable_and_checked(cuda_device, oracle, M):
+    N, K = 2048, 2048
     host, dev = _operands(oracle, M, N, K, seed=1, dev=cuda_device)
     need = pb.gemv_w4a16_workspace_bytes(M, N, K)
     ws = torch.zeros((need,), dtype=torch.uint8, device=cuda_device)
