@@ -17,8 +17,11 @@ Printed by rank 0, one JSON line:
             pinned-host operands are uploaded (qg_upload), the GEMM runs
             (qg_run_copy) and the bf16 result is read back (qg_download);
   roofline  tensor-bound: achieved TOPS of the GEMM kernel vs the measured
-            peak (2 x the measured bf16 dense burst figure of
-            MEASURED_PEAKS.json, INT8 being twice bf16 on this part);
+            peak: 2 x the measured bf16 dense figure of MEASURED_PEAKS.json
+            (INT8 being twice bf16 on this part; 4 x for FP4), the sustained
+            figure when the timed region is a long loop under the power cap
+            (the default run), the burst one for a short region; both
+            fractions are reported;
   cpu_baseline  the CPU oracle's INT8 GEMM (OpenMP, all host threads) on a
             bounded sample of rows of the same GEMM, rank 0 at N=1 only.
 Multi-GPU: one process per GPU (torchrun), each an independent instance with
@@ -322,10 +325,17 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         if wl["unit"] == "TOPS":
             work = ops / 1e12
             mult = wl.get("peak_mult", 2.0)   # dense INT8/FP8 = 2x bf16, FP4 = 4x bf16 on this part
-            peak = mult * peaks["bf16_tflops"]
-            peak_src = f"{mult:g} x {peaks['source']} bf16 dense burst ({peaks['bf16_tflops']} TFLOP/s)"
+            # the timed region is a back-to-back loop of ~1 s under the 1 kW cap:
+            # the sustained figure is the denominator, the burst one is reported beside it
+            timed_s = ms / 1e3
+            sustained = timed_s >= 0.2
+            base = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+            peak = mult * base
+            peak_src = (f"{mult:g} x {peaks['source']} bf16 dense {'sustained' if sustained else 'burst'} "
+                        f"({base} TFLOP/s; timed region {timed_s:.2f} s)")
             datasheet = mult / 2.0 * DATASHEET_INT8_TOPS
             extra = {f"frac_of_datasheet_{datasheet:g}": work / per_launch_s / datasheet,
+                     "frac_of_measured_burst": work / per_launch_s / (mult * peaks["bf16_tflops"]),
                      "frac_of_measured_sustained": work / per_launch_s / (mult * peaks["bf16_tflops_sustained"])}
         else:
             work = nbytes / 1e9
