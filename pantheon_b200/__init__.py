@@ -14,6 +14,7 @@ from __future__ import annotations
 from ._lib import (  # noqa: F401
     LIB_PATH,
     BIN_PATH,
+    DECODE_BIN_PATH,
     QG_FMT_INT8,
     QG_FMT_FP8,
     QG_FMT_NVFP4,
@@ -43,7 +44,7 @@ from .ops import (  # noqa: F401
 )
 
 __all__ = [
-    "LIB_PATH", "BIN_PATH", "QGError", "load_library", "Workload", "device_status",
+    "LIB_PATH", "BIN_PATH", "DECODE_BIN_PATH", "QGError", "load_library", "Workload", "device_status",
     "gemm_i8", "gemm_fp8_b128", "gen_fp8", "gemm_nvfp4", "gen_nvfp4", "nvfp4_sf_bytes", "gemv_w4a16", "gemv_w4a16_workspace_bytes", "gen_w4a16", "gen_i8", "gen_uniform_f32", "gen_normal_f32", "verify_words",
     "QG_FMT_INT8", "QG_FMT_FP8", "QG_FMT_NVFP4", "QG_FMT_W4A16",
     "QG_OUT_BF16", "QG_OUT_F32", "QG_OUT_S32",

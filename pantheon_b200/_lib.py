@@ -8,6 +8,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "lib" / "libpantheon_qgemm.so"
 BIN_PATH = PKG / "lib" / "quantized_gemm"
+DECODE_BIN_PATH = PKG / "lib" / "llm_decode"
 HEADER = PKG.parent / "include" / "pantheon_qgemm.h"
 
 QG_OK = 0

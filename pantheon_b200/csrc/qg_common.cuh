@@ -25,7 +25,7 @@ const char* last_error();
         cudaError_t e_ = (call);                                                       \
         if (e_ != cudaSuccess) {                                                       \
             ::qg::set_error("%s failed: %s (%d) at %s:%d", #call, cudaGetErrorString(e_), \
-                            (int)e_, __FILE__, __LINE__);                              \
+                            (int)e_, __FILE_NAME__, __LINE__);                         \
             return QG_ERR_CUDA;                                                        \
         }                                                                              \
     } while (0)

@@ -1,5 +1,15 @@
-// quantized_gemm -- drop-in replacement for Pantheon's `quantized_gemm`
-// workload binary, running real quantized GEMMs on the B200 tensor cores.
+// quantized_gemm / llm_decode -- drop-in replacements for Pantheon's
+// `quantized_gemm` and `llm_decode` workload binaries, running real quantized
+// GEMMs / the W4A16 decode GEMV on the B200.  One source, two binaries: built
+// with QG_DECODE_BINARY it is `llm_decode` (default --format w4a16, decode
+// banner, also reports tokens/s), otherwise `quantized_gemm` (default int8).
+//
+// llm_decode's reference (kernels/llm_decode/llm_decode.cpp:59-115) has the
+// same argv and flags; its `Throughput:` unit was tokens/s of a KV gather.
+// Here the decode step is the weight-only projection, a stream over the
+// weights, so `Throughput:` is GB/s (the runner derives MB/s per watt from a
+// GB/s row, pantheon.py:3559) and tokens/s (rows x calls / s) is logged on an
+// "  -> Tokens/s:" line.
 //
 // Process contract (kept from the reference):
 //   argv   <device> <duration_s> <mem_pct> [--verify] [--inject_error]
@@ -29,6 +39,16 @@
 
 namespace {
 
+#ifdef QG_DECODE_BINARY
+constexpr int kDefaultFormat = QG_FMT_W4A16;
+constexpr const char* kWorkload = "LLM Decode";
+constexpr const char* kFaultTag = "LLM_DECODE";
+#else
+constexpr int kDefaultFormat = QG_FMT_INT8;
+constexpr const char* kWorkload = "Quantized GEMM";
+constexpr const char* kFaultTag = "QUANTIZED_GEMM";
+#endif
+
 // Launch-knob clamps with the reference's bounds (common.h:248-311).
 constexpr int kMaxKernelLoops = 1000000;
 
@@ -37,7 +57,7 @@ struct Options {
     bool verify = false, inject = false;
     int kernel_loops = 0;        // GEMMs per timed batch; 0 = size a batch to ~200 ms
     int warmup_iters = 3;
-    int format = QG_FMT_INT8;
+    int format = kDefaultFormat;
     int m = 0, n = 0, k = 0, copies = 0;
     uint64_t seed = 1;
     bool seed_given = false;
@@ -151,8 +171,8 @@ int main(int argc, char* argv[]) {
     const double bytes = qg_bytes_per_launch(ctx);
     const bool bw_metric = (o.format == QG_FMT_W4A16);
 
-    std::cout << "[PANTHEON] GPU " << o.device << ": Quantized GEMM (" << format_name(o.format)
-              << ", tcgen05 sm_100a)" << std::endl;
+    std::cout << "[PANTHEON] GPU " << o.device << ": " << kWorkload << " (" << format_name(o.format)
+              << (bw_metric ? " GEMV" : "") << ", sm_100a)" << std::endl;
     std::cout << "  -> Working Set:   " << (need >> 20) << " MiB (" << cfg.copies << " operand cop"
               << (cfg.copies == 1 ? "y" : "ies") << ")" << std::endl;
     std::cout << "  -> Work/Launch:   " << ops / 1e12 << " Tops, " << bytes / 1e6 << " MB" << std::endl;
@@ -193,7 +213,7 @@ int main(int argc, char* argv[]) {
                 qg_mismatch log[8];
                 int nlog = qg_mismatch_log(ctx, log, 8);
                 for (int i = 0; i < nlog; ++i) {
-                    printf("[SDC FAULT][QUANTIZED_GEMM] Output mismatch! Word: %llu | Exp: 0x%08x | Act: 0x%08x | XOR: 0x%08x\n",
+                    printf("[SDC FAULT][%s] Output mismatch! Word: %llu | Exp: 0x%08x | Act: 0x%08x | XOR: 0x%08x\n", kFaultTag,
                            (unsigned long long)log[i].index, log[i].expected, log[i].actual, log[i].expected ^ log[i].actual);
                 }
                 fflush(stdout);
@@ -205,6 +225,11 @@ int main(int argc, char* argv[]) {
 
     const double rate = busy > 0 ? (bw_metric ? (bytes * (double)launches) / busy / 1e9 : (ops * (double)launches) / busy / 1e12) : 0.0;
     std::cout << "Throughput: " << rate << (bw_metric ? " GB/s" : " TOPS") << std::endl;
+    if (bw_metric && busy > 0) {
+        const double rows = o.m > 0 ? o.m : 1;   // the GEMV's default decode batch is one row
+        std::cout << "  -> Tokens/s:      " << rows * (double)launches / busy << " (" << rows << " row"
+                  << (rows == 1 ? "" : "s") << " per call)" << std::endl;
+    }
 
     int exit_code = 0;
     if (o.verify) {
@@ -216,7 +241,7 @@ int main(int argc, char* argv[]) {
             qg_mismatch log[8];
             int nlog = qg_mismatch_log(ctx, log, 8);
             for (int i = 0; i < nlog; ++i)
-                printf("[SDC FAULT][QUANTIZED_GEMM] Output mismatch! Word: %llu | Exp: 0x%08x | Act: 0x%08x | XOR: 0x%08x\n",
+                printf("[SDC FAULT][%s] Output mismatch! Word: %llu | Exp: 0x%08x | Act: 0x%08x | XOR: 0x%08x\n", kFaultTag,
                        (unsigned long long)log[i].index, log[i].expected, log[i].actual, log[i].expected ^ log[i].actual);
             fflush(stdout);
             mismatches += mm;

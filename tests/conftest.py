@@ -29,7 +29,7 @@ def qglib():
     """The in-tree C-ABI library, built if missing (build needs only nvcc)."""
     import pantheon_b200
     from pantheon_b200 import build
-    if not pantheon_b200.LIB_PATH.exists() or not pantheon_b200.BIN_PATH.exists():
+    if not all(x.exists() for x in (pantheon_b200.LIB_PATH, pantheon_b200.BIN_PATH, pantheon_b200.DECODE_BIN_PATH)):
         build.build()
     return pantheon_b200.load_library()
 

@@ -34,24 +34,30 @@ def test_library_exports_every_header_symbol(qglib):
     assert qglib.qg_abi_version() == 1
 
 
-def test_binary_needs_three_arguments(qglib):
-    from pantheon_b200 import BIN_PATH
-    for args in ([], ["0"], ["0", "1"]):
-        proc = subprocess.run([str(BIN_PATH), *args], capture_output=True, text=True, timeout=60)
-        assert proc.returncode == 1
-        assert "Throughput:" not in proc.stdout
+def _binaries():
+    from pantheon_b200 import BIN_PATH, DECODE_BIN_PATH
+    return [(BIN_PATH, "quantized_gemm"), (DECODE_BIN_PATH, "llm_decode")]
+
+
+def test_binaries_need_three_arguments(qglib):
+    """ai_workload_template.h:352-353 and llm_decode.cpp:60: argc < 4 exits 1."""
+    for path, _ in _binaries():
+        for args in ([], ["0"], ["0", "1"]):
+            proc = subprocess.run([str(path), *args], capture_output=True, text=True, timeout=60)
+            assert proc.returncode == 1
+            assert "Throughput:" not in proc.stdout
 
 
 @pytest.mark.skipif(_gpu_visible(), reason="checks the no-GPU failure path")
-def test_binary_without_gpu_fails_loudly(qglib):
-    from pantheon_b200 import BIN_PATH
-    proc = subprocess.run([str(BIN_PATH), "0", "1", "5", "--verify"], capture_output=True, text=True, timeout=60)
-    assert proc.returncode != 0
-    assert "[PANTHEON ERROR]" in proc.stderr
-    assert "Throughput:" not in proc.stdout
-    assert "Verification: PASS" not in proc.stdout
-    status = parse_kernel_output(proc.stdout, proc.stderr, proc.returncode, "quantized_gemm")[2]
-    assert status == "FAIL"
+def test_binaries_without_gpu_fail_loudly(qglib):
+    for path, name in _binaries():
+        proc = subprocess.run([str(path), "0", "1", "5", "--verify"], capture_output=True, text=True, timeout=60)
+        assert proc.returncode != 0
+        assert "[PANTHEON ERROR]" in proc.stderr
+        assert "Throughput:" not in proc.stdout
+        assert "Verification: PASS" not in proc.stdout
+        status = parse_kernel_output(proc.stdout, proc.stderr, proc.returncode, name)[2]
+        assert status == "FAIL"
 
 
 @pytest.mark.skipif(_gpu_visible(), reason="checks the no-GPU failure path")

@@ -49,3 +49,14 @@ def test_unknown_flags_are_ignored(cuda_device):
              "--m", 512, "--n", 512, "--k", 512, "--kernel_loops", 5, "--warmup_iters", 1)
     assert p.returncode == 0, p.stdout + p.stderr
     assert "Verification: PASS" in p.stdout
+
+
+@pytest.mark.parametrize("fmt,shape", [("fp8", (1024, 1024, 2048)), ("nvfp4", (1024, 1024, 2048)), ("w4a16", (4, 4096, 2048))])
+def test_other_formats_verify(cuda_device, fmt, shape):
+    m, n, k = shape
+    p = _run(0, 1, 50, "--verify", "--format", fmt, "--m", m, "--n", n, "--k", k)
+    assert p.returncode == 0, p.stdout + p.stderr
+    t, unit, status, _, _ = parse_kernel_output(p.stdout, p.stderr, p.returncode, "quantized_gemm")
+    assert status == "PASS" and t > 0 and unit == ("GB/s" if fmt == "w4a16" else "TOPS")
+    pi = _run(0, 1, 50, "--verify", "--inject_error", "--format", fmt, "--m", m, "--n", n, "--k", k)
+    assert pi.returncode != 0 and "[SDC FAULT]" in pi.stdout
