@@ -238,6 +238,18 @@ def run_reference(args, rank: int):
     return 0
 
 
+def max_over_ranks(values, world: int, device=None):
+    """Element-wise max of per-rank values (times, mismatch counts, error flags):
+    the job is as slow as its slowest rank.  One collective, the same on every
+    rank; a no-op for a single process."""
+    import torch
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -313,10 +325,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     barrier()
     e2e_ms = e0.elapsed_time(e1)
 
-    t = torch.tensor([ms, e2e_ms, float(mismatches), float(status != 0)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max, e2e_max, mm_max, bad = t.tolist()
+    ms_max, e2e_max, mm_max, bad = max_over_ranks([ms, e2e_ms, float(mismatches), float(status != 0)], world, dev)
 
     result = None
     if rank == 0:
