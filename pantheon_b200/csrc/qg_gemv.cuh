@@ -5,7 +5,30 @@
 
 #include "qg_common.cuh"
 
+#include <utility>
+
 namespace qg {
+
+// Launch with programmatic stream serialization (PDL): the kernel's CTAs may
+// start while the previous kernel on the stream drains; the kernels call
+// griddepcontrol.wait before any global memory access and
+// griddepcontrol.launch_dependents once all their CTAs are resident, so
+// back-to-back GEMV calls overlap one call's tail with the next one's launch.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, kernel, std::forward<Args>(args)...);
+}
 
 // The split of the work depends only on the shape (sized for the 148 SMs of a
 // B200), so workspace sizes are functions of (M, N, K) alone.

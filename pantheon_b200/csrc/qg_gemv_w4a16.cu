@@ -113,6 +113,11 @@ gemv_w4a16_kernel(Params p) {
                                                ~static_cast<uintptr_t>(15));
     int4* xi = reinterpret_cast<int4*>(xdat);
 
+    // Launched with programmatic stream serialization: this CTA may be resident
+    // before the previous kernel on the stream has finished, so nothing global
+    // is read or written until that grid is complete (a no-op otherwise).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
     // The first two batches of weights are requested before anything else, so
     // they stream in while the prologue below stages activations and scales.
     const int n0 = col0 + threadIdx.x * CPT;
@@ -275,6 +280,11 @@ gemv_w4a16_kernel(Params p) {
         }
     }
 
+    // every CTA of this call is resident by now: the next call on the stream may
+    // launch and take SMs as they free up (it waits for this grid before any
+    // global access)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
     // ---- publish: directly when K is not split, else partial + ticket
     auto store_row = [&](int m, const float* v) {
         if (p.out_type == QG_OUT_F32) {
@@ -433,7 +443,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         if (smem > 48 * 1024)                                                                                    \
             QG_CUDA(cudaFuncSetAttribute(w4::gemv_w4a16_kernel<MTV>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
                                          (int)smem));                                                            \
-        w4::gemv_w4a16_kernel<MTV><<<grid, w4::THREADS, smem, stream>>>(p);                                      \
+        QG_CUDA(launch_pdl(w4::gemv_w4a16_kernel<MTV>, grid, dim3(w4::THREADS), smem, stream, p));             \
         break;
             QG_W4_LAUNCH(1)
             QG_W4_LAUNCH(2)

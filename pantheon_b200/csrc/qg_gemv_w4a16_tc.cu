@@ -190,6 +190,10 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
     const int nu = (int)(u1 - u0);
     const UnitPos start{(int)(u0 / p.upt), (int)(u0 % p.upt)};
 
+    // launched with programmatic stream serialization: no global access (and
+    // no TMEM) until the previous grid on the stream is complete
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&bars->full[s], 1);
@@ -232,6 +236,8 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
                 armed |= 1u << s;
                 armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
             }
+            // every load of this CTA is issued: the next call may launch
+            asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
             // no copy may still be landing when the CTA exits
             for (int s = 0; s < STAGES; ++s)
                 if (armed & (1u << s)) mbar_wait(&bars->full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
@@ -586,7 +592,8 @@ int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, vo
     p.maxp = s.maxp;
     p.out_type = out_type;
     p.status = status;
-    w4tc::gemv_w4a16_tc_kernel<<<s.ctas, w4tc::THREADS, w4tc::SMEM_BYTES, stream>>>(tmW, tmX, p);
+    QG_CUDA(launch_pdl(w4tc::gemv_w4a16_tc_kernel, dim3(s.ctas), dim3(w4tc::THREADS), (size_t)w4tc::SMEM_BYTES, stream,
+                       tmW, tmX, p));
     QG_CUDA(cudaGetLastError());
     return QG_OK;
 }
