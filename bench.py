@@ -175,6 +175,7 @@ def cpu_baseline(target_s: float = 15.0):
     """
     import numpy as np
     from oracle import qg_oracle as O
+    O.set_threads(O.host_threads())   # all host threads, whatever the launcher set
     A, B, sa, sb = O.int8_operands(M, N, K, seed=1)
     per_row = _oracle_row_rate(O, A, B, sa, sb)
     nrows = int(max(64, min(M, target_s / max(per_row, 1e-9))))
@@ -210,6 +211,7 @@ def run_reference(args, rank: int):
     warm = max(0, args.warmup)
     import numpy as np
     from oracle import qg_oracle as O
+    O.set_threads(O.host_threads())   # torchrun sets OMP_NUM_THREADS=1; the arm uses every host thread
     A, B, sa, sb = O.int8_operands(M, N, K, seed=1)
     # bounded sample per step: the leading rows that keep the whole run near a minute
     per_row = _oracle_row_rate(O, A, B, sa, sb)

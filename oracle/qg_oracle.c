@@ -26,6 +26,15 @@ int qgo_threads(void) {
 #endif
 }
 
+/* Use n OpenMP threads from now on (a launcher may have set OMP_NUM_THREADS=1). */
+void qgo_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* ------------------------------------------------------------------------
  * Generator.  The reference fills operands from a hash of the element index
  * (ai_initialize, kernels/common/ai_workload_template.h:85-94;

@@ -110,6 +110,7 @@ double   qgo_max_rel_err(const void* y, const void* r, uint64_t n, int kind);
 
 /* number of OpenMP threads the oracle uses */
 int qgo_threads(void);
+void qgo_set_threads(int n);
 
 #ifdef __cplusplus
 }

@@ -67,6 +67,7 @@ def lib() -> C.CDLL:
             "qgo_count_mismatch_u32": (C.c_uint64, [_P, _P, C.c_uint64]),
             "qgo_max_rel_err": (C.c_double, [_P, _P, C.c_uint64, C.c_int]),
             "qgo_threads": (C.c_int, []),
+            "qgo_set_threads": (None, [C.c_int]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -284,3 +285,17 @@ def max_rel_err(y: np.ndarray, r: np.ndarray, kind: int) -> float:
 
 def threads() -> int:
     return lib().qgo_threads()
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads for the oracle from now on (overrides OMP_NUM_THREADS)."""
+    lib().qgo_set_threads(int(n))
+
+
+def host_threads() -> int:
+    """Cores this process may run on."""
+    import os
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
