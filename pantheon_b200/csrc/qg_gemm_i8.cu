@@ -82,6 +82,78 @@ __device__ __forceinline__ uint32_t cksum_weight(uint32_t m, uint32_t n) {
     return (m * 0x9E3779B1u + n * 0x85EBCA77u) | 1u;
 }
 
+// One 32-column chunk of an accumulator row: checksum fold, then the s32 /
+// dequantised f32 / bf16 store (ragged edges handled per element).
+template <int OUT>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, bool row_ok, float sam,
+                                               const Params& p, uint32_t& ck) {
+    if (!row_ok || n0 >= p.N) return;
+    const bool full_chunk = (n0 + 32 <= p.N);
+    if (p.row_cksum) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (full_chunk || n0 + i < p.N) ck += r[i] * cksum_weight((uint32_t)m, (uint32_t)(n0 + i));
+    }
+    if (OUT == QG_OUT_S32) {
+        int32_t* dst = static_cast<int32_t*>(p.C) + (size_t)m * p.N + n0;
+        if (full_chunk && (p.N % 4) == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<uint4*>(dst + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (n0 + i < p.N) dst[i] = (int32_t)r[i];
+        }
+        return;
+    }
+    float f[32];
+    if (full_chunk) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + i));
+            f[i + 0] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 0]), sam), s4.x);
+            f[i + 1] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 1]), sam), s4.y);
+            f[i + 2] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 2]), sam), s4.z);
+            f[i + 3] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 3]), sam), s4.w);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float sbn = (n0 + i < p.N) ? __ldg(p.sb + n0 + i) : 0.0f;
+            f[i] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i]), sam), sbn);
+        }
+    }
+    if (OUT == QG_OUT_F32) {
+        float* dst = static_cast<float*>(p.C) + (size_t)m * p.N + n0;
+        if (full_chunk && (p.N % 4) == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (n0 + i < p.N) dst[i] = f[i];
+        }
+    } else {
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
+        if (full_chunk && (p.N % 8) == 0) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+                w[i] = *reinterpret_cast<uint32_t*>(&h);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+                *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (n0 + i < p.N) dst[i] = __float2bfloat16_rn(f[i]);
+        }
+    }
+}
+
 template <int OUT>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
@@ -204,72 +276,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 __syncwarp();
                 tmem_ld_32x32b_x32(t_row + c, r);
                 tmem_ld_wait_regs(r);
-                const int n0 = nt * BN + c;
-                if (!row_ok || n0 >= p.N) continue;
-                const bool full_chunk = (n0 + 32 <= p.N);
-                if (p.row_cksum) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (full_chunk || n0 + i < p.N) ck += r[i] * cksum_weight((uint32_t)m, (uint32_t)(n0 + i));
-                }
-                if (OUT == QG_OUT_S32) {
-                    int32_t* dst = static_cast<int32_t*>(p.C) + (size_t)m * p.N + n0;
-                    if (full_chunk && (p.N % 4) == 0) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4)
-                            *reinterpret_cast<uint4*>(dst + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (n0 + i < p.N) dst[i] = (int32_t)r[i];
-                    }
-                    continue;
-                }
-                float f[32];
-                if (full_chunk) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + i));
-                        f[i + 0] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 0]), sam), s4.x);
-                        f[i + 1] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 1]), sam), s4.y);
-                        f[i + 2] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 2]), sam), s4.z);
-                        f[i + 3] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i + 3]), sam), s4.w);
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float sbn = (n0 + i < p.N) ? __ldg(p.sb + n0 + i) : 0.0f;
-                        f[i] = __fmul_rn(__fmul_rn(__int2float_rn((int)r[i]), sam), sbn);
-                    }
-                }
-                if (OUT == QG_OUT_F32) {
-                    float* dst = static_cast<float*>(p.C) + (size_t)m * p.N + n0;
-                    if (full_chunk && (p.N % 4) == 0) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (n0 + i < p.N) dst[i] = f[i];
-                    }
-                } else {
-                    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
-                    if (full_chunk && (p.N % 8) == 0) {
-                        uint32_t w[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-                            w[i] = *reinterpret_cast<uint32_t*>(&h);
-                        }
-#pragma unroll
-                        for (int i = 0; i < 16; i += 4)
-                            *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (n0 + i < p.N) dst[i] = __float2bfloat16_rn(f[i]);
-                    }
-                }
+                epilogue_chunk<OUT>(r, m, nt * BN + c, row_ok, sam, p, ck);
             }
             tc_fence_before();
             mbar_arrive(&bars->tmem_empty[acc]);
@@ -282,6 +289,185 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (warp == 2) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (M >= 256): a cluster of two CTAs computes 256x256 tiles
+// with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) issued by the even
+// CTA.  Each CTA loads its own 128 rows of A and its own 128 rows (half) of B
+// per K block, 32 KB instead of the single-CTA kernel's 48 KB, which relieves
+// the operand stream into shared memory that bounds the single-CTA kernel;
+// each CTA's TMEM holds its 128 rows of the 256-column accumulator and its
+// epilogue is the single-CTA one.  Protocol:
+//   * both CTAs' copies complete on the even CTA's `full` barrier (the even
+//     producer arms it with both CTAs' bytes); the odd producer paces itself
+//     on its own `empty` barrier;
+//   * the MMA thread commits `empty` and `tmem_full` to both CTAs (one plain
+//     commit per CTA, no multicast);
+//   * each epilogue warp of either CTA arrives on the even CTA's `tmem_empty`;
+//   * TMEM is allocated and freed by warp 2 of both CTAs (cta_group::2), and a
+//     cluster barrier keeps both CTAs alive until the last MMA has landed.
+constexpr int P_STAGES = 6;
+constexpr int PA_BYTES = BM * BK;                 // 16 KB: this CTA's A rows
+constexpr int PB_BYTES = (BN / 2) * BK;           // 16 KB: this CTA's half of B
+constexpr int P_STAGE_BYTES = PA_BYTES + PB_BYTES;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int P_EPI_WARPS = 4;
+
+template <int OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + P_STAGES * PA_BYTES;
+    struct PBarriers {
+        uint64_t full[P_STAGES];
+        uint64_t empty[P_STAGES];
+        uint64_t tmem_full[2];
+        uint64_t tmem_empty[2];
+        uint64_t drain;
+        uint32_t tmem_base;
+        int abort;
+    };
+    PBarriers* bars = reinterpret_cast<PBarriers*>(smem + P_STAGES * P_STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
+    const int tiles_n = (p.N + BN - 1) / BN;
+    const int tiles = tiles_m * tiles_n;
+    const int nk = (p.K + BK - 1) / BK;
+    const int pair = blockIdx.x >> 1;
+    const int pairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) { mbar_init(&bars->full[s], 1); mbar_init(&bars->empty[s], 1); }
+        for (int a = 0; a < 2; ++a) { mbar_init(&bars->tmem_full[a], 1); mbar_init(&bars->tmem_empty[a], 2 * P_EPI_WARPS); }
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 2) {
+        tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    // both CTAs' barriers initialised and TMEM allocated before anyone signals the other
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+    volatile int* abort_flag = &bars->abort;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------ producer (both CTAs)
+        uint32_t stage = 0, phase = 0;
+        uint32_t armed = 0, armed_phase = 0;
+        bool ok = true;
+        for (int t = pair; t < tiles && ok; t += pairs) {
+            int mt, nt;
+            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER)) { ok = false; break; }
+                if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * P_STAGE_BYTES);
+                const uint32_t full_leader = mapa_shared(smem_u32(&bars->full[stage]), 0);
+                tma_load_2d_pair(sA + stage * PA_BYTES, &tmA, full_leader, kb * BK, mt * 2 * BM + (int)rank * BM);
+                tma_load_2d_pair(sB + stage * PB_BYTES, &tmB, full_leader, kb * BK, nt * BN + (int)rank * (BN / 2));
+                armed |= 1u << stage;
+                armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        if (!ok && leader) {
+            // copies of both CTAs complete on these barriers: let them land
+            for (int s = 0; s < P_STAGES; ++s)
+                if (armed & (1u << s)) mbar_wait(&bars->full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
+        }
+    } else if (warp == 1 && lane == 0 && leader) {
+        // ------------------------------------------------------------ MMA issuer (even CTA)
+        constexpr uint32_t IDESC = make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, 2 * BM, BN);
+        uint32_t stage = 0, phase = 0;
+        bool ok = true, issued = false;
+        int iter = 0;
+        for (int t = pair; t < tiles && ok; t += pairs, ++iter) {
+            const uint32_t acc = iter & 1;
+            const uint32_t acc_phase = (iter >> 1) & 1;
+            if (!mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.status, SITE_MMA_TMEM)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_MMA_FULL)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sA + stage * PA_BYTES);
+                const uint32_t b_addr = smem_u32(sB + stage * PB_BYTES);
+#pragma unroll
+                for (int k = 0; k < BK / UMMA_K; ++k)
+                    umma_i8_pair(d_tmem, make_sdesc_kmajor_sw128(a_addr + k * UMMA_K),
+                                 make_sdesc_kmajor_sw128(b_addr + k * UMMA_K), IDESC, (kb | k) != 0 ? 1u : 0u);
+                issued = true;
+                const uint32_t e = smem_u32(&bars->empty[stage]);
+                umma_commit_pair(mapa_shared(e, 0));
+                umma_commit_pair(mapa_shared(e, 1));
+                if (++stage == P_STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (ok) {
+                const uint32_t f = smem_u32(&bars->tmem_full[acc]);
+                umma_commit_pair(mapa_shared(f, 0));
+                umma_commit_pair(mapa_shared(f, 1));
+            }
+        }
+        if (!ok && issued) {
+            umma_commit_pair(mapa_shared(smem_u32(&bars->drain), 0));
+            mbar_wait(&bars->drain, 0, nullptr, nullptr, 0);
+        }
+    } else if (warp >= EPI_WARP0) {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int ew = warp - EPI_WARP0;
+        const int row = ew * 32 + lane;
+        int iter = 0;
+        for (int t = pair; t < tiles; t += pairs, ++iter) {
+            int mt, nt;
+            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            const uint32_t acc = iter & 1;
+            const uint32_t acc_phase = (iter >> 1) & 1;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&bars->tmem_full[acc], acc_phase, abort_flag, p.status, SITE_EPI) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const int m = mt * 2 * BM + (int)rank * BM + row;
+            const bool row_ok = m < p.M;
+            const float sam = (OUT != QG_OUT_S32 && row_ok) ? __ldg(p.sa + m) : 0.0f;
+            uint32_t ck = 0;
+            const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * ACC_COLS;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(t_row + c, r);
+                tmem_ld_wait_regs(r);
+                epilogue_chunk<OUT>(r, m, nt * BN + c, row_ok, sam, p, ck);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&bars->tmem_empty[acc]), 0));
+            if (p.row_cksum && row_ok) atomicAdd(p.row_cksum + m, ck);
+        }
+    }
+
+    // the even CTA's MMAs read this CTA's shared memory and write its TMEM:
+    // neither CTA frees anything before both are done
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
     }
 }
 
@@ -309,11 +495,38 @@ static int launch(const void* A, const void* B, const float* sa, const float* sb
         QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<QG_OUT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<QG_OUT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<QG_OUT_S32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(gemm_i8_pair_kernel<QG_OUT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(gemm_i8_pair_kernel<QG_OUT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(gemm_i8_pair_kernel<QG_OUT_S32>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
         attr_set[dev & 63] = true;
     }
     if (cksum) QG_CUDA(cudaMemsetAsync(cksum, 0, sizeof(uint32_t) * (size_t)M, stream));
 
     Params p{M, N, K, sa, sb, C, cksum, status};
+    if (M >= 2 * BM && info->sm_count >= 2) {
+        // CTA pairs: each CTA's B box is half a tile high
+        CUtensorMap tmBh;
+        if ((rc = make_tmap_2d(&tmBh, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)N, (uint64_t)K, BK,
+                               BN / 2, CU_TENSOR_MAP_SWIZZLE_128B)))
+            return rc;
+        const int tiles2 = ceil_div(M, 2 * BM) * ceil_div(N, BN);
+        // persistent pairs: only as many as can be resident at once (a pair needs
+        // two free SMs of one GPC, so this can be below sm_count / 2)
+        static int resident[64] = {};
+        if (!resident[dev & 63]) {
+            cudaLaunchConfig_t lc = {};
+            lc.gridDim = dim3(info->sm_count & ~1);
+            lc.blockDim = dim3(THREADS);
+            lc.dynamicSmemBytes = P_SMEM_BYTES;
+            int n = 0;
+            QG_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_i8_pair_kernel<QG_OUT_BF16>, &lc));
+            resident[dev & 63] = n > 0 ? n : 1;
+        }
+        const int pairs = tiles2 < resident[dev & 63] ? tiles2 : resident[dev & 63];
+        gemm_i8_pair_kernel<OUT><<<2 * pairs, THREADS, P_SMEM_BYTES, stream>>>(tmA, tmBh, p);
+        QG_CUDA(cudaGetLastError());
+        return QG_OK;
+    }
     const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
     const int grid = tiles < info->sm_count ? tiles : info->sm_count;
     gemm_i8_kernel<OUT><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, p);

@@ -58,6 +58,8 @@ SHAPES = [
     (1000, 1000, 1008),   # ragged everything, K not a multiple of 128
     (384, 768, 4096),     # deeper K
     (300, 8, 2064),       # N < 16
+    (4096, 4096, 512),    # M >= 256: CTA pairs, several 256x256 tiles per pair
+    (2560, 384, 256),     # pairs with a ragged N tile
 ]
 
 
