@@ -58,6 +58,11 @@ def _stale(out: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
+def cuda_include() -> Path:
+    """CUDA headers beside nvcc (the binary uses NVTX's header-only API)."""
+    return Path(nvcc()).resolve().parent.parent / "include"
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     OBJ_DIR.mkdir(parents=True, exist_ok=True)
     LIB_DIR.mkdir(parents=True, exist_ok=True)
@@ -80,8 +85,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     main = CSRC / "quantized_gemm_main.cpp"
     for out, defs in ((BIN, []), (DECODE_BIN, ["-DQG_DECODE_BINARY"])):
         if force or _stale(out, [main, LIB, ROOT / "include" / "pantheon_qgemm.h"]):
-            _run(["g++", "-O2", "-std=c++17", *defs, f"-I{ROOT / 'include'}", str(main), "-o", str(out),
-                  f"-L{LIB_DIR}", "-lpantheon_qgemm", "-Wl,-rpath,$ORIGIN"], verbose)
+            _run(["g++", "-O2", "-std=c++17", *defs, f"-I{ROOT / 'include'}", f"-I{cuda_include()}", str(main),
+                  "-o", str(out), f"-L{LIB_DIR}", "-lpantheon_qgemm", "-ldl", "-Wl,-rpath,$ORIGIN"], verbose)
     return LIB
 
 

@@ -30,6 +30,8 @@
 // include/pantheon_qgemm.h.
 #include "../../include/pantheon_qgemm.h"
 
+#include <nvtx3/nvToolsExt.h>   // header-only; a no-op unless a profiler is attached
+
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -38,6 +40,14 @@
 #include <string>
 
 namespace {
+
+// NVTX ranges around the run's phases ("qg:fill", "qg:golden", "qg:warmup",
+// "qg:timed", "qg:verify"), so a profiler can be pointed at the timed
+// launches alone (ncu --nvtx --nvtx-include "qg:timed/").
+struct Phase {
+    explicit Phase(const char* name) { nvtxRangePushA(name); }
+    ~Phase() { nvtxRangePop(); }
+};
 
 #ifdef QG_DECODE_BINARY
 constexpr int kDefaultFormat = QG_FMT_W4A16;
@@ -177,13 +187,20 @@ int main(int argc, char* argv[]) {
               << (cfg.copies == 1 ? "y" : "ies") << ")" << std::endl;
     std::cout << "  -> Work/Launch:   " << ops / 1e12 << " Tops, " << bytes / 1e6 << " MB" << std::endl;
 
-    if (qg_fill(ctx, o.seed) != QG_OK) return fail_ctx(ctx, "qg_fill");
-    if (qg_golden(ctx) != QG_OK) return fail_ctx(ctx, "qg_golden");
+    {
+        Phase ph("qg:fill");
+        if (qg_fill(ctx, o.seed) != QG_OK || qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "qg_fill");
+    }
+    {
+        Phase ph("qg:golden");
+        if (qg_golden(ctx) != QG_OK || qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "qg_golden");
+    }
 
     // Warm-up, and a timing probe to size the batch (~200 ms per sync, as the
     // reference's vendor GEMM batches: vendor_gemm.h:560-571).
     auto t0 = std::chrono::high_resolution_clock::now();
     if (o.warmup_iters > 0) {
+        Phase ph("qg:warmup");
         if (qg_run(ctx, o.warmup_iters, nullptr) != QG_OK || qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "warm-up");
     }
     double per_launch = std::chrono::duration<double>(std::chrono::high_resolution_clock::now() - t0).count() /
@@ -201,14 +218,20 @@ int main(int argc, char* argv[]) {
     auto start = std::chrono::high_resolution_clock::now();
     do {
         auto b0 = std::chrono::high_resolution_clock::now();
-        if (qg_run(ctx, loops, nullptr) != QG_OK) return fail_ctx(ctx, "qg_run");
-        if (qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "kernel");
+        {
+            Phase ph("qg:timed");
+            if (qg_run(ctx, loops, nullptr) != QG_OK) return fail_ctx(ctx, "qg_run");
+            if (qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "kernel");
+        }
         busy += std::chrono::duration<double>(std::chrono::high_resolution_clock::now() - b0).count();
         launches += (uint64_t)loops;
         if (o.verify) {
             // Every batch is checked against the golden result, not only the last.
             uint64_t mm = 0;
-            if (qg_verify(ctx, &mm) != QG_OK) return fail_ctx(ctx, "qg_verify");
+            {
+                Phase ph("qg:verify");
+                if (qg_verify(ctx, &mm) != QG_OK) return fail_ctx(ctx, "qg_verify");
+            }
             if (mm) {
                 qg_mismatch log[8];
                 int nlog = qg_mismatch_log(ctx, log, 8);
