@@ -173,6 +173,18 @@ QG_API int  qg_gemm_i8(const void* A, const void* B, const void* sa, const void*
                 void* C, int out_type, void* row_checksums,
                 int M, int N, int K, void* stream);
 
+/* Tensor-furnace GEMMs (the mma_virus workload): C = out(alpha * A B^T) with
+ * fp32 accumulation on the tcgen05 tensor cores, A [M,K], B [N,K] K-contiguous;
+ * qg_gemm_bf16: bf16 operands (K % 8 == 0); qg_gemm_e4m3: e4m3 bytes (K % 16 == 0);
+ * out_type QG_OUT_BF16 or QG_OUT_F32.  M >= 256 runs on CTA pairs.
+ * Replaces: the cuBLASLt bf16 / fp8 GEMM of the tensor furnace
+ *   (kernels/common/vendor_gemm.h:279-360, driven by kernels/mma_virus/mma_virus.cpp:264-282)
+ *   and its WMMA fallback (mma_virus.cpp:57-135). */
+QG_API int  qg_gemm_bf16(const void* A, const void* B, float alpha, void* C, int out_type,
+                         int M, int N, int K, void* stream);
+QG_API int  qg_gemm_e4m3(const void* A, const void* B, float alpha, void* C, int out_type,
+                         int M, int N, int K, void* stream);
+
 /* FP8 e4m3 with fp32 block scales:
  *   C[m,n] = out( sum_kb P_kb[m,n] * sa[m,kb] * sb[n/128,kb] ),
  *   P_kb = sum over the 128-deep K block kb of A[m,k] B[n,k] (tensor cores, fp32),

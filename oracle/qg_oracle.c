@@ -297,6 +297,41 @@ void qgo_gemm_i8(const int8_t* A, const int8_t* B, const float* sa, const float*
 }
 
 /* ------------------------------------------------------------------------
+ * Tensor-furnace GEMMs (the mma_virus workload): C = alpha * A B^T with
+ * bf16 (kind 1) or e4m3 (kind 2) operands; the exact products are summed in
+ * double, rounded to fp32, scaled by alpha in fp32, then stored as fp32 or
+ * bf16.  Rows rows[0..nrows) of C (all when rows is NULL), compact.
+ * ---------------------------------------------------------------------- */
+void qgo_gemm_dense(int kind, const void* A, const void* B, float alpha, int M, int N, int K,
+                    const int32_t* rows, int nrows, int out_type, void* C) {
+    if (!rows) nrows = M;
+    float lut[256];
+    for (int i = 0; i < 256; ++i) lut[i] = qgo_e4m3_to_f32((uint8_t)i);
+    #pragma omp parallel for schedule(dynamic, 1)
+    for (int r = 0; r < nrows; ++r) {
+        int m = rows ? rows[r] : r;
+        float* av = (float*)malloc(sizeof(float) * (size_t)K);
+        for (int k = 0; k < K; ++k)
+            av[k] = kind == 1 ? qgo_bf16_to_f32(((const uint16_t*)A)[(size_t)m * K + k])
+                              : lut[((const uint8_t*)A)[(size_t)m * K + k]];
+        for (int n = 0; n < N; ++n) {
+            double s = 0.0;
+            for (int k = 0; k < K; ++k) {
+                float b = kind == 1 ? qgo_bf16_to_f32(((const uint16_t*)B)[(size_t)n * K + k])
+                                    : lut[((const uint8_t*)B)[(size_t)n * K + k]];
+                s += (double)av[k] * (double)b;
+            }
+            float f = (float)s;
+            f = f * alpha;
+            size_t o = (size_t)r * N + n;
+            if (out_type == 1) ((float*)C)[o] = f;
+            else ((uint16_t*)C)[o] = qgo_f32_to_bf16(f);
+        }
+        free(av);
+    }
+}
+
+/* ------------------------------------------------------------------------
  * FP8 e4m3 block-128: "values drawn N(0,1) then scaled so that
  * each block's absmax maps to 448"; scale s = absmax / 448 so x ~ q * s.
  * A blocks are 1x128 along K, B blocks 128x128.

@@ -110,6 +110,8 @@ double   qgo_max_rel_err(const void* y, const void* r, uint64_t n, int kind);
 
 /* number of OpenMP threads the oracle uses */
 int qgo_threads(void);
+void qgo_gemm_dense(int kind, const void* A, const void* B, float alpha, int M, int N, int K,
+                    const int32_t* rows, int nrows, int out_type, void* C);
 void qgo_set_threads(int n);
 
 #ifdef __cplusplus

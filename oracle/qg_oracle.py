@@ -58,6 +58,7 @@ def lib() -> C.CDLL:
             "qgo_quant_fp8_rows": (None, [_P, C.c_int, C.c_int, _P, _P]),
             "qgo_quant_fp8_blocks": (None, [_P, C.c_int, C.c_int, _P, _P]),
             "qgo_gemm_fp8_b128": (None, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, _P]),
+            "qgo_gemm_dense": (None, [C.c_int, _P, _P, C.c_float, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, _P]),
             "qgo_nvfp4_global_scale": (C.c_float, [_P, C.c_uint64]),
             "qgo_quant_nvfp4": (None, [_P, C.c_int, C.c_int, C.c_float, _P, _P]),
             "qgo_gemm_nvfp4": (None, [_P, _P, C.c_float, _P, _P, C.c_float, C.c_int, C.c_int, C.c_int, _P,
@@ -164,6 +165,20 @@ def gemm_fp8(A, B, sa, sb, out_type: int = 0, rows=None):
     nr = M if r is None else len(r)
     C_ = np.empty((nr, N), dtype=np.uint16 if out_type == 0 else np.float32)
     lib().qgo_gemm_fp8_b128(_p(A), _p(B), _p(sa), _p(sb), M, N, K, _p(r), nr, out_type, _p(C_))
+    return C_
+
+
+def gemm_dense(kind: int, A, B, alpha: float = 1.0, out_type: int = 0, rows=None):
+    """Oracle tensor-furnace GEMM: kind 1 = bf16 (A, B as uint16 bits), 2 = e4m3 (uint8)."""
+    dt = np.uint16 if kind == 1 else np.uint8
+    A = np.ascontiguousarray(A, dtype=dt)
+    B = np.ascontiguousarray(B, dtype=dt)
+    M, K = A.shape
+    N = B.shape[0]
+    r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int32)
+    nr = M if r is None else len(r)
+    C_ = np.empty((nr, N), dtype=np.uint16 if out_type == 0 else np.float32)
+    lib().qgo_gemm_dense(kind, _p(A), _p(B), float(alpha), M, N, K, _p(r), nr, out_type, _p(C_))
     return C_
 
 

@@ -29,6 +29,8 @@ from .ops import (  # noqa: F401
     Workload,
     device_status,
     gemm_fp8_b128,
+    gemm_bf16,
+    gemm_e4m3,
     gemm_i8,
     gemm_nvfp4,
     gen_nvfp4,
@@ -45,7 +47,7 @@ from .ops import (  # noqa: F401
 
 __all__ = [
     "LIB_PATH", "BIN_PATH", "DECODE_BIN_PATH", "QGError", "load_library", "Workload", "device_status",
-    "gemm_i8", "gemm_fp8_b128", "gen_fp8", "gemm_nvfp4", "gen_nvfp4", "nvfp4_sf_bytes", "gemv_w4a16", "gemv_w4a16_workspace_bytes", "gen_w4a16", "gen_i8", "gen_uniform_f32", "gen_normal_f32", "verify_words",
+    "gemm_i8", "gemm_fp8_b128", "gemm_bf16", "gemm_e4m3", "gen_fp8", "gemm_nvfp4", "gen_nvfp4", "nvfp4_sf_bytes", "gemv_w4a16", "gemv_w4a16_workspace_bytes", "gen_w4a16", "gen_i8", "gen_uniform_f32", "gen_normal_f32", "verify_words",
     "QG_FMT_INT8", "QG_FMT_FP8", "QG_FMT_NVFP4", "QG_FMT_W4A16",
     "QG_OUT_BF16", "QG_OUT_F32", "QG_OUT_S32",
 ]

@@ -61,6 +61,8 @@ _SIGNATURES = {
     "qg_destroy": (None, [_V]),
     "qg_gemm_i8": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, _V, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gemm_fp8_b128": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
+    "qg_gemm_bf16": (C.c_int, [_V, _V, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
+    "qg_gemm_e4m3": (C.c_int, [_V, _V, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gen_fp8": (C.c_int, [_V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint32, _V]),
     "qg_gemm_nvfp4": (C.c_int, [_V, _V, _V, _V, C.c_float, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_nvfp4_sf_bytes": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_uint64)]),

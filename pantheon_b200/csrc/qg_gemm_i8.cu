@@ -28,8 +28,8 @@ namespace i8 {
 
 constexpr int BM = 128;
 constexpr int BN = 256;
-constexpr int BK = 128;            // int8 elements = bytes = one 128-byte swizzle row
-constexpr int UMMA_K = 32;         // K per tcgen05.mma kind::i8
+constexpr int BK = 128;            // bytes of K per stage = one 128-byte swizzle row (128 int8 / 64 bf16)
+constexpr int UMMA_K = 32;         // bytes of K per tcgen05.mma (32 int8 / 16 bf16 / 32 e4m3)
 constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK;   // 16 KB
 constexpr int B_BYTES = BN * BK;   // 32 KB
@@ -39,6 +39,32 @@ constexpr int TMEM_COLS = 2 * ACC_COLS;
 constexpr int THREADS = 256;
 constexpr int EPI_WARP0 = 4;
 constexpr int GROUP_M = 16;        // tile rasterisation: 16 row-tiles share B tiles in L2
+
+// Operand kinds these kernels run.  The mainloops are the same for all three
+// (128-byte K rows per stage, 32-byte K steps per MMA: 32 int8 / 16 bf16 / 32
+// e4m3 elements); the MMA instruction, its descriptor and the epilogue differ.
+//   KIND_I8    s8 x s8 -> s32, epilogue f32(acc) * sa[m] * sb[n], row checksums
+//   KIND_BF16  bf16 x bf16 -> f32, epilogue acc * alpha          (tensor furnace)
+//   KIND_E4M3  e4m3 x e4m3 -> f32, epilogue acc * alpha          (tensor furnace)
+enum : int { KIND_I8 = 0, KIND_BF16 = 1, KIND_E4M3 = 2 };
+__host__ __device__ constexpr int elem_bytes(int kind) { return kind == KIND_BF16 ? 2 : 1; }
+__host__ __device__ constexpr uint32_t kind_idesc(int kind, uint32_t M, uint32_t N) {
+    return kind == KIND_I8     ? make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, M, N)
+           : kind == KIND_BF16 ? make_idesc(/*f32*/ 1, /*bf16*/ 1, /*bf16*/ 1, M, N)
+                               : make_idesc(/*f32*/ 1, /*e4m3*/ 0, /*e4m3*/ 0, M, N);
+}
+template <int KIND>
+__device__ __forceinline__ void umma_kind(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if constexpr (KIND == KIND_I8) umma_i8(d, a, b, idesc, acc);
+    else if constexpr (KIND == KIND_BF16) umma_f16(d, a, b, idesc, acc);
+    else umma_f8(d, a, b, idesc, acc);
+}
+template <int KIND>
+__device__ __forceinline__ void umma_kind_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if constexpr (KIND == KIND_I8) umma_i8_pair(d, a, b, idesc, acc);
+    else if constexpr (KIND == KIND_BF16) umma_f16_pair(d, a, b, idesc, acc);
+    else umma_f8_pair(d, a, b, idesc, acc);
+}
 
 // Barrier block that follows the operand ring in shared memory.
 struct Barriers {
@@ -66,6 +92,7 @@ struct Params {
     void* C;
     uint32_t* row_cksum;
     DeviceStatus* status;
+    float alpha;            // output scale of the f32-accumulating kinds
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
@@ -84,7 +111,7 @@ __device__ __forceinline__ uint32_t cksum_weight(uint32_t m, uint32_t n) {
 
 // One 32-column chunk of an accumulator row: checksum fold, then the s32 /
 // dequantised f32 / bf16 store (ragged edges handled per element).
-template <int OUT>
+template <int KIND, int OUT>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, bool row_ok, float sam,
                                                const Params& p, uint32_t& ck) {
     if (!row_ok || n0 >= p.N) return;
@@ -108,7 +135,10 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
         return;
     }
     float f[32];
-    if (full_chunk) {
+    if constexpr (KIND != KIND_I8) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) f[i] = __fmul_rn(__uint_as_float(r[i]), p.alpha);
+    } else if (full_chunk) {
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
             const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sb + n0 + i));
@@ -154,7 +184,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
     }
 }
 
-template <int OUT>
+template <int KIND, int OUT>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -171,7 +201,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int tiles_m = (p.M + BM - 1) / BM;
     const int tiles_n = (p.N + BN - 1) / BN;
     const int tiles = tiles_m * tiles_n;
-    const int nk = (p.K + BK - 1) / BK;
+    const int nk = (p.K * elem_bytes(KIND) + BK - 1) / BK;   // 128-byte K blocks
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(&bars->full[s], 1); mbar_init(&bars->empty[s], 1); }
@@ -217,7 +247,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------ MMA issuer
-        constexpr uint32_t IDESC = make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, BM, BN);
+        constexpr uint32_t IDESC = kind_idesc(KIND, BM, BN);
         uint32_t stage = 0, phase = 0;
         bool ok = true, issued = false;
         int iter = 0;
@@ -236,7 +266,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 for (int k = 0; k < BK / UMMA_K; ++k) {
                     const uint64_t ad = make_sdesc_kmajor_sw128(a_addr + k * UMMA_K);
                     const uint64_t bd = make_sdesc_kmajor_sw128(b_addr + k * UMMA_K);
-                    umma_i8(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+                    umma_kind<KIND>(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
                 }
                 issued = true;
                 umma_commit(&bars->empty[stage]);
@@ -267,7 +297,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
             const int m = mt * BM + row;
             const bool row_ok = m < p.M;
-            const float sam = (OUT != QG_OUT_S32 && row_ok) ? __ldg(p.sa + m) : 0.0f;
+            const float sam = (KIND == KIND_I8 && OUT != QG_OUT_S32 && row_ok) ? __ldg(p.sa + m) : 0.0f;
             uint32_t ck = 0;
             const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * ACC_COLS;
 #pragma unroll 1
@@ -276,7 +306,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 __syncwarp();
                 tmem_ld_32x32b_x32(t_row + c, r);
                 tmem_ld_wait_regs(r);
-                epilogue_chunk<OUT>(r, m, nt * BN + c, row_ok, sam, p, ck);
+                epilogue_chunk<KIND, OUT>(r, m, nt * BN + c, row_ok, sam, p, ck);
             }
             tc_fence_before();
             mbar_arrive(&bars->tmem_empty[acc]);
@@ -315,7 +345,7 @@ constexpr int P_STAGE_BYTES = PA_BYTES + PB_BYTES;
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 constexpr int P_EPI_WARPS = 4;
 
-template <int OUT>
+template <int KIND, int OUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -341,7 +371,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     const int tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
     const int tiles_n = (p.N + BN - 1) / BN;
     const int tiles = tiles_m * tiles_n;
-    const int nk = (p.K + BK - 1) / BK;
+    const int nk = (p.K * elem_bytes(KIND) + BK - 1) / BK;   // 128-byte K blocks
     const int pair = blockIdx.x >> 1;
     const int pairs = gridDim.x >> 1;
 
@@ -391,7 +421,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
     } else if (warp == 1 && lane == 0 && leader) {
         // ------------------------------------------------------------ MMA issuer (even CTA)
-        constexpr uint32_t IDESC = make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, 2 * BM, BN);
+        constexpr uint32_t IDESC = kind_idesc(KIND, 2 * BM, BN);
         uint32_t stage = 0, phase = 0;
         bool ok = true, issued = false;
         int iter = 0;
@@ -408,8 +438,8 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 const uint32_t b_addr = smem_u32(sB + stage * PB_BYTES);
 #pragma unroll
                 for (int k = 0; k < BK / UMMA_K; ++k)
-                    umma_i8_pair(d_tmem, make_sdesc_kmajor_sw128(a_addr + k * UMMA_K),
-                                 make_sdesc_kmajor_sw128(b_addr + k * UMMA_K), IDESC, (kb | k) != 0 ? 1u : 0u);
+                    umma_kind_pair<KIND>(d_tmem, make_sdesc_kmajor_sw128(a_addr + k * UMMA_K),
+                                         make_sdesc_kmajor_sw128(b_addr + k * UMMA_K), IDESC, (kb | k) != 0 ? 1u : 0u);
                 issued = true;
                 const uint32_t e = smem_u32(&bars->empty[stage]);
                 umma_commit_pair(mapa_shared(e, 0));
@@ -443,7 +473,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             tc_fence_after();
             const int m = mt * 2 * BM + (int)rank * BM + row;
             const bool row_ok = m < p.M;
-            const float sam = (OUT != QG_OUT_S32 && row_ok) ? __ldg(p.sa + m) : 0.0f;
+            const float sam = (KIND == KIND_I8 && OUT != QG_OUT_S32 && row_ok) ? __ldg(p.sa + m) : 0.0f;
             uint32_t ck = 0;
             const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * ACC_COLS;
 #pragma unroll 1
@@ -452,7 +482,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 __syncwarp();
                 tmem_ld_32x32b_x32(t_row + c, r);
                 tmem_ld_wait_regs(r);
-                epilogue_chunk<OUT>(r, m, nt * BN + c, row_ok, sam, p, ck);
+                epilogue_chunk<KIND, OUT>(r, m, nt * BN + c, row_ok, sam, p, ck);
             }
             tc_fence_before();
             __syncwarp();
@@ -471,20 +501,19 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
 }
 
-template <int OUT>
-static int launch(const void* A, const void* B, const float* sa, const float* sb, void* C, uint32_t* cksum,
-                  int M, int N, int K, cudaStream_t stream) {
+template <int KIND, int OUT>
+static int launch(const void* A, const void* B, const float* sa, const float* sb, float alpha, void* C,
+                  uint32_t* cksum, int M, int N, int K, cudaStream_t stream) {
     DeviceInfo* info = nullptr;
     int rc = current_device_info(&info);
     if (rc) return rc;
     DeviceStatus* status = nullptr;
     if ((rc = device_status_ptr(&status))) return rc;
 
-    CUtensorMap tmA, tmB;
-    if ((rc = make_tmap_2d(&tmA, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)M, (uint64_t)K, BK, BM,
-                           CU_TENSOR_MAP_SWIZZLE_128B)))
-        return rc;
-    if ((rc = make_tmap_2d(&tmB, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)N, (uint64_t)K, BK, BN,
+    // operands as byte matrices: rows of K * elem_bytes bytes
+    const uint64_t kb = (uint64_t)K * elem_bytes(KIND);
+    CUtensorMap tmA;
+    if ((rc = make_tmap_2d(&tmA, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, kb, (uint64_t)M, kb, BK, BM,
                            CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
 
@@ -492,22 +521,19 @@ static int launch(const void* A, const void* B, const float* sa, const float* sb
     int dev = 0;
     QG_CUDA(cudaGetDevice(&dev));
     if (!attr_set[dev & 63]) {
-        QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<QG_OUT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<QG_OUT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<QG_OUT_S32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        QG_CUDA(cudaFuncSetAttribute(gemm_i8_pair_kernel<QG_OUT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
-        QG_CUDA(cudaFuncSetAttribute(gemm_i8_pair_kernel<QG_OUT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
-        QG_CUDA(cudaFuncSetAttribute(gemm_i8_pair_kernel<QG_OUT_S32>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<KIND, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(gemm_i8_pair_kernel<KIND, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     P_SMEM_BYTES));
         attr_set[dev & 63] = true;
     }
     if (cksum) QG_CUDA(cudaMemsetAsync(cksum, 0, sizeof(uint32_t) * (size_t)M, stream));
 
-    Params p{M, N, K, sa, sb, C, cksum, status};
+    Params p{M, N, K, sa, sb, C, cksum, status, alpha};
     if (M >= 2 * BM && info->sm_count >= 2) {
         // CTA pairs: each CTA's B box is half a tile high
         CUtensorMap tmBh;
-        if ((rc = make_tmap_2d(&tmBh, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)N, (uint64_t)K, BK,
-                               BN / 2, CU_TENSOR_MAP_SWIZZLE_128B)))
+        if ((rc = make_tmap_2d(&tmBh, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, kb, (uint64_t)N, kb, BK, BN / 2,
+                               CU_TENSOR_MAP_SWIZZLE_128B)))
             return rc;
         const int tiles2 = ceil_div(M, 2 * BM) * ceil_div(N, BN);
         // persistent pairs: only as many as can be resident at once (a pair needs
@@ -519,17 +545,21 @@ static int launch(const void* A, const void* B, const float* sa, const float* sb
             lc.blockDim = dim3(THREADS);
             lc.dynamicSmemBytes = P_SMEM_BYTES;
             int n = 0;
-            QG_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_i8_pair_kernel<QG_OUT_BF16>, &lc));
+            QG_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_i8_pair_kernel<KIND, OUT>, &lc));
             resident[dev & 63] = n > 0 ? n : 1;
         }
         const int pairs = tiles2 < resident[dev & 63] ? tiles2 : resident[dev & 63];
-        gemm_i8_pair_kernel<OUT><<<2 * pairs, THREADS, P_SMEM_BYTES, stream>>>(tmA, tmBh, p);
+        gemm_i8_pair_kernel<KIND, OUT><<<2 * pairs, THREADS, P_SMEM_BYTES, stream>>>(tmA, tmBh, p);
         QG_CUDA(cudaGetLastError());
         return QG_OK;
     }
+    CUtensorMap tmB;
+    if ((rc = make_tmap_2d(&tmB, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, kb, (uint64_t)N, kb, BK, BN,
+                           CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
     const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
     const int grid = tiles < info->sm_count ? tiles : info->sm_count;
-    gemm_i8_kernel<OUT><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, p);
+    gemm_i8_kernel<KIND, OUT><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, p);
     QG_CUDA(cudaGetLastError());
     return QG_OK;
 }
@@ -547,11 +577,28 @@ int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* 
     const float* fsb = static_cast<const float*>(sb);
     uint32_t* ck = static_cast<uint32_t*>(row_cksum);
     switch (out_type) {
-        case QG_OUT_BF16: return i8::launch<QG_OUT_BF16>(A, B, fsa, fsb, C, ck, M, N, K, stream);
-        case QG_OUT_F32: return i8::launch<QG_OUT_F32>(A, B, fsa, fsb, C, ck, M, N, K, stream);
-        case QG_OUT_S32: return i8::launch<QG_OUT_S32>(A, B, fsa, fsb, C, ck, M, N, K, stream);
+        case QG_OUT_BF16: return i8::launch<i8::KIND_I8, QG_OUT_BF16>(A, B, fsa, fsb, 1.0f, C, ck, M, N, K, stream);
+        case QG_OUT_F32: return i8::launch<i8::KIND_I8, QG_OUT_F32>(A, B, fsa, fsb, 1.0f, C, ck, M, N, K, stream);
+        case QG_OUT_S32: return i8::launch<i8::KIND_I8, QG_OUT_S32>(A, B, fsa, fsb, 1.0f, C, ck, M, N, K, stream);
         default: set_error("qg_gemm_i8: unknown out_type %d", out_type); return QG_ERR_ARG;
     }
+}
+
+// Tensor-furnace GEMMs: C = alpha * A B^T with f32 accumulation, bf16 or e4m3 operands.
+int gemm_dense(int kind, const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
+               cudaStream_t stream) {
+    const char* name = kind == i8::KIND_BF16 ? "qg_gemm_bf16" : "qg_gemm_e4m3";
+    QG_CHECK_ARG(A && B && C, "%s: null operand or output", name);
+    QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "%s: empty shape %dx%dx%d", name, M, N, K);
+    QG_CHECK_ARG((K * i8::elem_bytes(kind)) % 16 == 0, "%s: K=%d: rows must be a multiple of 16 bytes", name, K);
+    QG_CHECK_ARG(out_type == QG_OUT_BF16 || out_type == QG_OUT_F32, "%s: out_type %d (bf16 or f32)", name, out_type);
+    if (kind == i8::KIND_BF16)
+        return out_type == QG_OUT_BF16
+                   ? i8::launch<i8::KIND_BF16, QG_OUT_BF16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream)
+                   : i8::launch<i8::KIND_BF16, QG_OUT_F32>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
+    return out_type == QG_OUT_BF16
+               ? i8::launch<i8::KIND_E4M3, QG_OUT_BF16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream)
+               : i8::launch<i8::KIND_E4M3, QG_OUT_F32>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
 }
 
 } // namespace qg
@@ -559,4 +606,14 @@ int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* 
 extern "C" int qg_gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type,
                           void* row_checksums, int M, int N, int K, void* stream) {
     return qg::gemm_i8(A, B, sa, sb, C, out_type, row_checksums, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qg_gemm_bf16(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
+                            void* stream) {
+    return qg::gemm_dense(qg::i8::KIND_BF16, A, B, alpha, C, out_type, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qg_gemm_e4m3(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
+                            void* stream) {
+    return qg::gemm_dense(qg::i8::KIND_E4M3, A, B, alpha, C, out_type, M, N, K, static_cast<cudaStream_t>(stream));
 }

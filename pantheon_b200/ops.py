@@ -82,6 +82,32 @@ def gemm_fp8_b128(A: torch.Tensor, B: torch.Tensor, sa: torch.Tensor, sb: torch.
     return out
 
 
+def gemm_bf16(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: int = QG_OUT_BF16,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = alpha * A @ B^T (fp32 accumulate) on the tcgen05 bf16 path: A bf16 [M,K], B bf16 [N,K]."""
+    _require_cuda(A, B)
+    M, K = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=_OUT_DTYPES[out_type], device=A.device)
+    check("qg_gemm_bf16", load_library().qg_gemm_bf16(_ptr(A), _ptr(B), float(alpha), _ptr(out), out_type, M, N, K,
+                                                       _stream(A.device)))
+    return out
+
+
+def gemm_e4m3(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: int = QG_OUT_BF16,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = alpha * A @ B^T (fp32 accumulate) on the tcgen05 e4m3 path: A, B e4m3 bytes [M,K] / [N,K]."""
+    _require_cuda(A, B)
+    M, K = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=_OUT_DTYPES[out_type], device=A.device)
+    check("qg_gemm_e4m3", load_library().qg_gemm_e4m3(_ptr(A), _ptr(B), float(alpha), _ptr(out), out_type, M, N, K,
+                                                       _stream(A.device)))
+    return out
+
+
 def gen_fp8(M: int, N: int, K: int, seed: int, tid0: int = 0, device="cuda"):
     """The FP8 workload's generated operands (A, B as uint8 e4m3 bytes; sa, sb fp32)."""
     A = torch.empty((M, K), dtype=torch.uint8, device=device)
