@@ -56,11 +56,18 @@ extern "C" {
 #define QG_FMT_FP8    1   /* FP8 e4m3, 1x128 (A) and 128x128 (B) fp32 block scales */
 #define QG_FMT_NVFP4  2   /* e2m1 + ue4m3 per 16 along K + fp32 per-tensor scale   */
 #define QG_FMT_W4A16  3   /* bf16 activations x int4 weights, fp16 scale/zero per 128 */
+/* Dense tensor-furnace formats (the mma_virus workload; C = A B^T, fp32 accumulate,
+ * operands uniform on [-1, 1) rounded to the format). */
+#define QG_FMT_BF16   4   /* bf16 x bf16 */
+#define QG_FMT_FP16   5   /* fp16 x fp16 */
+#define QG_FMT_TF32   6   /* tf32 x tf32 (stored as fp32 words) */
+#define QG_FMT_E4M3   7   /* e4m3 x e4m3, unscaled */
 
 /* Output element types. */
 #define QG_OUT_BF16   0
 #define QG_OUT_F32    1
 #define QG_OUT_S32    2   /* raw INT32 accumulators (INT8 only) */
+#define QG_OUT_F16    3   /* fp16 (dense formats only) */
 
 /* Workload configuration for a context. Zero fields take the format default. */
 typedef struct qg_cfg {
@@ -150,6 +157,11 @@ QG_API int  qg_synchronize(qg_ctx* ctx);
  * ai_workload_template.h:359). */
 QG_API int  qg_mem_info(int device, uint64_t* free_bytes, uint64_t* total_bytes);
 
+/* PCI bus id of `device` ("0000:1b:00.0"), for matching the device in NVML
+ * (CUDA and NVML ordinals can differ).  Replaces: the cudaDeviceGetPCIBusId
+ * call of the energy meter (kernels/common/vendor_gemm.h:383-404). */
+QG_API int  qg_pci_bus_id(int device, char* buf, int len);
+
 /* QG_ABI_VERSION of the loaded library. */
 QG_API int  qg_abi_version(void);
 
@@ -175,12 +187,19 @@ QG_API int  qg_gemm_i8(const void* A, const void* B, const void* sa, const void*
 
 /* Tensor-furnace GEMMs (the mma_virus workload): C = out(alpha * A B^T) with
  * fp32 accumulation on the tcgen05 tensor cores, A [M,K], B [N,K] K-contiguous;
- * qg_gemm_bf16: bf16 operands (K % 8 == 0); qg_gemm_e4m3: e4m3 bytes (K % 16 == 0);
- * out_type QG_OUT_BF16 or QG_OUT_F32.  M >= 256 runs on CTA pairs.
- * Replaces: the cuBLASLt bf16 / fp8 GEMM of the tensor furnace
+ *   qg_gemm_bf16: bf16 operands (K % 8 == 0)
+ *   qg_gemm_f16:  fp16 operands (K % 8 == 0)
+ *   qg_gemm_tf32: fp32 words read as tf32 (the MMA uses the top 19 bits; K % 4 == 0)
+ *   qg_gemm_e4m3: e4m3 bytes (K % 16 == 0)
+ * out_type QG_OUT_BF16, QG_OUT_F16 or QG_OUT_F32.  M >= 256 runs on CTA pairs.
+ * Replaces: the cuBLASLt bf16 / fp16 / tf32 / fp8 GEMMs of the tensor furnace
  *   (kernels/common/vendor_gemm.h:279-360, driven by kernels/mma_virus/mma_virus.cpp:264-282)
  *   and its WMMA fallback (mma_virus.cpp:57-135). */
 QG_API int  qg_gemm_bf16(const void* A, const void* B, float alpha, void* C, int out_type,
+                         int M, int N, int K, void* stream);
+QG_API int  qg_gemm_f16(const void* A, const void* B, float alpha, void* C, int out_type,
+                        int M, int N, int K, void* stream);
+QG_API int  qg_gemm_tf32(const void* A, const void* B, float alpha, void* C, int out_type,
                          int M, int N, int K, void* stream);
 QG_API int  qg_gemm_e4m3(const void* A, const void* B, float alpha, void* C, int out_type,
                          int M, int N, int K, void* stream);
@@ -266,6 +285,13 @@ QG_API int  qg_gen_uniform_f32(void* out, uint64_t n, float lo, float hi,
                         uint64_t seed, uint32_t tensor_id, void* stream);
 /* out[i] = standard normal deviate (seed, tensor_id, i), fp32. */
 QG_API int  qg_gen_normal_f32(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream);
+/* Dense tensor-furnace operands (format QG_FMT_BF16 / FP16 / TF32 / E4M3):
+ * out[i] = fmt_rn(j / 32768 - 1), j = top 16 bits of hash(seed, tensor_id, i);
+ * bf16 / fp16 / e4m3 (saturating) round to nearest even; tf32 is the fp32
+ * word rounded to nearest even at 10 mantissa bits, low 13 bits zero.
+ * Replaces: pantheon_gemm_fill (kernels/common/vendor_gemm.h:184-191), whose
+ * operands are uniform on [-1, 1) in steps of 2^-15. */
+QG_API int  qg_gen_dense(int format, void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream);
 /* FP8 operands of configs[2]: values N(0,1) (A: tensor tid0, B: tid0+2), each
  * block (A 1x128, B 128x128) scaled so its absmax maps to 448:
  * q = e4m3_rn_satfinite(x * (448/absmax)), scale = absmax/448 (fp32). */

@@ -297,11 +297,52 @@ void qgo_gemm_i8(const int8_t* A, const int8_t* B, const float* sa, const float*
 }
 
 /* ------------------------------------------------------------------------
- * Tensor-furnace GEMMs (the mma_virus workload): C = alpha * A B^T with
- * bf16 (kind 1) or e4m3 (kind 2) operands; the exact products are summed in
- * double, rounded to fp32, scaled by alpha in fp32, then stored as fp32 or
- * bf16.  Rows rows[0..nrows) of C (all when rows is NULL), compact.
+ * Tensor-furnace operands (the mma_virus workload; the reference fills them
+ * uniform on [-1, 1) in steps of 2^-15, kernels/common/vendor_gemm.h:184-191):
+ * v = j / 32768 - 1 with j the top 16 bits of the element's hash (exact in
+ * fp32), rounded to the operand format.  tf32 is kept as an fp32 word rounded
+ * to nearest even at 10 mantissa bits with the low 13 bits cleared.
  * ---------------------------------------------------------------------- */
+uint32_t qgo_f32_to_tf32_bits(float x) {
+    uint32_t u = f2u(x);
+    if (isnan(x)) return u | 0x00400000u;
+    u += 0xFFFu + ((u >> 13) & 1u);
+    return u & 0xFFFFE000u;
+}
+
+float qgo_dense_value(uint64_t h) {
+    return (float)(uint32_t)(h >> 48) * 3.0517578125e-05f - 1.0f;
+}
+
+void qgo_gen_dense(int fmt, void* out, uint64_t n, uint64_t seed, uint32_t tensor_id) {
+    #pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)n; ++i) {
+        float v = qgo_dense_value(qgo_hash64(seed, tensor_id, (uint64_t)i));
+        switch (fmt) {
+            case QGO_FMT_BF16: ((uint16_t*)out)[i] = qgo_f32_to_bf16(v); break;
+            case QGO_FMT_FP16: ((uint16_t*)out)[i] = qgo_f32_to_f16(v); break;
+            case QGO_FMT_TF32: ((uint32_t*)out)[i] = qgo_f32_to_tf32_bits(v); break;
+            default: ((uint8_t*)out)[i] = qgo_f32_to_e4m3(v); break;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------
+ * Tensor-furnace GEMMs: C = alpha * A B^T with bf16 (kind 1), e4m3 (kind 2),
+ * fp16 (kind 3) or tf32 (kind 4, fp32 words holding tf32 values) operands;
+ * the exact products are summed in double, rounded to fp32, scaled by alpha
+ * in fp32, then stored as bf16 (out_type 0), fp32 (1) or fp16 (3).  Rows
+ * rows[0..nrows) of C (all when rows is NULL), compact.
+ * ---------------------------------------------------------------------- */
+static float dense_operand(int kind, const void* X, size_t i, const float* lut) {
+    switch (kind) {
+        case 1: return qgo_bf16_to_f32(((const uint16_t*)X)[i]);
+        case 3: return qgo_f16_to_f32(((const uint16_t*)X)[i]);
+        case 4: return u2f(((const uint32_t*)X)[i]);
+        default: return lut[((const uint8_t*)X)[i]];
+    }
+}
+
 void qgo_gemm_dense(int kind, const void* A, const void* B, float alpha, int M, int N, int K,
                     const int32_t* rows, int nrows, int out_type, void* C) {
     if (!rows) nrows = M;
@@ -310,21 +351,16 @@ void qgo_gemm_dense(int kind, const void* A, const void* B, float alpha, int M, 
     #pragma omp parallel for schedule(dynamic, 1)
     for (int r = 0; r < nrows; ++r) {
         int m = rows ? rows[r] : r;
-        float* av = (float*)malloc(sizeof(float) * (size_t)K);
-        for (int k = 0; k < K; ++k)
-            av[k] = kind == 1 ? qgo_bf16_to_f32(((const uint16_t*)A)[(size_t)m * K + k])
-                              : lut[((const uint8_t*)A)[(size_t)m * K + k]];
+        double* av = (double*)malloc(sizeof(double) * (size_t)K);
+        for (int k = 0; k < K; ++k) av[k] = dense_operand(kind, A, (size_t)m * K + k, lut);
         for (int n = 0; n < N; ++n) {
             double s = 0.0;
-            for (int k = 0; k < K; ++k) {
-                float b = kind == 1 ? qgo_bf16_to_f32(((const uint16_t*)B)[(size_t)n * K + k])
-                                    : lut[((const uint8_t*)B)[(size_t)n * K + k]];
-                s += (double)av[k] * (double)b;
-            }
+            for (int k = 0; k < K; ++k) s += av[k] * (double)dense_operand(kind, B, (size_t)n * K + k, lut);
             float f = (float)s;
             f = f * alpha;
             size_t o = (size_t)r * N + n;
             if (out_type == 1) ((float*)C)[o] = f;
+            else if (out_type == 3) ((uint16_t*)C)[o] = qgo_f32_to_f16(f);
             else ((uint16_t*)C)[o] = qgo_f32_to_bf16(f);
         }
         free(av);

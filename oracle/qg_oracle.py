@@ -59,6 +59,9 @@ def lib() -> C.CDLL:
             "qgo_quant_fp8_blocks": (None, [_P, C.c_int, C.c_int, _P, _P]),
             "qgo_gemm_fp8_b128": (None, [_P, _P, _P, _P, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, _P]),
             "qgo_gemm_dense": (None, [C.c_int, _P, _P, C.c_float, C.c_int, C.c_int, C.c_int, _P, C.c_int, C.c_int, _P]),
+            "qgo_gen_dense": (None, [C.c_int, _P, C.c_uint64, C.c_uint64, C.c_uint32]),
+            "qgo_f32_to_tf32_bits": (C.c_uint32, [C.c_float]),
+            "qgo_dense_value": (C.c_float, [C.c_uint64]),
             "qgo_nvfp4_global_scale": (C.c_float, [_P, C.c_uint64]),
             "qgo_quant_nvfp4": (None, [_P, C.c_int, C.c_int, C.c_float, _P, _P]),
             "qgo_gemm_nvfp4": (None, [_P, _P, C.c_float, _P, _P, C.c_float, C.c_int, C.c_int, C.c_int, _P,
@@ -168,16 +171,40 @@ def gemm_fp8(A, B, sa, sb, out_type: int = 0, rows=None):
     return C_
 
 
+# Dense (tensor-furnace) formats: workload format id -> (GEMM kind, storage dtype).
+FMT_BF16, FMT_FP16, FMT_TF32, FMT_E4M3 = 4, 5, 6, 7
+KIND_BF16, KIND_E4M3, KIND_F16, KIND_TF32 = 1, 2, 3, 4
+DENSE_FORMATS = {FMT_BF16: (KIND_BF16, np.uint16), FMT_FP16: (KIND_F16, np.uint16),
+                 FMT_TF32: (KIND_TF32, np.uint32), FMT_E4M3: (KIND_E4M3, np.uint8)}
+_KIND_DTYPE = {KIND_BF16: np.uint16, KIND_F16: np.uint16, KIND_TF32: np.uint32, KIND_E4M3: np.uint8}
+_OUT_DTYPE = {0: np.uint16, 1: np.float32, 3: np.uint16}
+
+
+def gen_dense(fmt: int, n: int, seed: int, tensor_id: int):
+    """The dense workload's operand stream: format `fmt` bit patterns (uint16 / uint32 / uint8)."""
+    out = np.empty(n, dtype=DENSE_FORMATS[fmt][1])
+    lib().qgo_gen_dense(fmt, _p(out), n, seed, tensor_id)
+    return out
+
+
+def dense_operands(fmt: int, M: int, N: int, K: int, seed: int, copy: int = 0):
+    """A [M,K] and B [N,K] of copy `copy` of a dense workload (tensor ids 8*copy, 8*copy+1)."""
+    b = 8 * copy
+    return gen_dense(fmt, M * K, seed, b).reshape(M, K), gen_dense(fmt, N * K, seed, b + 1).reshape(N, K)
+
+
 def gemm_dense(kind: int, A, B, alpha: float = 1.0, out_type: int = 0, rows=None):
-    """Oracle tensor-furnace GEMM: kind 1 = bf16 (A, B as uint16 bits), 2 = e4m3 (uint8)."""
-    dt = np.uint16 if kind == 1 else np.uint8
+    """Oracle tensor-furnace GEMM C = alpha * A B^T: kind 1 = bf16, 3 = fp16 (A, B as uint16
+    bits), 4 = tf32 (uint32 fp32 words), 2 = e4m3 (uint8); out_type 0 = bf16 bits, 1 = f32,
+    3 = fp16 bits."""
+    dt = _KIND_DTYPE[kind]
     A = np.ascontiguousarray(A, dtype=dt)
     B = np.ascontiguousarray(B, dtype=dt)
     M, K = A.shape
     N = B.shape[0]
     r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int32)
     nr = M if r is None else len(r)
-    C_ = np.empty((nr, N), dtype=np.uint16 if out_type == 0 else np.float32)
+    C_ = np.empty((nr, N), dtype=_OUT_DTYPE[out_type])
     lib().qgo_gemm_dense(kind, _p(A), _p(B), float(alpha), M, N, K, _p(r), nr, out_type, _p(C_))
     return C_
 

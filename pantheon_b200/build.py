@@ -28,6 +28,7 @@ OBJ_DIR = ROOT / "_build" / "obj"
 LIB = LIB_DIR / "libpantheon_qgemm.so"
 BIN = LIB_DIR / "quantized_gemm"
 DECODE_BIN = LIB_DIR / "llm_decode"
+MMA_BIN = LIB_DIR / "mma_virus"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
@@ -83,7 +84,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         _run([cc, *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs),
               "-Xlinker", "--exclude-libs,ALL"], verbose)
     main = CSRC / "quantized_gemm_main.cpp"
-    for out, defs in ((BIN, []), (DECODE_BIN, ["-DQG_DECODE_BINARY"])):
+    for out, defs in ((BIN, []), (DECODE_BIN, ["-DQG_DECODE_BINARY"]), (MMA_BIN, ["-DQG_MMA_VIRUS_BINARY"])):
         if force or _stale(out, [main, LIB, ROOT / "include" / "pantheon_qgemm.h"]):
             _run(["g++", "-O2", "-std=c++17", *defs, f"-I{ROOT / 'include'}", f"-I{cuda_include()}", str(main),
                   "-o", str(out), f"-L{LIB_DIR}", "-lpantheon_qgemm", "-ldl", "-Wl,-rpath,$ORIGIN"], verbose)

@@ -58,6 +58,8 @@ void free_ctx_memory(qg_ctx* c) {
     c->log = nullptr;
 }
 
+uint64_t out_alloc_bytes(const qg::Layout& L) { return (L.out_bytes + 15) / 16 * 16; }
+
 int alloc(void** p, uint64_t bytes) {
     if (bytes == 0) { *p = nullptr; return QG_OK; }
     QG_CUDA(cudaMalloc(p, (size_t)bytes));
@@ -76,7 +78,7 @@ int qg_required_bytes(const qg_cfg* cfg, uint64_t* bytes) {
     const int copies = cfg->copies > 0 ? cfg->copies : 1;
     uint64_t per = 0;
     for (int i = 0; i < L.n_ops; ++i) per += L.op_bytes[i];
-    per += 2 * L.out_bytes + 2 * L.cksum_bytes + L.scratch_bytes;
+    per += 2 * out_alloc_bytes(L) + 2 * L.cksum_bytes + L.scratch_bytes;
     *bytes = per * (uint64_t)copies + 4096;
     return QG_OK;
 }
@@ -106,8 +108,13 @@ int qg_create(qg_ctx** out, int device, const qg_cfg* cfg) {
     for (auto& cp : c->copies) {
         for (int i = 0; i < L.n_ops; ++i)
             if ((rc = alloc(&cp.op[i], L.op_bytes[i]))) goto oom;
-        if ((rc = alloc(&cp.out, L.out_bytes))) goto oom;
-        if ((rc = alloc(&cp.golden, L.out_bytes))) goto oom;
+        // Outputs are padded to whole 16-byte groups and zeroed, so the verifier
+        // can compare whole 32-bit words even when a 2-byte output has an odd
+        // element count (the padding stays zero in both copies).
+        if ((rc = alloc(&cp.out, out_alloc_bytes(L)))) goto oom;
+        if ((rc = alloc(&cp.golden, out_alloc_bytes(L)))) goto oom;
+        if (cp.out && cudaMemset(cp.out, 0, out_alloc_bytes(L)) != cudaSuccess) { rc = QG_ERR_CUDA; goto oom; }
+        if (cp.golden && cudaMemset(cp.golden, 0, out_alloc_bytes(L)) != cudaSuccess) { rc = QG_ERR_CUDA; goto oom; }
         if ((rc = alloc(&cp.cksum, L.cksum_bytes))) goto oom;
         if ((rc = alloc(&cp.golden_cksum, L.cksum_bytes))) goto oom;
         if ((rc = alloc(&cp.scratch, L.scratch_bytes))) goto oom;
@@ -186,7 +193,7 @@ int qg_verify(qg_ctx* c, uint64_t* mismatches) {
     CTX_CUDA(c, cudaDeviceSynchronize());
     CTX_CUDA(c, cudaMemsetAsync(c->counters, 0, 2 * sizeof(unsigned long long), c->stream));
     for (auto& cp : c->copies) {
-        int rc = qg::verify_words(cp.out, cp.golden, c->layout.out_bytes / 4, c->counters, c->log, c->log_cap, c->stream);
+        int rc = qg::verify_words(cp.out, cp.golden, (c->layout.out_bytes + 3) / 4, c->counters, c->log, c->log_cap, c->stream);
         if (rc) return fail(c, rc);
         if (c->layout.cksum_bytes) {
             rc = qg::verify_words(cp.cksum, cp.golden_cksum, c->layout.cksum_bytes / 4, c->counters, c->log, c->log_cap,
@@ -292,6 +299,12 @@ int qg_mem_info(int device, uint64_t* free_bytes, uint64_t* total_bytes) {
     QG_CUDA(cudaMemGetInfo(&f, &t));
     *free_bytes = f;
     *total_bytes = t;
+    return QG_OK;
+}
+
+int qg_pci_bus_id(int device, char* buf, int len) {
+    QG_CHECK_ARG(buf && len >= 16, "qg_pci_bus_id: buffer of at least 16 bytes required");
+    QG_CUDA(cudaDeviceGetPCIBusId(buf, len, device));
     return QG_OK;
 }
 

@@ -2,13 +2,22 @@
 //
 // Format defaults are the workload configurations: INT8 W8A8 at M=N=K=8192
 // with bf16 output; FP8 block-128 at M=N=8192, K=16384; NVFP4 at 16384^3;
-// W4A16 at M=1, K=8192, N=28672.  Tensor ids give every tensor of every copy
+// W4A16 at M=1, K=8192, N=28672; the dense tensor-furnace formats at 8192^3.  Tensor ids give every tensor of every copy
 // its own generator stream: id = 8 * copy + slot.
 #include "qg_formats.cuh"
 
 namespace qg {
 
-static int out_elem_bytes(int out_type) { return out_type == QG_OUT_BF16 ? 2 : 4; }
+static int out_elem_bytes(int out_type) { return (out_type == QG_OUT_BF16 || out_type == QG_OUT_F16) ? 2 : 4; }
+
+uint32_t dense_elem_bytes(int fmt) {
+    switch (fmt) {
+        case QG_FMT_BF16: case QG_FMT_FP16: return 2;
+        case QG_FMT_TF32: return 4;
+        case QG_FMT_E4M3: return 1;
+        default: return 0;
+    }
+}
 
 int layout_for(const qg_cfg& cfg, Layout* L) {
     Layout l;
@@ -85,6 +94,27 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
             l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes);
             break;
         }
+        case QG_FMT_BF16:
+        case QG_FMT_FP16:
+        case QG_FMT_TF32:
+        case QG_FMT_E4M3: {
+            // The tensor furnace: C = A B^T at 8192^3 by default, as the
+            // reference's vendor GEMM (vendor_gemm.h:38).
+            const uint32_t eb = dense_elem_bytes(cfg.format);
+            l.M = cfg.m > 0 ? cfg.m : 8192;
+            l.N = cfg.n > 0 ? cfg.n : 8192;
+            l.K = cfg.k > 0 ? cfg.k : 8192;
+            QG_CHECK_ARG(((uint64_t)l.K * eb) % 16 == 0, "dense GEMM: K=%d must make 16-byte rows", l.K);
+            QG_CHECK_ARG(l.out_type == QG_OUT_BF16 || l.out_type == QG_OUT_F16 || l.out_type == QG_OUT_F32,
+                         "dense GEMM: bad out_type %d", l.out_type);
+            l.n_ops = 2;
+            l.op_bytes[0] = (uint64_t)l.M * l.K * eb;
+            l.op_bytes[1] = (uint64_t)l.N * l.K * eb;
+            l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
+            l.ops = 2.0 * l.M * (double)l.N * l.K;
+            l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.out_bytes);
+            break;
+        }
         default:
             set_error("format %d is not available in this build", cfg.format);
             return QG_ERR_ARG;
@@ -120,6 +150,14 @@ int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_inde
         case QG_FMT_W4A16:
             if (cp.scratch) QG_CUDA(cudaMemsetAsync(cp.scratch, 0, L.scratch_bytes, s));
             return gen_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], L.M, L.N, L.K, seed, base, s);
+        case QG_FMT_BF16:
+        case QG_FMT_FP16:
+        case QG_FMT_TF32:
+        case QG_FMT_E4M3: {
+            const uint32_t eb = dense_elem_bytes(cfg.format);
+            if ((rc = gen_dense(cfg.format, cp.op[0], L.op_bytes[0] / eb, seed, base + 0, s))) return rc;
+            return gen_dense(cfg.format, cp.op[1], L.op_bytes[1] / eb, seed, base + 1, s);
+        }
         default:
             set_error("format %d is not available in this build", cfg.format);
             return QG_ERR_ARG;
@@ -138,6 +176,11 @@ int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaS
         case QG_FMT_W4A16:
             return gemv_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, cp.scratch,
                               L.scratch_bytes, s);
+        case QG_FMT_BF16:
+        case QG_FMT_FP16:
+        case QG_FMT_TF32:
+        case QG_FMT_E4M3:
+            return gemm_dense_format(cfg.format, cp.op[0], cp.op[1], 1.0f, cp.out, L.out_type, L.M, L.N, L.K, s);
         default:
             set_error("format %d is not available in this build", cfg.format);
             return QG_ERR_ARG;

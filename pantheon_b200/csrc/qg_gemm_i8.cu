@@ -22,6 +22,7 @@
 #include "qg_common.cuh"
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 namespace qg {
 namespace i8 {
@@ -40,29 +41,39 @@ constexpr int THREADS = 256;
 constexpr int EPI_WARP0 = 4;
 constexpr int GROUP_M = 16;        // tile rasterisation: 16 row-tiles share B tiles in L2
 
-// Operand kinds these kernels run.  The mainloops are the same for all three
-// (128-byte K rows per stage, 32-byte K steps per MMA: 32 int8 / 16 bf16 / 32
-// e4m3 elements); the MMA instruction, its descriptor and the epilogue differ.
+// Operand kinds these kernels run.  The mainloops are the same for all of
+// them (128-byte K rows per stage, 32-byte K steps per MMA: 32 int8 / 16
+// bf16 or fp16 / 8 tf32 / 32 e4m3 elements); the MMA instruction, its
+// descriptor and the epilogue differ.
 //   KIND_I8    s8 x s8 -> s32, epilogue f32(acc) * sa[m] * sb[n], row checksums
 //   KIND_BF16  bf16 x bf16 -> f32, epilogue acc * alpha          (tensor furnace)
 //   KIND_E4M3  e4m3 x e4m3 -> f32, epilogue acc * alpha          (tensor furnace)
-enum : int { KIND_I8 = 0, KIND_BF16 = 1, KIND_E4M3 = 2 };
-__host__ __device__ constexpr int elem_bytes(int kind) { return kind == KIND_BF16 ? 2 : 1; }
+//   KIND_F16   fp16 x fp16 -> f32, epilogue acc * alpha          (tensor furnace)
+//   KIND_TF32  tf32 x tf32 -> f32, epilogue acc * alpha          (tensor furnace;
+//              operands are fp32 words, the MMA reads their top 19 bits)
+enum : int { KIND_I8 = 0, KIND_BF16 = 1, KIND_E4M3 = 2, KIND_F16 = 3, KIND_TF32 = 4 };
+__host__ __device__ constexpr int elem_bytes(int kind) {
+    return (kind == KIND_BF16 || kind == KIND_F16) ? 2 : kind == KIND_TF32 ? 4 : 1;
+}
 __host__ __device__ constexpr uint32_t kind_idesc(int kind, uint32_t M, uint32_t N) {
     return kind == KIND_I8     ? make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, M, N)
            : kind == KIND_BF16 ? make_idesc(/*f32*/ 1, /*bf16*/ 1, /*bf16*/ 1, M, N)
+           : kind == KIND_F16  ? make_idesc(/*f32*/ 1, /*f16*/ 0, /*f16*/ 0, M, N)
+           : kind == KIND_TF32 ? make_idesc(/*f32*/ 1, /*tf32*/ 2, /*tf32*/ 2, M, N)
                                : make_idesc(/*f32*/ 1, /*e4m3*/ 0, /*e4m3*/ 0, M, N);
 }
 template <int KIND>
 __device__ __forceinline__ void umma_kind(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     if constexpr (KIND == KIND_I8) umma_i8(d, a, b, idesc, acc);
-    else if constexpr (KIND == KIND_BF16) umma_f16(d, a, b, idesc, acc);
+    else if constexpr (KIND == KIND_BF16 || KIND == KIND_F16) umma_f16(d, a, b, idesc, acc);
+    else if constexpr (KIND == KIND_TF32) umma_tf32(d, a, b, idesc, acc);
     else umma_f8(d, a, b, idesc, acc);
 }
 template <int KIND>
 __device__ __forceinline__ void umma_kind_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     if constexpr (KIND == KIND_I8) umma_i8_pair(d, a, b, idesc, acc);
-    else if constexpr (KIND == KIND_BF16) umma_f16_pair(d, a, b, idesc, acc);
+    else if constexpr (KIND == KIND_BF16 || KIND == KIND_F16) umma_f16_pair(d, a, b, idesc, acc);
+    else if constexpr (KIND == KIND_TF32) umma_tf32_pair(d, a, b, idesc, acc);
     else umma_f8_pair(d, a, b, idesc, acc);
 }
 
@@ -163,6 +174,23 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
 #pragma unroll
             for (int i = 0; i < 32; ++i)
                 if (n0 + i < p.N) dst[i] = f[i];
+        }
+    } else if (OUT == QG_OUT_F16) {
+        __half* dst = static_cast<__half*>(p.C) + (size_t)m * p.N + n0;
+        if (full_chunk && (p.N % 8) == 0) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+                w[i] = *reinterpret_cast<uint32_t*>(&h);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+                *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (n0 + i < p.N) dst[i] = __float2half_rn(f[i]);
         }
     } else {
         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
@@ -584,21 +612,57 @@ int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* 
     }
 }
 
-// Tensor-furnace GEMMs: C = alpha * A B^T with f32 accumulation, bf16 or e4m3 operands.
+// Tensor-furnace GEMMs: C = alpha * A B^T with f32 accumulation; bf16, fp16,
+// tf32 or e4m3 operands; bf16, fp16 or f32 output.
+namespace {
+template <int KIND>
+int dense_out(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
+              cudaStream_t stream) {
+    switch (out_type) {
+        case QG_OUT_BF16: return i8::launch<KIND, QG_OUT_BF16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
+        case QG_OUT_F16: return i8::launch<KIND, QG_OUT_F16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
+        default: return i8::launch<KIND, QG_OUT_F32>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
+    }
+}
+} // namespace
+
+const char* dense_kind_entry(int kind) {
+    switch (kind) {
+        case i8::KIND_BF16: return "qg_gemm_bf16";
+        case i8::KIND_F16: return "qg_gemm_f16";
+        case i8::KIND_TF32: return "qg_gemm_tf32";
+        case i8::KIND_E4M3: return "qg_gemm_e4m3";
+        default: return "qg_gemm_dense";
+    }
+}
+
 int gemm_dense(int kind, const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
                cudaStream_t stream) {
-    const char* name = kind == i8::KIND_BF16 ? "qg_gemm_bf16" : "qg_gemm_e4m3";
+    const char* name = dense_kind_entry(kind);
+    QG_CHECK_ARG(kind == i8::KIND_BF16 || kind == i8::KIND_F16 || kind == i8::KIND_TF32 || kind == i8::KIND_E4M3,
+                 "%s: unknown operand kind %d", name, kind);
     QG_CHECK_ARG(A && B && C, "%s: null operand or output", name);
     QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "%s: empty shape %dx%dx%d", name, M, N, K);
-    QG_CHECK_ARG((K * i8::elem_bytes(kind)) % 16 == 0, "%s: K=%d: rows must be a multiple of 16 bytes", name, K);
-    QG_CHECK_ARG(out_type == QG_OUT_BF16 || out_type == QG_OUT_F32, "%s: out_type %d (bf16 or f32)", name, out_type);
-    if (kind == i8::KIND_BF16)
-        return out_type == QG_OUT_BF16
-                   ? i8::launch<i8::KIND_BF16, QG_OUT_BF16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream)
-                   : i8::launch<i8::KIND_BF16, QG_OUT_F32>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
-    return out_type == QG_OUT_BF16
-               ? i8::launch<i8::KIND_E4M3, QG_OUT_BF16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream)
-               : i8::launch<i8::KIND_E4M3, QG_OUT_F32>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
+    QG_CHECK_ARG(((int64_t)K * i8::elem_bytes(kind)) % 16 == 0, "%s: K=%d: rows must be a multiple of 16 bytes", name, K);
+    QG_CHECK_ARG(out_type == QG_OUT_BF16 || out_type == QG_OUT_F16 || out_type == QG_OUT_F32,
+                 "%s: out_type %d (bf16, f16 or f32)", name, out_type);
+    switch (kind) {
+        case i8::KIND_BF16: return dense_out<i8::KIND_BF16>(A, B, alpha, C, out_type, M, N, K, stream);
+        case i8::KIND_F16: return dense_out<i8::KIND_F16>(A, B, alpha, C, out_type, M, N, K, stream);
+        case i8::KIND_TF32: return dense_out<i8::KIND_TF32>(A, B, alpha, C, out_type, M, N, K, stream);
+        default: return dense_out<i8::KIND_E4M3>(A, B, alpha, C, out_type, M, N, K, stream);
+    }
+}
+
+int gemm_dense_format(int fmt, const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
+                      cudaStream_t stream) {
+    switch (fmt) {
+        case QG_FMT_BF16: return gemm_dense(i8::KIND_BF16, A, B, alpha, C, out_type, M, N, K, stream);
+        case QG_FMT_FP16: return gemm_dense(i8::KIND_F16, A, B, alpha, C, out_type, M, N, K, stream);
+        case QG_FMT_TF32: return gemm_dense(i8::KIND_TF32, A, B, alpha, C, out_type, M, N, K, stream);
+        case QG_FMT_E4M3: return gemm_dense(i8::KIND_E4M3, A, B, alpha, C, out_type, M, N, K, stream);
+        default: set_error("format %d is not a dense format", fmt); return QG_ERR_ARG;
+    }
 }
 
 } // namespace qg
@@ -616,4 +680,14 @@ extern "C" int qg_gemm_bf16(const void* A, const void* B, float alpha, void* C, 
 extern "C" int qg_gemm_e4m3(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
                             void* stream) {
     return qg::gemm_dense(qg::i8::KIND_E4M3, A, B, alpha, C, out_type, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qg_gemm_f16(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
+                           void* stream) {
+    return qg::gemm_dense(qg::i8::KIND_F16, A, B, alpha, C, out_type, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qg_gemm_tf32(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
+                            void* stream) {
+    return qg::gemm_dense(qg::i8::KIND_TF32, A, B, alpha, C, out_type, M, N, K, static_cast<cudaStream_t>(stream));
 }

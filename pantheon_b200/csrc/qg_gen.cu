@@ -107,6 +107,32 @@ __global__ void gen_fp8_rows_kernel(uint8_t* Q, float* S, int R, int K, uint64_t
     }
 }
 
+// Dense tensor-furnace operands: v = j / 32768 - 1 with j the top 16 bits of the
+// element's hash (uniform on [-1, 1) in steps of 2^-15; exact in fp32), rounded
+// to the operand format (nearest even; e4m3 saturating; tf32 = fp32 word with
+// the low 13 mantissa bits cleared after rounding).
+__device__ __forceinline__ float dense_value(uint64_t h) {
+    return __fsub_rn(__fmul_rn((float)(uint32_t)(h >> 48), 3.0517578125e-05f), 1.0f);
+}
+
+__device__ __forceinline__ uint32_t tf32_rn_bits(float v) {
+    uint32_t u = __float_as_uint(v);
+    u += 0xFFFu + ((u >> 13) & 1u);
+    return u & 0xFFFFE000u;
+}
+
+template <int FMT>
+__global__ void gen_dense_kernel(void* out, uint64_t n, uint64_t key) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float v = dense_value(hash_at(key, i));
+        if constexpr (FMT == QG_FMT_BF16) static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+        else if constexpr (FMT == QG_FMT_FP16) static_cast<__half*>(out)[i] = __float2half_rn(v);
+        else if constexpr (FMT == QG_FMT_TF32) static_cast<uint32_t*>(out)[i] = tf32_rn_bits(v);
+        else static_cast<uint8_t*>(out)[i] = to_e4m3(v);
+    }
+}
+
 // B: 128 x 128 blocks, one 256-thread CTA per block (thread t: row t/2, 64 k).
 __global__ void gen_fp8_blocks_kernel(uint8_t* Q, float* S, int R, int K, uint64_t key) {
     const int kb_count = K / 128;
@@ -246,6 +272,22 @@ int gen_i8(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, cudaStream_
     return QG_OK;
 }
 
+int gen_dense(int fmt, void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, cudaStream_t s) {
+    QG_CHECK_ARG(out || n == 0, "qg_gen_dense: null output");
+    if (n == 0) return QG_OK;
+    const uint64_t key = gen::stream_key(seed, tensor_id);
+    const int grid = gen::grid_for(n);
+    switch (fmt) {
+        case QG_FMT_BF16: gen::gen_dense_kernel<QG_FMT_BF16><<<grid, 256, 0, s>>>(out, n, key); break;
+        case QG_FMT_FP16: gen::gen_dense_kernel<QG_FMT_FP16><<<grid, 256, 0, s>>>(out, n, key); break;
+        case QG_FMT_TF32: gen::gen_dense_kernel<QG_FMT_TF32><<<grid, 256, 0, s>>>(out, n, key); break;
+        case QG_FMT_E4M3: gen::gen_dense_kernel<QG_FMT_E4M3><<<grid, 256, 0, s>>>(out, n, key); break;
+        default: set_error("qg_gen_dense: format %d is not a dense format", fmt); return QG_ERR_ARG;
+    }
+    QG_CUDA(cudaGetLastError());
+    return QG_OK;
+}
+
 int gen_uniform(void* out, uint64_t n, float lo, float hi, uint64_t seed, uint32_t tensor_id, cudaStream_t s) {
     QG_CHECK_ARG(out || n == 0, "qg_gen_uniform_f32: null output");
     if (n == 0) return QG_OK;
@@ -349,4 +391,8 @@ extern "C" int qg_gen_uniform_f32(void* out, uint64_t n, float lo, float hi, uin
 
 extern "C" int qg_gen_normal_f32(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream) {
     return qg::gen_normal(out, n, seed, tensor_id, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qg_gen_dense(int format, void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream) {
+    return qg::gen_dense(format, out, n, seed, tensor_id, static_cast<cudaStream_t>(stream));
 }

@@ -11,10 +11,12 @@ import ctypes as C
 
 import torch
 
-from ._lib import (QG_FMT_INT8, QG_OUT_BF16, QG_OUT_F32, QG_OUT_S32, QGCfg, QGMismatch, QGError, check,
+from ._lib import (QG_FMT_INT8, QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3, QG_OUT_BF16, QG_OUT_F16,
+                   QG_OUT_F32, QG_OUT_S32, QGCfg, QGMismatch, QGError, check,
                    last_error, load_library)
 
-_OUT_DTYPES = {QG_OUT_BF16: torch.bfloat16, QG_OUT_F32: torch.float32, QG_OUT_S32: torch.int32}
+_OUT_DTYPES = {QG_OUT_BF16: torch.bfloat16, QG_OUT_F32: torch.float32, QG_OUT_S32: torch.int32,
+               QG_OUT_F16: torch.float16}
 
 
 class _DeviceBytes:
@@ -82,29 +84,52 @@ def gemm_fp8_b128(A: torch.Tensor, B: torch.Tensor, sa: torch.Tensor, sb: torch.
     return out
 
 
-def gemm_bf16(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: int = QG_OUT_BF16,
-              out: torch.Tensor | None = None) -> torch.Tensor:
-    """C = alpha * A @ B^T (fp32 accumulate) on the tcgen05 bf16 path: A bf16 [M,K], B bf16 [N,K]."""
+def _gemm_dense(entry: str, A: torch.Tensor, B: torch.Tensor, alpha: float, out_type: int,
+                out: torch.Tensor | None) -> torch.Tensor:
     _require_cuda(A, B)
     M, K = A.shape
     N = B.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=_OUT_DTYPES[out_type], device=A.device)
-    check("qg_gemm_bf16", load_library().qg_gemm_bf16(_ptr(A), _ptr(B), float(alpha), _ptr(out), out_type, M, N, K,
-                                                       _stream(A.device)))
+    check(entry, getattr(load_library(), entry)(_ptr(A), _ptr(B), float(alpha), _ptr(out), out_type, M, N, K,
+                                                _stream(A.device)))
     return out
+
+
+def gemm_bf16(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: int = QG_OUT_BF16,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = alpha * A @ B^T (fp32 accumulate) on the tcgen05 bf16 path: A bf16 [M,K], B bf16 [N,K]."""
+    return _gemm_dense("qg_gemm_bf16", A, B, alpha, out_type, out)
+
+
+def gemm_f16(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: int = QG_OUT_F16,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = alpha * A @ B^T (fp32 accumulate) on the tcgen05 fp16 path: A fp16 [M,K], B fp16 [N,K]."""
+    return _gemm_dense("qg_gemm_f16", A, B, alpha, out_type, out)
+
+
+def gemm_tf32(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: int = QG_OUT_F32,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = alpha * A @ B^T (fp32 accumulate) on the tcgen05 tf32 path: A, B fp32 [M,K] / [N,K]
+    holding tf32 values (low 13 mantissa bits zero)."""
+    return _gemm_dense("qg_gemm_tf32", A, B, alpha, out_type, out)
 
 
 def gemm_e4m3(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: int = QG_OUT_BF16,
               out: torch.Tensor | None = None) -> torch.Tensor:
     """C = alpha * A @ B^T (fp32 accumulate) on the tcgen05 e4m3 path: A, B e4m3 bytes [M,K] / [N,K]."""
-    _require_cuda(A, B)
-    M, K = A.shape
-    N = B.shape[0]
-    if out is None:
-        out = torch.empty((M, N), dtype=_OUT_DTYPES[out_type], device=A.device)
-    check("qg_gemm_e4m3", load_library().qg_gemm_e4m3(_ptr(A), _ptr(B), float(alpha), _ptr(out), out_type, M, N, K,
-                                                       _stream(A.device)))
+    return _gemm_dense("qg_gemm_e4m3", A, B, alpha, out_type, out)
+
+
+_DENSE_DTYPES = {QG_FMT_BF16: torch.bfloat16, QG_FMT_FP16: torch.float16, QG_FMT_TF32: torch.float32,
+                 QG_FMT_E4M3: torch.uint8}
+
+
+def gen_dense(fmt: int, rows: int, cols: int, seed: int, tensor_id: int, device="cuda") -> torch.Tensor:
+    """A dense workload operand [rows, cols] from the generator stream (seed, tensor_id)."""
+    out = torch.empty((rows, cols), dtype=_DENSE_DTYPES[fmt], device=device)
+    check("qg_gen_dense", load_library().qg_gen_dense(fmt, _ptr(out), rows * cols, seed, tensor_id,
+                                                       _stream(out.device)))
     return out
 
 

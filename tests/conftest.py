@@ -29,7 +29,8 @@ def qglib():
     """The in-tree C-ABI library, built if missing (build needs only nvcc)."""
     import pantheon_b200
     from pantheon_b200 import build
-    if not all(x.exists() for x in (pantheon_b200.LIB_PATH, pantheon_b200.BIN_PATH, pantheon_b200.DECODE_BIN_PATH)):
+    if not all(x.exists() for x in (pantheon_b200.LIB_PATH, pantheon_b200.BIN_PATH, pantheon_b200.DECODE_BIN_PATH,
+                                     pantheon_b200.MMA_BIN_PATH)):
         build.build()
     return pantheon_b200.load_library()
 

@@ -35,12 +35,12 @@ def test_library_exports_every_header_symbol(qglib):
 
 
 def _binaries():
-    from pantheon_b200 import BIN_PATH, DECODE_BIN_PATH
-    return [(BIN_PATH, "quantized_gemm"), (DECODE_BIN_PATH, "llm_decode")]
+    from pantheon_b200 import BIN_PATH, DECODE_BIN_PATH, MMA_BIN_PATH
+    return [(BIN_PATH, "quantized_gemm"), (DECODE_BIN_PATH, "llm_decode"), (MMA_BIN_PATH, "mma_virus")]
 
 
 def test_binaries_need_three_arguments(qglib):
-    """ai_workload_template.h:352-353 and llm_decode.cpp:60: argc < 4 exits 1."""
+    """ai_workload_template.h:352-353, llm_decode.cpp:60 and mma_virus.cpp:182: argc < 4 exits 1."""
     for path, _ in _binaries():
         for args in ([], ["0"], ["0", "1"]):
             proc = subprocess.run([str(path), *args], capture_output=True, text=True, timeout=60)
@@ -84,6 +84,44 @@ def test_library_rejects_bad_shapes_before_touching_a_device(qglib):
     assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == 0
     # A, B, sa, sb, C and golden (bf16), row checksums and golden checksums
     assert b.value == 8192 * 8192 * 2 + 8 * 8192 + 2 * 8192 * 8192 * 2 + 2 * 4 * 8192 + 4096
+
+
+@pytest.mark.parametrize("gemm_type, why", [("fp32", "no tensor-core path"), ("int4", "Unknown --gemm_type")])
+def test_mma_virus_rejects_gemm_types_it_cannot_run(qglib, gemm_type, why):
+    """vendor_gemm.h:525-529: an unknown --gemm_type is an error (exit 1), checked before any device call."""
+    from pantheon_b200 import MMA_BIN_PATH
+    proc = subprocess.run([str(MMA_BIN_PATH), "0", "1", "5", "--gemm_type", gemm_type], capture_output=True, text=True,
+                          timeout=60)
+    assert proc.returncode == 1
+    assert why in proc.stderr
+    assert "Throughput:" not in proc.stdout
+
+
+def test_mma_virus_rejects_small_gemm_dims(qglib):
+    """vendor_gemm.h:530-533: --gemm_m/n/k below 16 is an error."""
+    from pantheon_b200 import MMA_BIN_PATH
+    proc = subprocess.run([str(MMA_BIN_PATH), "0", "1", "5", "--gemm_m", "8"], capture_output=True, text=True,
+                          timeout=60)
+    assert proc.returncode == 1 and "at least 16" in proc.stderr
+
+
+def test_dense_formats_size_and_validate(qglib):
+    import ctypes as C
+    import pantheon_b200 as pb
+    b = C.c_uint64()
+    # A, B (bf16) and C, golden (bf16) at the 8192^3 default
+    cfg = pb._lib.QGCfg(pb.QG_FMT_BF16, 0, 0, 0, pb.QG_OUT_BF16, 1, 0)
+    assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == 0
+    assert b.value == 4 * 8192 * 8192 * 2 + 4096
+    cfg = pb._lib.QGCfg(pb.QG_FMT_TF32, 256, 256, 256, pb.QG_OUT_F32, 2, 0)
+    assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == 0
+    assert b.value == 2 * (2 * 256 * 256 * 4 + 2 * 256 * 256 * 4) + 4096
+    cfg = pb._lib.QGCfg(pb.QG_FMT_FP16, 256, 256, 100, pb.QG_OUT_F16, 1, 0)   # 200-byte rows
+    assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == pb._lib.QG_ERR_ARG
+    cfg = pb._lib.QGCfg(pb.QG_FMT_E4M3, 256, 256, 256, pb.QG_OUT_S32, 1, 0)   # no integer output
+    assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == pb._lib.QG_ERR_ARG
+    for entry in ("qg_gemm_bf16", "qg_gemm_f16", "qg_gemm_tf32", "qg_gemm_e4m3"):
+        assert getattr(qglib, entry)(None, None, 1.0, None, 0, 128, 128, 128, None) == pb._lib.QG_ERR_ARG
 
 
 def test_runner_parser_on_reference_mock_binary():
