@@ -378,6 +378,15 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Relaxed arrive on an mbarrier of any CTA of the cluster.  For releasing a TMEM
+// buffer whose reads have completed (tcgen05.wait::ld, then
+// tcgen05.fence::before_thread_sync): no memory operation of the arriving thread
+// needs ordering before the consumer's MMAs, and a release arrive would wait for
+// every load the thread has in flight (prefetched scales, for one).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // 2D tiled load into this CTA's shared memory, completing the transaction
 // bytes on an mbarrier of either CTA of the pair (cluster address).
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr,

@@ -32,7 +32,8 @@ def test_quantiser_matches_oracle(cuda_device, oracle):
     np.testing.assert_array_equal(_np(sb).view(np.uint32), rsb.view(np.uint32))
 
 
-SHAPES = [(128, 256, 128), (256, 512, 1024), (130, 200, 384), (1, 17, 128), (1000, 1000, 2048), (384, 128, 4096)]
+SHAPES = [(128, 256, 128), (256, 512, 1024), (130, 200, 384), (1, 17, 128), (1000, 1000, 2048), (384, 128, 4096),
+          (512, 136, 256), (768, 64, 128), (300, 1100, 640)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
