@@ -135,7 +135,11 @@ QG_API double qg_bytes_per_launch(const qg_ctx* ctx);
 
 /* Copy the context's operands from / its output to HOST memory (pinned or
  * pageable), on `stream`; used for the end-to-end path.  The host layouts are
- * the device layouts described under the direct entry points below. */
+ * the device layouts described under the direct entry points below.
+ * host_operands holds one pointer per operand of the format, in the order of
+ * qg_tensor's slots: 2 for the dense formats (A, B), 4 for INT8 / FP8 (A, B,
+ * sa, sb) and W4A16 (X, W, S, Z), 5 for NVFP4 (A, sfa, B, sfb, and the two
+ * fp32 per-tensor scales, which the next launch of that copy uses). */
 QG_API int  qg_upload(qg_ctx* ctx, int copy, const void* const* host_operands, void* stream);
 QG_API int  qg_download(qg_ctx* ctx, int copy, void* host_out, void* stream);
 

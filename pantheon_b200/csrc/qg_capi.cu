@@ -242,6 +242,12 @@ int qg_upload(qg_ctx* c, int copy, const void* const* host, void* stream) {
         CTX_CUDA(c, cudaMemcpyAsync(c->copies[(size_t)copy].op[i], host[i], c->layout.op_bytes[i],
                                     cudaMemcpyHostToDevice, s));
     }
+    if (c->cfg.format == QG_FMT_NVFP4) {
+        // the launch passes the two per-tensor scales by value: take the uploaded ones
+        const float* g = static_cast<const float*>(host[4]);
+        c->copies[(size_t)copy].global_a = g[0];
+        c->copies[(size_t)copy].global_b = g[1];
+    }
     return QG_OK;
 }
 

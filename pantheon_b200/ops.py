@@ -341,6 +341,16 @@ class Workload:
         self._check("qg_tensor", self.lib.qg_tensor(self.ctx, copy, slot, C.byref(p), C.byref(b)))
         return p.value, b.value
 
+    def n_operands(self) -> int:
+        """Operand slots of this format (the tensors qg_upload copies): 2 for the dense
+        formats, 4 for INT8 / FP8 / W4A16, 5 for NVFP4."""
+        n = 0
+        p = C.c_void_p()
+        b = C.c_uint64()
+        while n < 5 and self.lib.qg_tensor(self.ctx, 0, n, C.byref(p), C.byref(b)) == 0 and b.value > 0:
+            n += 1
+        return n
+
     def tensor(self, copy: int, slot: int, dtype=torch.uint8) -> torch.Tensor:
         """Copy a device tensor of the context to a new CUDA tensor (raw bytes viewed as dtype)."""
         ptr, nbytes = self.tensor_ptr(copy, slot)
@@ -349,6 +359,9 @@ class Workload:
         return view.clone().view(dtype)
 
     def upload(self, copy: int, host_tensors, stream=None):
+        """Copy host operands (one per operand slot, in slot order) into copy `copy`."""
+        if len(host_tensors) != self.n_operands():
+            raise ValueError(f"upload: {len(host_tensors)} host tensors for {self.n_operands()} operand slots")
         arr = (C.c_void_p * len(host_tensors))(*[t.data_ptr() for t in host_tensors])
         s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)
         self._check("qg_upload", self.lib.qg_upload(self.ctx, copy, arr, s))
