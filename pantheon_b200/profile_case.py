@@ -1,6 +1,7 @@
 """Run a few launches of one workload kernel, for profilers (ncu) and quick timing.
 
-    python -m pantheon_b200.profile_case --format int8 [--m M --n N --k K] [--iters 3] [--copies 1]
+    python -m pantheon_b200.profile_case --format int8|fp8|nvfp4|w4a16|bf16|fp16|tf32|e4m3
+                                         [--m M --n N --k K] [--iters 3] [--copies 1]
 
 Fills the operands, computes the golden result (one launch), then runs
 `--iters` launches and synchronizes.  Prints the mean device time per launch
@@ -15,7 +16,10 @@ import torch
 
 import pantheon_b200 as pb
 
-FORMATS = {"int8": pb.QG_FMT_INT8, "fp8": pb.QG_FMT_FP8, "nvfp4": pb.QG_FMT_NVFP4, "w4a16": pb.QG_FMT_W4A16}
+FORMATS = {"int8": pb.QG_FMT_INT8, "fp8": pb.QG_FMT_FP8, "nvfp4": pb.QG_FMT_NVFP4, "w4a16": pb.QG_FMT_W4A16,
+           "bf16": pb.QG_FMT_BF16, "fp16": pb.QG_FMT_FP16, "tf32": pb.QG_FMT_TF32, "e4m3": pb.QG_FMT_E4M3}
+# output type of each format (the dense furnace formats write their own type, tf32 fp32, e4m3 bf16)
+OUT_TYPES = {"fp16": pb.QG_OUT_F16, "tf32": pb.QG_OUT_F32}
 
 
 def main(argv=None) -> int:
@@ -29,7 +33,8 @@ def main(argv=None) -> int:
     ap.add_argument("--seed", type=int, default=1)
     a = ap.parse_args(argv)
     torch.cuda.set_device(0)
-    with pb.Workload(FORMATS[a.format], a.m, a.n, a.k, copies=a.copies, seed=a.seed) as w:
+    with pb.Workload(FORMATS[a.format], a.m, a.n, a.k, copies=a.copies, seed=a.seed,
+                     out_type=OUT_TYPES.get(a.format, pb.QG_OUT_BF16)) as w:
         w.fill(a.seed)
         w.golden()
         s = torch.cuda.current_stream()
