@@ -38,9 +38,13 @@ constexpr int kGemvSms = 148;
 uint64_t gemv_w4a16_tc_partial_bytes(int N, int K);
 uint64_t gemv_w4a16_tc_ticket_count(int N);
 
-// One launch for `mrows` (1..16) activation rows; `partials` and `tickets`
-// come from the caller's workspace, tickets zero on entry (and on return).
+// Bytes of the prepared-X area (quantised activation tiles and their scales).
+uint64_t gemv_w4a16_tc_xprep_bytes(int K);
+
+// One call for `mrows` (1..16) activation rows (two launches: the X pre-pass,
+// then the GEMV); `partials`, `tickets` and `xprep` come from the caller's
+// workspace, tickets zero on entry (and on return).
 int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
-                  int K, float* partials, unsigned int* tickets, cudaStream_t stream);
+                  int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream);
 
 } // namespace qg

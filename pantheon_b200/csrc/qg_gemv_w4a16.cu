@@ -371,8 +371,16 @@ static uint64_t ticket_bytes(int N) {
     return (a > b ? a : b) * 4;
 }
 
-// Workspace: fp32 partials for the largest row chunk, then the tickets (shared
-// by both kernels: each leaves them zero).
+// Workspace: fp32 partials for the largest row chunk, the tensor-core path's
+// prepared X (when any chunk takes it), then the tickets (shared by both
+// kernels: each leaves them zero).
+static uint64_t xprep_bytes(int M, int K) {
+    for (int m0 = 0; m0 < M; m0 += w4::MAX_M)
+        if ((M - m0 < w4::MAX_M ? M - m0 : w4::MAX_M) >= kTensorMinRows)
+            return (gemv_w4a16_tc_xprep_bytes(K) + 255) & ~255ull;
+    return 0;
+}
+
 uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int /*sm_count*/) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     uint64_t partials = 0;
@@ -387,7 +395,7 @@ uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int /*sm_count*/) {
         }
         if (ws > partials) partials = ws;
     }
-    return ((partials + 255) & ~255ull) + ticket_bytes(N);
+    return ((partials + 255) & ~255ull) + xprep_bytes(M, K) + ticket_bytes(N);
 }
 
 int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,
@@ -409,13 +417,14 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
                  (unsigned long long)workspace_bytes);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const uint64_t tickets_off = need - ticket_bytes(N);
+    const uint64_t xprep_off = tickets_off - xprep_bytes(M, K);
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mrows = (M - m0) < w4::MAX_M ? (M - m0) : w4::MAX_M;
         if (mrows >= kTensorMinRows) {
             rc = gemv_w4a16_tc(static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K, W, S, Z,
                                static_cast<uint8_t*>(Y) + (size_t)m0 * N * (out_type == QG_OUT_F32 ? 4 : 2), out_type,
                                mrows, N, K, reinterpret_cast<float*>(ws),
-                               reinterpret_cast<unsigned int*>(ws + tickets_off), stream);
+                               reinterpret_cast<unsigned int*>(ws + tickets_off), ws + xprep_off, stream);
             if (rc) return rc;
             continue;
         }

@@ -32,25 +32,34 @@
 // a workspace with a ticket per (tile, lane quarter): the last CTA to finish
 // sums the pieces in order, so the result is bit-for-bit reproducible.
 //
-// Per CTA, 832 threads (26 warps):
-//   warp 0      producer: per unit, TMA loads of the W tile (32 packed rows x
-//               128 columns, no swizzle) and the raw X slab (M rows x 256 bf16)
-//               into a 6-stage ring (96 KB of W in flight per SM).
-//   warps 2-5   activation staging: quantise the X slab as above into one
-//               32-row x 128-byte, 128-byte-swizzled K-major tile per group (in
-//               the MMA's K order, below), plus each (row, group)'s 2^e and
-//               sum xi.  Rows M..15 (and 16+M..31) are zeroed once.
-//   warps 10-25 dequant, two teams of 8 taking alternate units (one team's
+// Two launches per call (both with programmatic stream serialization):
+//   xprep_kernel  quantises X once per call, one CTA per pair of groups: per
+//                 (row, group) the 14-bit digits above, written straight into
+//                 the MMA's 32-row x 128-byte, 128-byte-swizzled K-major tile
+//                 per group (in the MMA's K order, below; rows M..15 and
+//                 16+M..31 zero), plus the row's 2^e and sum of xi.  Every unit
+//                 of the main kernel used to redo this for its own slab of X
+//                 (the largest CUDA-core cost of a unit).
+//   gemv kernel   per CTA, 736 threads (23 warps):
+//   warp 0      W producer: per unit, a TMA load of the W tile (32 packed rows
+//               x 128 columns, no swizzle) into an 11-stage ring (176 KB of W
+//               in flight per SM); a stage is free again as soon as the dequant
+//               team has turned it into TMEM columns, so the HBM stream does not
+//               wait for the MMA or the fold.
+//   warp 2      X producer: per unit, a bulk copy of the unit's two prepared X
+//               tiles into a 4-stage ring, freed by the unit's MMA commit.
+//   warps 7-22  dequant, two teams of 8 taking alternate units (one team's
 //               barrier round trips overlap the other's): each warp owns a TMEM
 //               lane quarter and 8 of the 16 packed rows of a group; lane n
 //               turns each word into two TMEM columns of four 16q bytes, written
 //               with tcgen05.st as the MMA's A operand.
 //   warp 1      TMEM allocator and MMA issuer: per group 4 x tcgen05.mma M=128
 //               N=32 K=32 into a 32-column int32 accumulator.
-//   warps 6-9   fold, one per lane quarter: per unit, read both groups'
-//               accumulators and fold all 16 rows; scales and zero points
-//               arrive by cp.async SZ_AHEAD units ahead (a load consumed in its
-//               own iteration put an HBM round trip on every unit).
+//   warps 3-6   fold, one per lane quarter: per unit, read both groups'
+//               accumulators and fold all 16 rows; scales, zero points and the
+//               rows' 2^e and sums arrive by cp.async SZ_AHEAD units ahead (a
+//               load consumed in its own iteration put an HBM round trip on
+//               every unit).
 // K order inside each packed word kw: TMEM column 2kw holds k = 8kw + 0, 2, 4,
 // 6 and column 2kw+1 holds k = 8kw + 1, 3, 5, 7, so the activation tile stores
 // each run of eight as (x0, x2, x4, x6, x1, x3, x5, x7); both operands use the
@@ -72,15 +81,18 @@ constexpr int UG = 2;                         // groups per unit
 constexpr int MROWS = 16;                     // activation rows, padded
 constexpr int MMA_N = 2 * MROWS;              // h rows, then l rows
 constexpr int UMMA_K = 32;                    // int8 elements per MMA
-constexpr int STAGES = 6;
 constexpr int W_ROWS = UG * GROUP / 8;                    // 32 packed rows
 constexpr int W_BYTES = TILE_N * W_ROWS * 4;              // 16 KB
-constexpr int XRAW_ROW = UG * GROUP * 2;                  // 512 B per activation row
-constexpr int XRAW_BYTES = MROWS * XRAW_ROW;              // 8 KB (rows >= M not loaded)
 constexpr int XT_GROUP = MMA_N * GROUP;                   // 4 KB int8 tile per group
-constexpr int XT_OFF = W_BYTES + XRAW_BYTES;
-constexpr int STAGE_BYTES = XT_OFF + UG * XT_GROUP;       // 32 KB
-static_assert(XT_OFF % 1024 == 0 && STAGE_BYTES % 1024 == 0, "swizzled tiles need 1 KB alignment");
+constexpr int XT_BYTES = UG * XT_GROUP;                   // 8 KB: a unit's two X tiles
+constexpr int W_STAGES = 11;                              // W ring: 176 KB
+constexpr int X_STAGES = 4;                               // prepared-X ring: 32 KB
+constexpr int X_RING_OFF = W_STAGES * W_BYTES;
+constexpr int RINGS_BYTES = X_RING_OFF + X_STAGES * XT_BYTES;
+static_assert(X_RING_OFF % 1024 == 0 && XT_BYTES % 1024 == 0, "swizzled tiles need 1 KB alignment");
+// prepared X per group in the workspace: the 4 KB tile, then (after all tiles)
+// 16 scales 2^e and 16 sums of xi per group
+constexpr int XS_GROUP = 2 * MROWS;                       // floats per group
 constexpr int TEAMS = 2;                      // dequant teams, alternate units
 constexpr int NA = 4;                         // A operand buffers in TMEM
 constexpr int A_COLS = UG * GROUP / 4;        // 64 columns per unit: 2 x 128 bytes per lane
@@ -90,45 +102,46 @@ constexpr int D_COL0 = NA * A_COLS;
 constexpr int TMEM_COLS = 512;
 static_assert(D_COL0 + ND * D_COLS <= TMEM_COLS, "TMEM budget");
 static_assert(NA % TEAMS == 0, "each team cycles through its own A buffers");
-constexpr int XS_RING = 16;                   // row sums / scales by unit (>= STAGES + ND)
 constexpr int SZ_AHEAD = 4;                   // units between an S/Z fetch and its fold
 constexpr int SZ_RING = 8;                    // >= SZ_AHEAD + 1
-static_assert(XS_RING >= STAGES + ND && SZ_RING >= SZ_AHEAD + 1, "ring depths");
-constexpr int XW0 = 2, XWARPS = 4;            // activation staging warps
-constexpr int FW0 = 6, FWARPS = 4;            // fold warps
-constexpr int DW0 = 10, DWARPS = 8;           // dequant warps per team
-constexpr int THREADS = (DW0 + TEAMS * DWARPS) * 32;      // 832
+static_assert(SZ_RING >= SZ_AHEAD + 1, "ring depth");
+constexpr int XPW = 2;                        // X producer warp
+constexpr int FW0 = 3, FWARPS = 4;            // fold warps
+constexpr int DW0 = 7, DWARPS = 8;            // dequant warps per team
+constexpr int THREADS = (DW0 + TEAMS * DWARPS) * 32;      // 736
+static_assert(FW0 + FWARPS == DW0, "the fold warps are the ones between the MMA warp and the dequant teams");
 // A warp reaches TMEM lanes 32 * (warp % 4) .. +31 only: the four fold warps and
 // each half-team of four dequant warps are consecutive, so they cover all four.
 constexpr int SLICES = FWARPS;                // reduction slices of a tile = lane quarters
-constexpr int EMPTY_ARRIVALS = DWARPS + XWARPS + 1;       // one team, staging warps, MMA commit
+constexpr int W_EMPTY_ARRIVALS = DWARPS;      // the dequant team of the unit
+constexpr int XPREP_THREADS = 128;            // prepass CTA: 16 rows x 2 groups x 4 quarters
 
 constexpr uint32_t SITE_PRODUCER = 0x00040001u;
 constexpr uint32_t SITE_MMA = 0x00040002u;
-constexpr uint32_t SITE_X = 0x00040003u;
 constexpr uint32_t SITE_DEQ = 0x00040004u;
 constexpr uint32_t SITE_FOLD = 0x00040005u;
 
 struct Barriers {
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
-    uint64_t x_full[STAGES];
+    uint64_t w_full[W_STAGES];
+    uint64_t w_empty[W_STAGES];
+    uint64_t x_full[X_STAGES];
+    uint64_t x_empty[X_STAGES];
     uint64_t a_full[NA];
     uint64_t a_empty[NA];
     uint64_t d_full[ND];
     uint64_t d_empty[ND];
-    uint64_t xs_full[XS_RING];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
 };
 
-// per (unit slot, group, row): the row's 2^e and sum of xi
-constexpr int XSUM_BYTES = XS_RING * UG * MROWS * 4 * 2;              // 4 KB
 constexpr int SZ_BYTES = FWARPS * SZ_RING * UG * 64 * 2;              // 8 KB: 32 scales + 32 zeros
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + XSUM_BYTES + SZ_BYTES + (int)sizeof(Barriers) + 1024;
+constexpr int XS_BYTES = FWARPS * SZ_RING * UG * XS_GROUP * 4;        // 8 KB: rows' 2^e and sums
+constexpr int SMEM_BYTES = RINGS_BYTES + SZ_BYTES + XS_BYTES + (int)sizeof(Barriers) + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget (227 KB per CTA)");
 
 struct Params {
+    const uint8_t* xprep;    // [G2][4 KB] prepared X tiles, then [G2][2][16] fp32 (2^e, sum xi)
     const __half* S;
     const __half* Z;
     void* Y;
@@ -136,7 +149,7 @@ struct Params {
     unsigned int* tickets;   // [tiles][SLICES], zero between calls
     int M, N, K;
     int G;                   // groups = K / 128
-    int upt;                 // units per tile = ceil(G / UG)
+    int upt;                 // units per tile = ceil(G / UG); G2 = UG * upt prepared groups
     long long units;         // tiles * upt
     int maxp;                // most CTAs sharing one tile
     int out_type;
@@ -172,15 +185,15 @@ __device__ __forceinline__ int xt_offset(int row, int chunk) {
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
-gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, Params p) {
+gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-    uint8_t* stages = smem;
-    float* xscale = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES);     // [XS_RING][UG][16]
-    float* xsum = xscale + XS_RING * UG * MROWS;                              // [XS_RING][UG][16]
-    uint16_t* szring = reinterpret_cast<uint16_t*>(smem + STAGES * STAGE_BYTES + XSUM_BYTES);
-    Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * STAGE_BYTES + XSUM_BYTES + SZ_BYTES);
+    uint8_t* wring = smem;
+    uint8_t* xring = smem + X_RING_OFF;
+    uint16_t* szring = reinterpret_cast<uint16_t*>(smem + RINGS_BYTES);
+    float* xsring = reinterpret_cast<float*>(smem + RINGS_BYTES + SZ_BYTES);
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + RINGS_BYTES + SZ_BYTES + XS_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -190,24 +203,23 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
     const int nu = (int)(u1 - u0);
     const UnitPos start{(int)(u0 / p.upt), (int)(u0 % p.upt)};
 
-    // launched with programmatic stream serialization: no global access (and
-    // no TMEM) until the previous grid on the stream is complete
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Launched with programmatic stream serialization after xprep_kernel, whose
+    // CTAs trigger this launch only once their own griddepcontrol.wait has
+    // returned: when any CTA of this grid runs, every kernel before the pre-pass
+    // is complete, so W, S, Z, Y, the workspace and TMEM may be touched at once.
+    // Only the pre-pass's output (the prepared X) waits for griddepcontrol.wait
+    // (the X producer before its first tile, the fold warps before their first
+    // scale fetch).
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&bars->full[s], 1);
-            mbar_init(&bars->empty[s], EMPTY_ARRIVALS);
-            mbar_init(&bars->x_full[s], XWARPS);
-        }
+        for (int s = 0; s < W_STAGES; ++s) { mbar_init(&bars->w_full[s], 1); mbar_init(&bars->w_empty[s], W_EMPTY_ARRIVALS); }
+        for (int s = 0; s < X_STAGES; ++s) { mbar_init(&bars->x_full[s], 1); mbar_init(&bars->x_empty[s], 1); }
         for (int b = 0; b < NA; ++b) { mbar_init(&bars->a_full[b], DWARPS); mbar_init(&bars->a_empty[b], 1); }
         for (int b = 0; b < ND; ++b) { mbar_init(&bars->d_full[b], 1); mbar_init(&bars->d_empty[b], FWARPS); }
-        for (int b = 0; b < XS_RING; ++b) mbar_init(&bars->xs_full[b], XWARPS);
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmW);
-        tma_prefetch_desc(&tmX);
     }
     if (warp == 1) {
         tmem_alloc(&bars->tmem_base, TMEM_COLS);
@@ -220,27 +232,42 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
     volatile int* abort_flag = &bars->abort;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ producer
+        // ------------------------------------------------------------ W producer
         if (lane == 0) {
             uint32_t armed = 0, armed_phase = 0;
-            const uint32_t tx = W_BYTES + (uint32_t)p.M * XRAW_ROW;
             UnitPos pos = start;
             for (int i = 0; i < nu; ++i, pos.next(p.upt)) {
-                const int s = i % STAGES;
-                const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-                if (!mbar_wait(&bars->empty[s], ph ^ 1u, abort_flag, p.status, SITE_PRODUCER)) break;
-                uint8_t* st = stages + s * STAGE_BYTES;
-                mbar_arrive_expect_tx(&bars->full[s], tx);
-                tma_load_2d(st, &tmW, &bars->full[s], pos.t * TILE_N, pos.j * W_ROWS);
-                tma_load_2d(st + W_BYTES, &tmX, &bars->full[s], pos.j * UG * GROUP, 0);
+                const int s = i % W_STAGES;
+                const uint32_t ph = (uint32_t)(i / W_STAGES) & 1u;
+                if (!mbar_wait(&bars->w_empty[s], ph ^ 1u, abort_flag, p.status, SITE_PRODUCER)) break;
+                mbar_arrive_expect_tx(&bars->w_full[s], W_BYTES);
+                tma_load_2d(wring + s * W_BYTES, &tmW, &bars->w_full[s], pos.t * TILE_N, pos.j * W_ROWS);
                 armed |= 1u << s;
                 armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
             }
-            // every load of this CTA is issued: the next call may launch
+            // every weight load of this CTA is issued: the next call may launch
             asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
             // no copy may still be landing when the CTA exits
-            for (int s = 0; s < STAGES; ++s)
-                if (armed & (1u << s)) mbar_wait(&bars->full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
+            for (int s = 0; s < W_STAGES; ++s)
+                if (armed & (1u << s)) mbar_wait(&bars->w_full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
+        }
+    } else if (warp == XPW) {
+        // ------------------------------------------------------------ X producer
+        if (lane == 0) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");   // the pre-pass's tiles
+            uint32_t armed = 0, armed_phase = 0;
+            UnitPos pos = start;
+            for (int i = 0; i < nu; ++i, pos.next(p.upt)) {
+                const int s = i % X_STAGES;
+                const uint32_t ph = (uint32_t)(i / X_STAGES) & 1u;
+                if (!mbar_wait(&bars->x_empty[s], ph ^ 1u, abort_flag, p.status, SITE_PRODUCER)) break;
+                mbar_arrive_expect_tx(&bars->x_full[s], XT_BYTES);
+                bulk_load(xring + s * XT_BYTES, p.xprep + (size_t)pos.j * XT_BYTES, XT_BYTES, &bars->x_full[s]);
+                armed |= 1u << s;
+                armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
+            }
+            for (int s = 0; s < X_STAGES; ++s)
+                if (armed & (1u << s)) mbar_wait(&bars->x_full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -248,15 +275,15 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
             constexpr uint32_t IDESC = make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, TILE_N, MMA_N);
             bool ok = true, issued = false;
             for (int i = 0; i < nu && ok; ++i) {
-                const int s = i % STAGES, ab = i % NA, db = i % ND;
-                if (!mbar_wait(&bars->x_full[s], (uint32_t)(i / STAGES) & 1u, abort_flag, p.status, SITE_MMA) ||
+                const int s = i % X_STAGES, ab = i % NA, db = i % ND;
+                if (!mbar_wait(&bars->x_full[s], (uint32_t)(i / X_STAGES) & 1u, abort_flag, p.status, SITE_MMA) ||
                     !mbar_wait(&bars->a_full[ab], (uint32_t)(i / NA) & 1u, abort_flag, p.status, SITE_MMA) ||
                     !mbar_wait(&bars->d_empty[db], ((uint32_t)(i / ND) & 1u) ^ 1u, abort_flag, p.status, SITE_MMA)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t xt = smem_u32(stages + s * STAGE_BYTES + XT_OFF);
+                const uint32_t xt = smem_u32(xring + s * XT_BYTES);
 #pragma unroll
                 for (int k = 0; k < GROUP / UMMA_K; ++k)
 #pragma unroll
@@ -267,110 +294,16 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
                 issued = true;
                 umma_commit(&bars->d_full[db]);
                 umma_commit(&bars->a_empty[ab]);
-                umma_commit(&bars->empty[s]);
+                umma_commit(&bars->x_empty[s]);
             }
             if (!ok && issued) {
                 umma_commit(&bars->drain);
                 mbar_wait(&bars->drain, 0, nullptr, nullptr, 0);
             }
         }
-    } else if (warp < FW0) {
-        // ------------------------------------------------------------ activation staging
-        const int xi = threadIdx.x - XW0 * 32;      // 0..127
-        const int m = xi >> 3;                      // row 0..15
-        const int g = (xi >> 2) & 1;                // group of the unit
-        const int qk = xi & 3;                      // 32-element quarter of the group: chunks 2qk, 2qk+1
-        // rows M..15 (h) and 16+M..31 (l) of every stage's tiles stay zero for the whole kernel
-        if (m >= p.M)
-            for (int s = 0; s < STAGES; ++s) {
-                uint8_t* xt = stages + s * STAGE_BYTES + XT_OFF + g * XT_GROUP;
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    *reinterpret_cast<uint4*>(xt + xt_offset(m, 2 * qk + c)) = make_uint4(0u, 0u, 0u, 0u);
-                    *reinterpret_cast<uint4*>(xt + xt_offset(MROWS + m, 2 * qk + c)) = make_uint4(0u, 0u, 0u, 0u);
-                }
-            }
-        for (int i = 0; i < nu; ++i) {
-            const int s = i % STAGES, slot = i % XS_RING;
-            if (!warp_wait(&bars->full[s], (uint32_t)(i / STAGES) & 1u, abort_flag, p.status, SITE_X)) break;
-            // every lane runs the shuffles below (rows >= M as zeros), so the
-            // full-warp masks hold whatever M is
-            const bool live = m < p.M;
-            uint4 v[4];
-            {
-                const uint4* xraw =
-                    reinterpret_cast<const uint4*>(stages + s * STAGE_BYTES + W_BYTES + m * XRAW_ROW + g * (GROUP * 2)) + qk * 4;
-#pragma unroll
-                for (int r = 0; r < 4; ++r) v[r] = live ? xraw[r] : make_uint4(0u, 0u, 0u, 0u);
-            }
-            // group absmax over the 4 threads of this (row, group)
-            uint32_t amax = 0;
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const uint32_t w4[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) amax = max(amax, max(w4[e] & 0x7FFFu, (w4[e] >> 16) & 0x7FFFu));
-            }
-            amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-            // xi = round(x * 2^(13 - E)), E = the absmax's exponent: |xi| <= 2^14.  A
-            // group whose absmax is below 2^-113 (or zero) is taken as zero.
-            const int ebits = (int)(amax >> 7);
-            const bool usable = ebits >= 14;
-            const float mul = usable ? __uint_as_float((uint32_t)(127 + 13 + 127 - ebits) << 23) : 0.0f;
-            const float scale = usable ? __uint_as_float((uint32_t)(ebits - 13) << 23) : 0.0f;
-            int isum = 0;
-            uint8_t* xt = stages + s * STAGE_BYTES + XT_OFF + g * XT_GROUP;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t hw[4], lw[4];
-#pragma unroll
-                for (int rr = 0; rr < 2; ++rr) {
-                    const uint4 vv = v[2 * c + rr];
-                    const uint32_t w4[4] = {vv.x, vv.y, vv.z, vv.w};
-                    int xiv[8];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        // exact scaling by a power of two, then round half to even via the 1.5 * 2^23 shifter
-                        const float lo = __uint_as_float(w4[e] << 16) * mul;
-                        const float hi = __uint_as_float(w4[e] & 0xFFFF0000u) * mul;
-                        xiv[2 * e] = min(__float_as_int(lo + 12582912.0f) - 0x4B400000, 16383);
-                        xiv[2 * e + 1] = min(__float_as_int(hi + 12582912.0f) - 0x4B400000, 16383);
-                    }
-                    uint32_t hb[8], lb[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        isum += xiv[e];
-                        hb[e] = (uint32_t)(xiv[e] >> 7) & 0xFFu;   // arithmetic shift: floor
-                        lb[e] = (uint32_t)xiv[e] & 0x7Fu;
-                    }
-                    // K order (x0, x2, x4, x6, x1, x3, x5, x7)
-                    hw[2 * rr] = hb[0] | (hb[2] << 8) | (hb[4] << 16) | (hb[6] << 24);
-                    hw[2 * rr + 1] = hb[1] | (hb[3] << 8) | (hb[5] << 16) | (hb[7] << 24);
-                    lw[2 * rr] = lb[0] | (lb[2] << 8) | (lb[4] << 16) | (lb[6] << 24);
-                    lw[2 * rr + 1] = lb[1] | (lb[3] << 8) | (lb[5] << 16) | (lb[7] << 24);
-                }
-                if (live) {
-                    *reinterpret_cast<uint4*>(xt + xt_offset(m, 2 * qk + c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                    *reinterpret_cast<uint4*>(xt + xt_offset(MROWS + m, 2 * qk + c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-                }
-            }
-            isum += __shfl_xor_sync(0xffffffffu, isum, 1);
-            isum += __shfl_xor_sync(0xffffffffu, isum, 2);
-            if (qk == 0) {
-                xscale[(slot * UG + g) * MROWS + m] = scale;
-                xsum[(slot * UG + g) * MROWS + m] = (float)isum;
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // tiles visible to the MMA
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&bars->x_full[s]);
-                mbar_arrive(&bars->xs_full[slot]);
-                mbar_arrive(&bars->empty[s]);
-            }
-        }
     } else if (warp < DW0) {
         // ------------------------------------------------------------ fold
+        asm volatile("griddepcontrol.wait;" ::: "memory");   // the prepared X's scales
         const int q = warp & 3;                     // TMEM lane quarter
         const int n_local = q * 32 + lane;
         const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
@@ -422,8 +355,11 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
             for (int m = 0; m < MROWS; ++m) y[m] = 0.0f;
         };
 
-        // S/Z ring of this warp: [SZ_RING][UG][S: 32 | Z: 32] fp16, filled in unit order
+        // S/Z ring of this warp: [SZ_RING][UG][S: 32 | Z: 32] fp16, filled in unit order,
+        // and the rows' 2^e and sums: [SZ_RING][UG][2^e: 16 | sum: 16] fp32
         uint16_t* my_sz = szring + q * SZ_RING * UG * 64;
+        float* my_xs = xsring + q * SZ_RING * UG * XS_GROUP;
+        const float* xs_src = reinterpret_cast<const float*>(p.xprep + (size_t)p.upt * UG * XT_GROUP);
         UnitPos zpos = start;
         auto fetch_sz = [&](int i) {   // lanes 0-15: scale pairs, 16-31: zero pairs
             if (i < nu) {
@@ -435,6 +371,8 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
                     const bool in = n < p.N && grp < p.G;
                     const __half* src = (lane < 16 ? p.S : p.Z) + (in ? (size_t)grp * p.N + n : 0);
                     cp_async_4(my_sz + ((i % SZ_RING) * UG + g) * 64 + (lane >> 4) * 32 + 2 * w, src, in ? 4u : 0u);
+                    cp_async_4(my_xs + ((i % SZ_RING) * UG + g) * XS_GROUP + lane,
+                               xs_src + (size_t)(zpos.j * UG + g) * XS_GROUP + lane, 4u);
                 }
                 zpos.next(p.upt);
             }
@@ -445,10 +383,8 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
         UnitPos fpos = start;
         for (int i = 0; i < nu; ++i) {
             fetch_sz(i + SZ_AHEAD);
-            const int db = i % ND, slot = i % XS_RING;
-            if (!warp_wait(&bars->d_full[db], (uint32_t)(i / ND) & 1u, abort_flag, p.status, SITE_FOLD) ||
-                !warp_wait(&bars->xs_full[slot], (uint32_t)(i / XS_RING) & 1u, abort_flag, p.status, SITE_FOLD))
-                break;
+            const int db = i % ND;
+            if (!warp_wait(&bars->d_full[db], (uint32_t)(i / ND) & 1u, abort_flag, p.status, SITE_FOLD)) break;
             tc_fence_after();
             cp_async_wait<SZ_AHEAD>();
             __syncwarp();
@@ -460,8 +396,9 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
                 const uint16_t* sz = my_sz + ((i % SZ_RING) * UG + g) * 64;
                 const float sc = __half2float(__ushort_as_half(sz[lane]));
                 const float z = __half2float(__ushort_as_half(sz[32 + lane]));
-                const float4* xs4 = reinterpret_cast<const float4*>(xsum + (slot * UG + g) * MROWS);
-                const float4* xe4 = reinterpret_cast<const float4*>(xscale + (slot * UG + g) * MROWS);
+                const float* xsg = my_xs + ((i % SZ_RING) * UG + g) * XS_GROUP;
+                const float4* xe4 = reinterpret_cast<const float4*>(xsg);
+                const float4* xs4 = reinterpret_cast<const float4*>(xsg + MROWS);
 #pragma unroll
                 for (int m4 = 0; m4 < MROWS / 4; ++m4) {
                     const float4 xs = xs4[m4], xe = xe4[m4];
@@ -489,15 +426,15 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
         const int n_local = q * 32 + lane;
         const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
         for (int i = team; i < nu; i += TEAMS) {
-            const int s = i % STAGES, ab = i % NA;
-            if (!warp_wait(&bars->full[s], (uint32_t)(i / STAGES) & 1u, abort_flag, p.status, SITE_DEQ) ||
+            const int s = i % W_STAGES, ab = i % NA;
+            if (!warp_wait(&bars->w_full[s], (uint32_t)(i / W_STAGES) & 1u, abort_flag, p.status, SITE_DEQ) ||
                 !warp_wait(&bars->a_empty[ab], ((uint32_t)(i / NA) & 1u) ^ 1u, abort_flag, p.status, SITE_DEQ))
                 break;
             tc_fence_after();
 #pragma unroll
             for (int g = 0; g < UG; ++g) {
                 const uint32_t* wsm =
-                    reinterpret_cast<const uint32_t*>(stages + s * STAGE_BYTES) + (g * 16 + 8 * h) * TILE_N + n_local;
+                    reinterpret_cast<const uint32_t*>(wring + s * W_BYTES) + (g * 16 + 8 * h) * TILE_N + n_local;
                 uint32_t a[16];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
@@ -507,13 +444,12 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
                 }
                 tmem_st_32x32b_x16(t_lane + ab * A_COLS + g * (GROUP / 4) + 16 * h, a);
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->w_empty[s]);   // W is in registers / TMEM now
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&bars->a_full[ab]);
-                mbar_arrive(&bars->empty[s]);
-            }
+            if (lane == 0) mbar_arrive(&bars->a_full[ab]);
         }
     }
 
@@ -522,6 +458,86 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_const
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// X for one call, prepared once: CTA j quantises groups 2j and 2j + 1 (thread
+// xi: row m = xi / 8, group g = (xi / 4) % 2, 32-element quarter qk = xi % 4)
+// into the MMA's swizzled tiles and the rows' 2^e and sums.  Rows >= M and
+// groups past K come out as zero tiles with zero scales.
+__global__ void __launch_bounds__(XPREP_THREADS)
+xprep_kernel(const __nv_bfloat16* __restrict__ X, int M, int K, int G, uint8_t* __restrict__ xprep, int G2) {
+    // programmatic stream serialization: X may come from the previous kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int xi = threadIdx.x;
+    const int m = xi >> 3;                      // row 0..15
+    const int g = (xi >> 2) & 1;                // group of the pair
+    const int qk = xi & 3;                      // 32-element quarter of the group: chunks 2qk, 2qk+1
+    const int grp = blockIdx.x * UG + g;
+    const bool live = m < M && grp < G;
+    uint4 v[4];
+    {
+        const uint4* xg = reinterpret_cast<const uint4*>(X + (size_t)(live ? m : 0) * K + (size_t)(live ? grp : 0) * GROUP) + qk * 4;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) v[r] = live ? __ldg(xg + r) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    // group absmax over the 4 threads of this (row, group)
+    uint32_t amax = 0;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const uint32_t w4[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) amax = max(amax, max(w4[e] & 0x7FFFu, (w4[e] >> 16) & 0x7FFFu));
+    }
+    amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    // xi = round(x * 2^(13 - E)), E = the absmax's exponent: |xi| <= 2^14.  A
+    // group whose absmax is below 2^-113 (or zero) is taken as zero.
+    const int ebits = (int)(amax >> 7);
+    const bool usable = ebits >= 14;
+    const float mul = usable ? __uint_as_float((uint32_t)(127 + 13 + 127 - ebits) << 23) : 0.0f;
+    const float scale = usable ? __uint_as_float((uint32_t)(ebits - 13) << 23) : 0.0f;
+    int isum = 0;
+    uint8_t* xt = xprep + (size_t)grp * XT_GROUP;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const uint4 vv = v[2 * c + rr];
+            const uint32_t w4[4] = {vv.x, vv.y, vv.z, vv.w};
+            int xiv[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                // exact scaling by a power of two, then round half to even via the 1.5 * 2^23 shifter
+                const float lo = __uint_as_float(w4[e] << 16) * mul;
+                const float hi = __uint_as_float(w4[e] & 0xFFFF0000u) * mul;
+                xiv[2 * e] = min(__float_as_int(lo + 12582912.0f) - 0x4B400000, 16383);
+                xiv[2 * e + 1] = min(__float_as_int(hi + 12582912.0f) - 0x4B400000, 16383);
+            }
+            uint32_t hb[8], lb[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                isum += xiv[e];
+                hb[e] = (uint32_t)(xiv[e] >> 7) & 0xFFu;   // arithmetic shift: floor
+                lb[e] = (uint32_t)xiv[e] & 0x7Fu;
+            }
+            // K order (x0, x2, x4, x6, x1, x3, x5, x7)
+            hw[2 * rr] = hb[0] | (hb[2] << 8) | (hb[4] << 16) | (hb[6] << 24);
+            hw[2 * rr + 1] = hb[1] | (hb[3] << 8) | (hb[5] << 16) | (hb[7] << 24);
+            lw[2 * rr] = lb[0] | (lb[2] << 8) | (lb[4] << 16) | (lb[6] << 24);
+            lw[2 * rr + 1] = lb[1] | (lb[3] << 8) | (lb[5] << 16) | (lb[7] << 24);
+        }
+        *reinterpret_cast<uint4*>(xt + xt_offset(m, 2 * qk + c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(xt + xt_offset(MROWS + m, 2 * qk + c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    isum += __shfl_xor_sync(0xffffffffu, isum, 1);
+    isum += __shfl_xor_sync(0xffffffffu, isum, 2);
+    if (qk == 0) {
+        float* xs = reinterpret_cast<float*>(xprep + (size_t)G2 * XT_GROUP) + (size_t)grp * XS_GROUP;
+        xs[m] = scale;
+        xs[MROWS + m] = (float)isum;
     }
 }
 
@@ -555,18 +571,21 @@ uint64_t gemv_w4a16_tc_partial_bytes(int N, int K) {
 
 uint64_t gemv_w4a16_tc_ticket_count(int N) { return (uint64_t)((N + w4tc::TILE_N - 1) / w4tc::TILE_N) * w4tc::SLICES; }
 
+uint64_t gemv_w4a16_tc_xprep_bytes(int K) {
+    const int G2 = (K / w4tc::GROUP + w4tc::UG - 1) / w4tc::UG * w4tc::UG;
+    return (uint64_t)G2 * (w4tc::XT_GROUP + w4tc::XS_GROUP * 4);
+}
+
 int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
-                  int K, float* partials, unsigned int* tickets, cudaStream_t stream) {
+                  int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream) {
     QG_CHECK_ARG(mrows >= 1 && mrows <= w4tc::MROWS, "gemv_w4a16_tc: %d rows (1..16)", mrows);
     DeviceStatus* status = nullptr;
     int rc = device_status_ptr(&status);
     if (rc) return rc;
-    CUtensorMap tmW, tmX;
+    QG_CHECK_ARG(((uintptr_t)xprep & 15) == 0, "gemv_w4a16_tc: prepared-X area must be 16-byte aligned");
+    CUtensorMap tmW;
     if ((rc = make_tmap_2d(&tmW, W, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)N, (uint64_t)K / 8, (uint64_t)N * 4,
                            w4tc::TILE_N, w4tc::W_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE)))
-        return rc;
-    if ((rc = make_tmap_2d(&tmX, X, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)K, (uint64_t)mrows, (uint64_t)K * 2,
-                           w4tc::UG * w4tc::GROUP, (uint32_t)mrows, CU_TENSOR_MAP_SWIZZLE_NONE)))
         return rc;
     static bool attr_set[64] = {};
     int dev = 0;
@@ -578,6 +597,7 @@ int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, vo
     }
     const w4tc::Shape s = w4tc::shape_of(N, K);
     w4tc::Params p;
+    p.xprep = static_cast<const uint8_t*>(xprep);
     p.S = static_cast<const __half*>(S);
     p.Z = static_cast<const __half*>(Z);
     p.Y = Y;
@@ -592,8 +612,10 @@ int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, vo
     p.maxp = s.maxp;
     p.out_type = out_type;
     p.status = status;
+    QG_CUDA(launch_pdl(w4tc::xprep_kernel, dim3(s.upt), dim3(w4tc::XPREP_THREADS), 0, stream,
+                       static_cast<const __nv_bfloat16*>(X), mrows, K, s.G, static_cast<uint8_t*>(xprep), s.upt * w4tc::UG));
     QG_CUDA(launch_pdl(w4tc::gemv_w4a16_tc_kernel, dim3(s.ctas), dim3(w4tc::THREADS), (size_t)w4tc::SMEM_BYTES, stream,
-                       tmW, tmX, p));
+                       tmW, p));
     QG_CUDA(cudaGetLastError());
     return QG_OK;
 }
