@@ -42,12 +42,18 @@
 //                 (the largest CUDA-core cost of a unit).
 //   gemv kernel   per CTA, 736 threads (23 warps):
 //   warp 0      W producer: per unit, a TMA load of the W tile (32 packed rows
-//               x 128 columns, no swizzle) into an 11-stage ring (176 KB of W
+//               x 128 columns, no swizzle) into a 4-stage ring (64 KB of W
 //               in flight per SM); a stage is free again as soon as the dequant
 //               team has turned it into TMEM columns, so the HBM stream does not
 //               wait for the MMA or the fold.
-//   warp 2      X producer: per unit, a bulk copy of the unit's two prepared X
-//               tiles into a 4-stage ring, freed by the unit's MMA commit.
+//   warp 2      X producer: per unit, the unit's two prepared X tiles (8 KB,
+//               hot in L2) copied with per-lane 16-byte cp.async into a
+//               10-stage ring freed by the unit's MMA commit, and published
+//               X_LAG units later.  Not a TMA copy: the SM's TMA engine serves
+//               its copies in order, and an X tile queued behind 128 KB of
+//               weight loads arrived ~7 us after issue, which with the ring
+//               refilled only after each MMA held the kernel to one unit per
+//               ~1500 cycles.
 //   warps 7-22  dequant, two teams of 8 taking alternate units (one team's
 //               barrier round trips overlap the other's): each warp owns a TMEM
 //               lane quarter and 8 of the 16 packed rows of a group; lane n
@@ -85,8 +91,14 @@ constexpr int W_ROWS = UG * GROUP / 8;                    // 32 packed rows
 constexpr int W_BYTES = TILE_N * W_ROWS * 4;              // 16 KB
 constexpr int XT_GROUP = MMA_N * GROUP;                   // 4 KB int8 tile per group
 constexpr int XT_BYTES = UG * XT_GROUP;                   // 8 KB: a unit's two X tiles
-constexpr int W_STAGES = 11;                              // W ring: 176 KB
-constexpr int X_STAGES = 4;                               // prepared-X ring: 32 KB
+// Ring depths measured (M=16, 4 rotating weight sets): W 4 / 6 / 8 stages with
+// X 10 took 48.0 / 48.8 / 49.6 us; under this saturated stream every load,
+// L2 hits included, takes ~7 us, so fewer weight bytes in flight shorten the
+// queues the X tiles wait in without costing weight bandwidth.
+constexpr int W_STAGES = 4;                               // W ring: 64 KB
+constexpr int X_STAGES = 10;                              // prepared-X ring: 80 KB
+constexpr int X_LAG = 4;                                  // units between an X copy and its publication
+static_assert(X_LAG < X_STAGES, "X ring depth");
 constexpr int X_RING_OFF = W_STAGES * W_BYTES;
 constexpr int RINGS_BYTES = X_RING_OFF + X_STAGES * XT_BYTES;
 static_assert(X_RING_OFF % 1024 == 0 && XT_BYTES % 1024 == 0, "swizzled tiles need 1 KB alignment");
@@ -252,23 +264,31 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
                 if (armed & (1u << s)) mbar_wait(&bars->w_full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
         }
     } else if (warp == XPW) {
-        // ------------------------------------------------------------ X producer
-        if (lane == 0) {
-            asm volatile("griddepcontrol.wait;" ::: "memory");   // the pre-pass's tiles
-            uint32_t armed = 0, armed_phase = 0;
-            UnitPos pos = start;
-            for (int i = 0; i < nu; ++i, pos.next(p.upt)) {
-                const int s = i % X_STAGES;
-                const uint32_t ph = (uint32_t)(i / X_STAGES) & 1u;
-                if (!mbar_wait(&bars->x_empty[s], ph ^ 1u, abort_flag, p.status, SITE_PRODUCER)) break;
-                mbar_arrive_expect_tx(&bars->x_full[s], XT_BYTES);
-                bulk_load(xring + s * XT_BYTES, p.xprep + (size_t)pos.j * XT_BYTES, XT_BYTES, &bars->x_full[s]);
-                armed |= 1u << s;
-                armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
+        // ------------------------------------------------------------ X producer (whole warp)
+        asm volatile("griddepcontrol.wait;" ::: "memory");   // the pre-pass's tiles
+        auto publish_x = [&](int u) {   // unit u's copies have landed (cp.async.wait_group done)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the MMA
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->x_full[u % X_STAGES]);
+        };
+        UnitPos pos = start;
+        int i = 0;
+        for (; i < nu; ++i, pos.next(p.upt)) {
+            const int s = i % X_STAGES;
+            if (!warp_wait(&bars->x_empty[s], ((uint32_t)(i / X_STAGES) & 1u) ^ 1u, abort_flag, p.status, SITE_PRODUCER))
+                break;
+            const uint8_t* src = p.xprep + (size_t)pos.j * XT_BYTES;
+            uint8_t* dst = xring + s * XT_BYTES;
+#pragma unroll
+            for (int c = 0; c < XT_BYTES / (32 * 16); ++c) cp_async_16(dst + (c * 32 + lane) * 16, src + (c * 32 + lane) * 16);
+            cp_async_commit();
+            if (i >= X_LAG) {
+                cp_async_wait<X_LAG>();
+                publish_x(i - X_LAG);
             }
-            for (int s = 0; s < X_STAGES; ++s)
-                if (armed & (1u << s)) mbar_wait(&bars->x_full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
         }
+        cp_async_wait<0>();   // nothing may still be landing when the CTA exits
+        for (int u = (i > X_LAG ? i - X_LAG : 0); u < i; ++u) publish_x(u);
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {

@@ -99,6 +99,10 @@ __device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc, uin
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(src_bytes)
                  : "memory");
 }
+// 16-byte global -> shared copy through the load/store path (not the TMA engine).
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // Wait until at most N of this thread's most recent groups are pending.
 template <int N>
