@@ -39,7 +39,6 @@ constexpr int ACC_COLS = BN;       // s32 accumulator columns per buffer
 constexpr int TMEM_COLS = 2 * ACC_COLS;
 constexpr int THREADS = 256;
 constexpr int EPI_WARP0 = 4;
-constexpr int GROUP_M = 16;        // tile rasterisation: 16 row-tiles share B tiles in L2
 
 // Operand kinds these kernels run.  The mainloops are the same for all of
 // them (128-byte K rows per stage, 32-byte K steps per MMA: 32 int8 / 16
@@ -55,6 +54,13 @@ enum : int { KIND_I8 = 0, KIND_BF16 = 1, KIND_E4M3 = 2, KIND_F16 = 3, KIND_TF32 
 __host__ __device__ constexpr int elem_bytes(int kind) {
     return (kind == KIND_BF16 || kind == KIND_F16) ? 2 : kind == KIND_TF32 ? 4 : 1;
 }
+// Tile rasterisation: consecutive tiles walk group_m row-tiles (sharing B tiles
+// in L2) before moving to the next columns.  Measured at 8192^3 on the pair
+// kernel (DRAM bytes read per launch): INT8 16 / 8 / 32 row-tiles 222 / 337 /
+// 652 MB; BF16 8 / 16 / 4 / 32 row-tiles 1.09 / 1.25 / 1.44 / 2.05 GB, and 8
+// was also the fastest for the 2-byte kinds.  TF32 (4-byte rows, a slower MMA)
+// ran faster at 16 than at 4 (709 against 668 TFLOP/s).
+__host__ __device__ constexpr int group_m(int kind) { return elem_bytes(kind) == 2 ? 8 : 16; }
 __host__ __device__ constexpr uint32_t kind_idesc(int kind, uint32_t M, uint32_t N) {
     return kind == KIND_I8     ? make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, M, N)
            : kind == KIND_BF16 ? make_idesc(/*f32*/ 1, /*bf16*/ 1, /*bf16*/ 1, M, N)
@@ -106,6 +112,7 @@ struct Params {
     float alpha;            // output scale of the f32-accumulating kinds
 };
 
+template <int GROUP_M>
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
     const int group = GROUP_M * tiles_n;
     const int g = t / group;
@@ -257,7 +264,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             int mt, nt;
-            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            tile_coords<group_m(KIND)>(t, tiles_m, tiles_n, mt, nt);
             for (int kb = 0; kb < nk; ++kb) {
                 if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER)) { ok = false; break; }
                 mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
@@ -314,7 +321,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         int iter = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
             int mt, nt;
-            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            tile_coords<group_m(KIND)>(t, tiles_m, tiles_n, mt, nt);
             const uint32_t acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
             int ok = 1;
@@ -430,7 +437,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         bool ok = true;
         for (int t = pair; t < tiles && ok; t += pairs) {
             int mt, nt;
-            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            tile_coords<group_m(KIND)>(t, tiles_m, tiles_n, mt, nt);
             for (int kb = 0; kb < nk; ++kb) {
                 if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER)) { ok = false; break; }
                 if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * P_STAGE_BYTES);
@@ -491,7 +498,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         int iter = 0;
         for (int t = pair; t < tiles; t += pairs, ++iter) {
             int mt, nt;
-            tile_coords(t, tiles_m, tiles_n, mt, nt);
+            tile_coords<group_m(KIND)>(t, tiles_m, tiles_n, mt, nt);
             const uint32_t acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
             int ok = 1;
