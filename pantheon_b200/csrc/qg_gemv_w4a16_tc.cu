@@ -105,6 +105,7 @@ static_assert(X_RING_OFF % 1024 == 0 && XT_BYTES % 1024 == 0, "swizzled tiles ne
 // prepared X per group in the workspace: the 4 KB tile, then (after all tiles)
 // 16 scales 2^e and 16 sums of xi per group
 constexpr int XS_GROUP = 2 * MROWS;                       // floats per group
+static_assert(XS_GROUP == 32, "the fold warps fetch a group's 2^e and sums with one 4-byte copy per lane");
 constexpr int TEAMS = 2;                      // dequant teams, alternate units
 constexpr int NA = 4;                         // A operand buffers in TMEM
 constexpr int A_COLS = UG * GROUP / 4;        // 64 columns per unit: 2 x 128 bytes per lane
