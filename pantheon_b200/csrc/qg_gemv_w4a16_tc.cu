@@ -84,36 +84,25 @@ namespace w4tc {
 constexpr int TILE_N = 128;                   // weight columns per tile = MMA M
 constexpr int GROUP = 128;                    // K per group (one scale / zero point)
 constexpr int UG = 2;                         // groups per unit
-constexpr int MROWS = 16;                     // activation rows, padded
-constexpr int MMA_N = 2 * MROWS;              // h rows, then l rows
+constexpr int MAX_MROWS = 16;                 // activation rows per launch, at most
 constexpr int UMMA_K = 32;                    // int8 elements per MMA
 constexpr int W_ROWS = UG * GROUP / 8;                    // 32 packed rows
 constexpr int W_BYTES = TILE_N * W_ROWS * 4;              // 16 KB
-constexpr int XT_GROUP = MMA_N * GROUP;                   // 4 KB int8 tile per group
-constexpr int XT_BYTES = UG * XT_GROUP;                   // 8 KB: a unit's two X tiles
 // Ring depths measured (M=16, 4 rotating weight sets): W 4 / 6 / 8 stages with
 // X 10 took 48.0 / 48.8 / 49.6 us; under this saturated stream every load,
 // L2 hits included, takes ~7 us, so fewer weight bytes in flight shorten the
 // queues the X tiles wait in without costing weight bandwidth.
 constexpr int W_STAGES = 4;                               // W ring: 64 KB
-constexpr int X_STAGES = 10;                              // prepared-X ring: 80 KB
+constexpr int X_STAGES = 10;                              // prepared-X ring: 80 KB at 16 rows
 constexpr int X_LAG = 4;                                  // units between an X copy and its publication
 static_assert(X_LAG < X_STAGES, "X ring depth");
 constexpr int X_RING_OFF = W_STAGES * W_BYTES;
-constexpr int RINGS_BYTES = X_RING_OFF + X_STAGES * XT_BYTES;
-static_assert(X_RING_OFF % 1024 == 0 && XT_BYTES % 1024 == 0, "swizzled tiles need 1 KB alignment");
-// prepared X per group in the workspace: the 4 KB tile, then (after all tiles)
-// 16 scales 2^e and 16 sums of xi per group
-constexpr int XS_GROUP = 2 * MROWS;                       // floats per group
-static_assert(XS_GROUP == 32, "the fold warps fetch a group's 2^e and sums with one 4-byte copy per lane");
 constexpr int TEAMS = 2;                      // dequant teams, alternate units
 constexpr int NA = 4;                         // A operand buffers in TMEM
 constexpr int A_COLS = UG * GROUP / 4;        // 64 columns per unit: 2 x 128 bytes per lane
 constexpr int ND = 4;                         // accumulator buffers in TMEM
-constexpr int D_COLS = UG * MMA_N;            // 64 columns per unit
 constexpr int D_COL0 = NA * A_COLS;
 constexpr int TMEM_COLS = 512;
-static_assert(D_COL0 + ND * D_COLS <= TMEM_COLS, "TMEM budget");
 static_assert(NA % TEAMS == 0, "each team cycles through its own A buffers");
 constexpr int SZ_AHEAD = 4;                   // units between an S/Z fetch and its fold
 constexpr int SZ_RING = 8;                    // >= SZ_AHEAD + 1
@@ -128,6 +117,29 @@ static_assert(FW0 + FWARPS == DW0, "the fold warps are the ones between the MMA 
 constexpr int SLICES = FWARPS;                // reduction slices of a tile = lane quarters
 constexpr int W_EMPTY_ARRIVALS = DWARPS;      // the dequant team of the unit
 constexpr int XPREP_THREADS = 128;            // prepass CTA: 16 rows x 2 groups x 4 quarters
+constexpr int SZ_BYTES = FWARPS * SZ_RING * UG * 64 * 2;              // 8 KB: 32 scales + 32 zeros
+
+// Everything that depends on the activation rows a launch carries: MR = 8 for
+// 1..8 rows, 16 for 9..16.  At 8 rows the X tiles and the fold's work are half
+// the 16-row ones: at M = 8 the kernel took 41.2 us against 47.6 us with
+// 16-row tiles (bit-identical results).
+template <int MR>
+struct Tile {
+    static constexpr int MROWS = MR;                      // activation rows, padded
+    static constexpr int MMA_N = 2 * MR;                  // h rows, then l rows
+    static constexpr int XT_GROUP = MMA_N * GROUP;        // int8 tile per group (2 / 4 KB)
+    static constexpr int XT_BYTES = UG * XT_GROUP;        // a unit's two X tiles
+    // prepared X per group in the workspace: the tile, then (after all tiles)
+    // MR scales 2^e and MR sums of xi per group
+    static constexpr int XS_GROUP = 2 * MR;               // floats per group
+    static constexpr int D_COLS = UG * MMA_N;             // accumulator columns per unit
+    static constexpr int RINGS_BYTES = X_RING_OFF + X_STAGES * XT_BYTES;
+    static constexpr int XS_BYTES = FWARPS * SZ_RING * UG * XS_GROUP * 4;   // rows' 2^e and sums
+    static_assert(MR == 8 || MR == 16, "8 or 16 activation rows per tile");
+    static_assert(XS_GROUP <= 32, "the fold warps fetch a group's 2^e and sums with one 4-byte copy per lane");
+    static_assert(X_RING_OFF % 1024 == 0 && XT_GROUP % 1024 == 0, "swizzled tiles need 1 KB alignment");
+    static_assert(D_COL0 + ND * D_COLS <= TMEM_COLS, "TMEM budget");
+};
 
 constexpr uint32_t SITE_PRODUCER = 0x00040001u;
 constexpr uint32_t SITE_MMA = 0x00040002u;
@@ -148,17 +160,18 @@ struct Barriers {
     int abort;
 };
 
-constexpr int SZ_BYTES = FWARPS * SZ_RING * UG * 64 * 2;              // 8 KB: 32 scales + 32 zeros
-constexpr int XS_BYTES = FWARPS * SZ_RING * UG * XS_GROUP * 4;        // 8 KB: rows' 2^e and sums
-constexpr int SMEM_BYTES = RINGS_BYTES + SZ_BYTES + XS_BYTES + (int)sizeof(Barriers) + 1024;
-static_assert(SMEM_BYTES <= 232448, "shared memory budget (227 KB per CTA)");
+template <int MR>
+constexpr int smem_bytes() {
+    return Tile<MR>::RINGS_BYTES + SZ_BYTES + Tile<MR>::XS_BYTES + (int)sizeof(Barriers) + 1024;
+}
+static_assert(smem_bytes<16>() <= 232448 && smem_bytes<8>() <= 232448, "shared memory budget (227 KB per CTA)");
 
 struct Params {
-    const uint8_t* xprep;    // [G2][4 KB] prepared X tiles, then [G2][2][16] fp32 (2^e, sum xi)
+    const uint8_t* xprep;    // [G2][XT_GROUP] prepared X tiles, then [G2][2][MR] fp32 (2^e, sum xi)
     const __half* S;
     const __half* Z;
     void* Y;
-    float* ws;               // [tiles][maxp][SLICES][16 rows][32 lanes] fp32 partials
+    float* ws;               // [tiles][maxp][SLICES][MR rows][32 lanes] fp32 partials
     unsigned int* tickets;   // [tiles][SLICES], zero between calls
     int M, N, K;
     int G;                   // groups = K / 128
@@ -197,16 +210,18 @@ __device__ __forceinline__ int xt_offset(int row, int chunk) {
     return (row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
+template <int MR>
 __global__ void __launch_bounds__(THREADS, 1)
 gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
+    using T = Tile<MR>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     uint8_t* wring = smem;
     uint8_t* xring = smem + X_RING_OFF;
-    uint16_t* szring = reinterpret_cast<uint16_t*>(smem + RINGS_BYTES);
-    float* xsring = reinterpret_cast<float*>(smem + RINGS_BYTES + SZ_BYTES);
-    Barriers* bars = reinterpret_cast<Barriers*>(smem + RINGS_BYTES + SZ_BYTES + XS_BYTES);
+    uint16_t* szring = reinterpret_cast<uint16_t*>(smem + T::RINGS_BYTES);
+    float* xsring = reinterpret_cast<float*>(smem + T::RINGS_BYTES + SZ_BYTES);
+    Barriers* bars = reinterpret_cast<Barriers*>(smem + T::RINGS_BYTES + SZ_BYTES + T::XS_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -278,10 +293,10 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
             const int s = i % X_STAGES;
             if (!warp_wait(&bars->x_empty[s], ((uint32_t)(i / X_STAGES) & 1u) ^ 1u, abort_flag, p.status, SITE_PRODUCER))
                 break;
-            const uint8_t* src = p.xprep + (size_t)pos.j * XT_BYTES;
-            uint8_t* dst = xring + s * XT_BYTES;
+            const uint8_t* src = p.xprep + (size_t)pos.j * T::XT_BYTES;
+            uint8_t* dst = xring + s * T::XT_BYTES;
 #pragma unroll
-            for (int c = 0; c < XT_BYTES / (32 * 16); ++c) cp_async_16(dst + (c * 32 + lane) * 16, src + (c * 32 + lane) * 16);
+            for (int c = 0; c < T::XT_BYTES / (32 * 16); ++c) cp_async_16(dst + (c * 32 + lane) * 16, src + (c * 32 + lane) * 16);
             cp_async_commit();
             if (i >= X_LAG) {
                 cp_async_wait<X_LAG>();
@@ -293,7 +308,7 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t IDESC = make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, TILE_N, MMA_N);
+            constexpr uint32_t IDESC = make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, TILE_N, T::MMA_N);
             bool ok = true, issued = false;
             for (int i = 0; i < nu && ok; ++i) {
                 const int s = i % X_STAGES, ab = i % NA, db = i % ND;
@@ -304,14 +319,14 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
                     break;
                 }
                 tc_fence_after();
-                const uint32_t xt = smem_u32(xring + s * XT_BYTES);
+                const uint32_t xt = smem_u32(xring + s * T::XT_BYTES);
 #pragma unroll
                 for (int k = 0; k < GROUP / UMMA_K; ++k)
 #pragma unroll
                     for (int g = 0; g < UG; ++g)
-                        umma_i8_tmem_a(tmem_base + D_COL0 + db * D_COLS + g * MMA_N,
+                        umma_i8_tmem_a(tmem_base + D_COL0 + db * T::D_COLS + g * T::MMA_N,
                                        tmem_base + ab * A_COLS + g * (GROUP / 4) + k * (UMMA_K / 4),
-                                       make_sdesc_kmajor_sw128(xt + g * XT_GROUP + k * UMMA_K), IDESC, k > 0 ? 1u : 0u);
+                                       make_sdesc_kmajor_sw128(xt + g * T::XT_GROUP + k * UMMA_K), IDESC, k > 0 ? 1u : 0u);
                 issued = true;
                 umma_commit(&bars->d_full[db]);
                 umma_commit(&bars->a_empty[ab]);
@@ -328,9 +343,9 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
         const int q = warp & 3;                     // TMEM lane quarter
         const int n_local = q * 32 + lane;
         const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
-        float y[MROWS];
+        float y[T::MROWS];
 #pragma unroll
-        for (int m = 0; m < MROWS; ++m) y[m] = 0.0f;
+        for (int m = 0; m < T::MROWS; ++m) y[m] = 0.0f;
 
         auto publish = [&](int t) {
             const int n = t * TILE_N + n_local;
@@ -340,7 +355,7 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
             auto store = [&](const float* v) {
                 if (n >= p.N) return;
 #pragma unroll
-                for (int m = 0; m < MROWS; ++m) {
+                for (int m = 0; m < T::MROWS; ++m) {
                     if (m >= p.M) break;
                     if (p.out_type == QG_OUT_F32) static_cast<float*>(p.Y)[(size_t)m * p.N + n] = v[m];
                     else static_cast<__nv_bfloat16*>(p.Y)[(size_t)m * p.N + n] = __float2bfloat16_rn(v[m]);
@@ -350,9 +365,9 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
                 store(y);
             } else {
                 const int piece = (int)blockIdx.x - first;
-                float* dst = p.ws + (((size_t)t * p.maxp + piece) * SLICES + q) * (MROWS * 32);
+                float* dst = p.ws + (((size_t)t * p.maxp + piece) * SLICES + q) * (T::MROWS * 32);
 #pragma unroll
-                for (int m = 0; m < MROWS; ++m) dst[m * 32 + lane] = y[m];
+                for (int m = 0; m < T::MROWS; ++m) dst[m * 32 + lane] = y[m];
                 __threadfence();
                 __syncwarp();
                 unsigned int tk = 0;
@@ -360,27 +375,27 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
                 tk = __shfl_sync(0xffffffffu, tk, 0);
                 if (tk == (unsigned int)np - 1) {
                     __threadfence();
-                    float acc[MROWS];
+                    float acc[T::MROWS];
 #pragma unroll
-                    for (int m = 0; m < MROWS; ++m) acc[m] = 0.0f;
+                    for (int m = 0; m < T::MROWS; ++m) acc[m] = 0.0f;
                     for (int pc = 0; pc < np; ++pc) {
-                        const float* src = p.ws + (((size_t)t * p.maxp + pc) * SLICES + q) * (MROWS * 32);
+                        const float* src = p.ws + (((size_t)t * p.maxp + pc) * SLICES + q) * (T::MROWS * 32);
 #pragma unroll
-                        for (int m = 0; m < MROWS; ++m) acc[m] += __ldcg(src + m * 32 + lane);
+                        for (int m = 0; m < T::MROWS; ++m) acc[m] += __ldcg(src + m * 32 + lane);
                     }
                     store(acc);
                     if (lane == 0) p.tickets[(size_t)t * SLICES + q] = 0;   // ready for the next call
                 }
             }
 #pragma unroll
-            for (int m = 0; m < MROWS; ++m) y[m] = 0.0f;
+            for (int m = 0; m < T::MROWS; ++m) y[m] = 0.0f;
         };
 
         // S/Z ring of this warp: [SZ_RING][UG][S: 32 | Z: 32] fp16, filled in unit order,
         // and the rows' 2^e and sums: [SZ_RING][UG][2^e: 16 | sum: 16] fp32
         uint16_t* my_sz = szring + q * SZ_RING * UG * 64;
-        float* my_xs = xsring + q * SZ_RING * UG * XS_GROUP;
-        const float* xs_src = reinterpret_cast<const float*>(p.xprep + (size_t)p.upt * UG * XT_GROUP);
+        float* my_xs = xsring + q * SZ_RING * UG * T::XS_GROUP;
+        const float* xs_src = reinterpret_cast<const float*>(p.xprep + (size_t)p.upt * UG * T::XT_GROUP);
         UnitPos zpos = start;
         auto fetch_sz = [&](int i) {   // lanes 0-15: scale pairs, 16-31: zero pairs
             if (i < nu) {
@@ -392,8 +407,9 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
                     const bool in = n < p.N && grp < p.G;
                     const __half* src = (lane < 16 ? p.S : p.Z) + (in ? (size_t)grp * p.N + n : 0);
                     cp_async_4(my_sz + ((i % SZ_RING) * UG + g) * 64 + (lane >> 4) * 32 + 2 * w, src, in ? 4u : 0u);
-                    cp_async_4(my_xs + ((i % SZ_RING) * UG + g) * XS_GROUP + lane,
-                               xs_src + (size_t)(zpos.j * UG + g) * XS_GROUP + lane, 4u);
+                    if (lane < T::XS_GROUP)   // one float per lane: 2^e of each row, then the sums
+                        cp_async_4(my_xs + ((i % SZ_RING) * UG + g) * T::XS_GROUP + lane,
+                                   xs_src + (size_t)(zpos.j * UG + g) * T::XS_GROUP + lane, 4u);
                 }
                 zpos.next(p.upt);
             }
@@ -411,23 +427,24 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
             __syncwarp();
 #pragma unroll
             for (int g = 0; g < UG; ++g) {
-                uint32_t r[32];   // D_h (columns 0-15) and D_l (16-31) of the group
-                tmem_ld_32x32b_x32(t_lane + D_COL0 + db * D_COLS + g * MMA_N, r);
+                uint32_t r[T::MMA_N];   // D_h (columns 0..MR-1) and D_l (MR..2MR-1) of the group
+                if constexpr (MR == 16) tmem_ld_32x32b_x32(t_lane + D_COL0 + db * T::D_COLS + g * T::MMA_N, r);
+                else tmem_ld_32x32b_x16(t_lane + D_COL0 + db * T::D_COLS + g * T::MMA_N, r);
                 tmem_ld_wait_regs(r);
                 const uint16_t* sz = my_sz + ((i % SZ_RING) * UG + g) * 64;
                 const float sc = __half2float(__ushort_as_half(sz[lane]));
                 const float z = __half2float(__ushort_as_half(sz[32 + lane]));
-                const float* xsg = my_xs + ((i % SZ_RING) * UG + g) * XS_GROUP;
+                const float* xsg = my_xs + ((i % SZ_RING) * UG + g) * T::XS_GROUP;
                 const float4* xe4 = reinterpret_cast<const float4*>(xsg);
-                const float4* xs4 = reinterpret_cast<const float4*>(xsg + MROWS);
+                const float4* xs4 = reinterpret_cast<const float4*>(xsg + T::MROWS);
 #pragma unroll
-                for (int m4 = 0; m4 < MROWS / 4; ++m4) {
+                for (int m4 = 0; m4 < T::MROWS / 4; ++m4) {
                     const float4 xs = xs4[m4], xe = xe4[m4];
                     const float xsv[4] = {xs.x, xs.y, xs.z, xs.w}, xev[4] = {xe.x, xe.y, xe.z, xe.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int m = 4 * m4 + e;
-                        const int sqx = 8 * (int)r[m] + ((int)r[MROWS + m] >> 4);   // sum_k q xi, exact
+                        const int sqx = 8 * (int)r[m] + ((int)r[T::MROWS + m] >> 4);   // sum_k q xi, exact
                         y[m] = fmaf(sc * xev[e], fmaf(-z, xsv[e], (float)sqx), y[m]);
                     }
                 }
@@ -486,8 +503,10 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
 // xi: row m = xi / 8, group g = (xi / 4) % 2, 32-element quarter qk = xi % 4)
 // into the MMA's swizzled tiles and the rows' 2^e and sums.  Rows >= M and
 // groups past K come out as zero tiles with zero scales.
+template <int MR>
 __global__ void __launch_bounds__(XPREP_THREADS)
 xprep_kernel(const __nv_bfloat16* __restrict__ X, int M, int K, int G, uint8_t* __restrict__ xprep, int G2) {
+    using T = Tile<MR>;
     // programmatic stream serialization: X may come from the previous kernel
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -520,7 +539,7 @@ xprep_kernel(const __nv_bfloat16* __restrict__ X, int M, int K, int G, uint8_t* 
     const float mul = usable ? __uint_as_float((uint32_t)(127 + 13 + 127 - ebits) << 23) : 0.0f;
     const float scale = usable ? __uint_as_float((uint32_t)(ebits - 13) << 23) : 0.0f;
     int isum = 0;
-    uint8_t* xt = xprep + (size_t)grp * XT_GROUP;
+    uint8_t* xt = xprep + (size_t)grp * T::XT_GROUP;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
         uint32_t hw[4], lw[4];
@@ -550,15 +569,17 @@ xprep_kernel(const __nv_bfloat16* __restrict__ X, int M, int K, int G, uint8_t* 
             lw[2 * rr] = lb[0] | (lb[2] << 8) | (lb[4] << 16) | (lb[6] << 24);
             lw[2 * rr + 1] = lb[1] | (lb[3] << 8) | (lb[5] << 16) | (lb[7] << 24);
         }
-        *reinterpret_cast<uint4*>(xt + xt_offset(m, 2 * qk + c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(xt + xt_offset(MROWS + m, 2 * qk + c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        if (m < T::MROWS) {   // an 8-row tile has no rows 8-15 (their threads only join the shuffles)
+            *reinterpret_cast<uint4*>(xt + xt_offset(m, 2 * qk + c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4*>(xt + xt_offset(T::MROWS + m, 2 * qk + c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
     }
     isum += __shfl_xor_sync(0xffffffffu, isum, 1);
     isum += __shfl_xor_sync(0xffffffffu, isum, 2);
-    if (qk == 0) {
-        float* xs = reinterpret_cast<float*>(xprep + (size_t)G2 * XT_GROUP) + (size_t)grp * XS_GROUP;
+    if (qk == 0 && m < T::MROWS) {
+        float* xs = reinterpret_cast<float*>(xprep + (size_t)G2 * T::XT_GROUP) + (size_t)grp * T::XS_GROUP;
         xs[m] = scale;
-        xs[MROWS + m] = (float)isum;
+        xs[T::MROWS + m] = (float)isum;
     }
 }
 
@@ -587,19 +608,19 @@ static Shape shape_of(int N, int K) {
 
 uint64_t gemv_w4a16_tc_partial_bytes(int N, int K) {
     const w4tc::Shape s = w4tc::shape_of(N, K);
-    return (uint64_t)s.tiles * s.maxp * w4tc::SLICES * w4tc::MROWS * 32 * 4;
+    return (uint64_t)s.tiles * s.maxp * w4tc::SLICES * w4tc::MAX_MROWS * 32 * 4;   // enough for either tile
 }
 
 uint64_t gemv_w4a16_tc_ticket_count(int N) { return (uint64_t)((N + w4tc::TILE_N - 1) / w4tc::TILE_N) * w4tc::SLICES; }
 
 uint64_t gemv_w4a16_tc_xprep_bytes(int K) {
     const int G2 = (K / w4tc::GROUP + w4tc::UG - 1) / w4tc::UG * w4tc::UG;
-    return (uint64_t)G2 * (w4tc::XT_GROUP + w4tc::XS_GROUP * 4);
+    return (uint64_t)G2 * (w4tc::Tile<16>::XT_GROUP + w4tc::Tile<16>::XS_GROUP * 4);   // enough for either tile
 }
 
 int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
                   int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream) {
-    QG_CHECK_ARG(mrows >= 1 && mrows <= w4tc::MROWS, "gemv_w4a16_tc: %d rows (1..16)", mrows);
+    QG_CHECK_ARG(mrows >= 1 && mrows <= w4tc::MAX_MROWS, "gemv_w4a16_tc: %d rows (1..16)", mrows);
     DeviceStatus* status = nullptr;
     int rc = device_status_ptr(&status);
     if (rc) return rc;
@@ -612,8 +633,10 @@ int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, vo
     int dev = 0;
     QG_CUDA(cudaGetDevice(&dev));
     if (!attr_set[dev & 63]) {
-        QG_CUDA(cudaFuncSetAttribute(w4tc::gemv_w4a16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     w4tc::SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(w4tc::gemv_w4a16_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     w4tc::smem_bytes<8>()));
+        QG_CUDA(cudaFuncSetAttribute(w4tc::gemv_w4a16_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     w4tc::smem_bytes<16>()));
         attr_set[dev & 63] = true;
     }
     const w4tc::Shape s = w4tc::shape_of(N, K);
@@ -633,10 +656,20 @@ int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, vo
     p.maxp = s.maxp;
     p.out_type = out_type;
     p.status = status;
-    QG_CUDA(launch_pdl(w4tc::xprep_kernel, dim3(s.upt), dim3(w4tc::XPREP_THREADS), 0, stream,
-                       static_cast<const __nv_bfloat16*>(X), mrows, K, s.G, static_cast<uint8_t*>(xprep), s.upt * w4tc::UG));
-    QG_CUDA(launch_pdl(w4tc::gemv_w4a16_tc_kernel, dim3(s.ctas), dim3(w4tc::THREADS), (size_t)w4tc::SMEM_BYTES, stream,
-                       tmW, p));
+    // 8-row tiles for up to 8 rows: half the X traffic and fold work of 16-row ones
+    const __nv_bfloat16* Xb = static_cast<const __nv_bfloat16*>(X);
+    uint8_t* xp = static_cast<uint8_t*>(xprep);
+    if (mrows <= 8) {
+        QG_CUDA(launch_pdl(w4tc::xprep_kernel<8>, dim3(s.upt), dim3(w4tc::XPREP_THREADS), 0, stream, Xb, mrows, K, s.G, xp,
+                           s.upt * w4tc::UG));
+        QG_CUDA(launch_pdl(w4tc::gemv_w4a16_tc_kernel<8>, dim3(s.ctas), dim3(w4tc::THREADS),
+                           (size_t)w4tc::smem_bytes<8>(), stream, tmW, p));
+    } else {
+        QG_CUDA(launch_pdl(w4tc::xprep_kernel<16>, dim3(s.upt), dim3(w4tc::XPREP_THREADS), 0, stream, Xb, mrows, K, s.G, xp,
+                           s.upt * w4tc::UG));
+        QG_CUDA(launch_pdl(w4tc::gemv_w4a16_tc_kernel<16>, dim3(s.ctas), dim3(w4tc::THREADS),
+                           (size_t)w4tc::smem_bytes<16>(), stream, tmW, p));
+    }
     QG_CUDA(cudaGetLastError());
     return QG_OK;
 }
