@@ -13,6 +13,12 @@ The fixtures pin the CPU oracle against independent implementations:
   * formats.json -- e4m3 / f16 / bf16 / e2m1 encodings of a fixed sample of
     fp32 values, from torch / numpy casts (the oracle's converters are checked
     against these).
+  * dense.json -- the tensor-furnace GEMM (mma_virus) of each operand format
+    (bf16, fp16, tf32, e4m3) on the dense generator's operands: C = A B^T from
+    numpy's float64 matmul of the decoded operands, which is exact here (every
+    operand is a multiple of 2^-15 of magnitude at most 1, so every product is a
+    multiple of 2^-30 and a K <= 256 sum fits a double's 53 bits), rounded to
+    fp32 by numpy and to the format's output type by torch's casts.
 The operands themselves come from the oracle's generator (the GPU generator is
 checked against it bit for bit in the GPU tests).
 """
@@ -107,12 +113,39 @@ def formats_fixture() -> dict:
     return res
 
 
+DENSE = {  # format id: (name, storage dtype, decoder, output type name)
+    4: ("bf16", np.uint16, lambda b: torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).float().numpy(), "bf16"),
+    5: ("fp16", np.uint16, lambda b: b.view(np.float16).astype(np.float32), "f16"),
+    6: ("tf32", np.uint32, lambda b: b.view(np.float32), "f32"),
+    7: ("e4m3", np.uint8, lambda b: torch.from_numpy(b).view(torch.float8_e4m3fn).float().numpy(), "bf16"),
+}
+
+
+def dense_case(fmt: int, M: int, N: int, K: int, seed: int) -> dict:
+    name, _, decode, out = DENSE[fmt]
+    A, B = O.dense_operands(fmt, M, N, K, seed)
+    a, b = decode(A).astype(np.float64), decode(B).astype(np.float64)
+    # the exactness premise: multiples of 2^-15, magnitude at most 1
+    for x in (a, b):
+        assert np.all(np.abs(x) <= 1) and np.all(np.mod(x * 32768.0, 1.0) == 0)
+    f32 = (a @ b.T).astype(np.float32)
+    t = torch.from_numpy(f32)
+    outv = {"bf16": lambda: t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16),
+            "f16": lambda: t.to(torch.float16).view(torch.int16).numpy().view(np.uint16),
+            "f32": lambda: f32}[out]()
+    return {"format": fmt, "name": name, "M": M, "N": N, "K": K, "seed": seed, "out_type": out,
+            "A_sha256": sha(A), "B_sha256": sha(B), "f32_sha256": sha(f32), "out_sha256": sha(outv),
+            "f32_head": [float(x) for x in f32.ravel()[:6]]}
+
+
 def main() -> None:
     O.build()
     cases = [int8_case(512, 512, 512, 0), int8_case(130, 200, 48, 3)]
     (HERE / "int8_config1.json").write_text(json.dumps({"cases": cases}, indent=1) + "\n")
     (HERE / "generator.json").write_text(json.dumps(generator_fixture(), indent=1) + "\n")
     (HERE / "formats.json").write_text(json.dumps(formats_fixture(), indent=1) + "\n")
+    dense = [dense_case(f, 48, 40, 256, 9) for f in sorted(DENSE)] + [dense_case(4, 33, 17, 128, 2)]
+    (HERE / "dense.json").write_text(json.dumps({"cases": dense}, indent=1) + "\n")
     print("wrote", sorted(p.name for p in HERE.glob("*.json")))
 
 

@@ -78,3 +78,22 @@ def test_dense_generator_values(oracle, fmt):
         np.testing.assert_array_equal(out, want)
     # distinct tensor ids are distinct streams
     assert not np.array_equal(out, oracle.gen_dense(fmt, n, seed, tid + 1))
+
+
+def test_dense_oracle_matches_golden_known_answers(oracle):
+    """tests/golden/dense.json: each operand format's GEMM on the dense generator's operands,
+    from numpy's float64 matmul (exact for these operands) rounded by numpy / torch casts."""
+    import hashlib
+    import json
+    from pathlib import Path
+    sha = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+    cases = json.loads((Path(__file__).parent / "golden" / "dense.json").read_text())["cases"]
+    assert {c["name"] for c in cases} == {"bf16", "fp16", "tf32", "e4m3"}
+    for c in cases:
+        kind = oracle.DENSE_FORMATS[c["format"]][0]
+        A, B = oracle.dense_operands(c["format"], c["M"], c["N"], c["K"], c["seed"])
+        assert sha(A) == c["A_sha256"] and sha(B) == c["B_sha256"], c["name"]
+        f32 = oracle.gemm_dense(kind, A, B, alpha=1.0, out_type=1)
+        assert sha(f32) == c["f32_sha256"], c["name"]
+        out_type = {"bf16": 0, "f16": 3, "f32": 1}[c["out_type"]]
+        assert sha(oracle.gemm_dense(kind, A, B, alpha=1.0, out_type=out_type)) == c["out_sha256"], c["name"]
