@@ -34,6 +34,9 @@ def test_injected_fault_fails(cuda_device):
     assert "Verification: FAIL" in p.stdout
     assert "[SDC FAULT]" in p.stdout
     assert parse_kernel_output(p.stdout, p.stderr, p.returncode, "quantized_gemm")[2] == "FAIL"
+    # the runner hook reads the binary's count line (what the runner would record in the row)
+    from pantheon_b200 import runner_hook
+    assert runner_hook.row_fields("quantized_gemm", p.stdout)["SDC Mismatches"] >= 1
 
 
 def test_default_configuration_runs(cuda_device):

@@ -54,6 +54,8 @@ def test_injected_fault_fails(cuda_device):
     assert "Verification: FAIL" in p.stdout
     assert "[SDC FAULT][MMA_VIRUS]" in p.stdout
     assert parse_kernel_output(p.stdout, p.stderr, p.returncode, "mma_virus")[2] == "FAIL"
+    from pantheon_b200 import runner_hook
+    assert runner_hook.row_fields("mma_virus", p.stdout)["SDC Mismatches"] >= 1
 
 
 def test_auto_picks_a_format(cuda_device):

@@ -33,7 +33,7 @@ def _bf16_bits(t):
     return t.view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-@pytest.mark.parametrize("M", [1, 16])
+@pytest.mark.parametrize("M", [1, 8, 16])   # CUDA cores; tensor cores with 8- and 16-row activation tiles
 def test_noalloc_matches_workspace_entry_point_twice(cuda_device, oracle, qglib, M):
     N, K = 28672, 8192                       # configs[3]
     X, W, S, Z = pb.gen_w4a16(M, N, K, seed=21 + M)
