@@ -62,6 +62,7 @@ extern "C" {
 #define QG_FMT_FP16   5   /* fp16 x fp16 */
 #define QG_FMT_TF32   6   /* tf32 x tf32 (stored as fp32 words) */
 #define QG_FMT_E4M3   7   /* e4m3 x e4m3, unscaled */
+#define QG_FMT_FP32   8   /* fp32 x fp32 on the CUDA cores (the furnace's fp32 type) */
 
 /* Output element types. */
 #define QG_OUT_BF16   0
@@ -207,6 +208,12 @@ QG_API int  qg_gemm_tf32(const void* A, const void* B, float alpha, void* C, int
                          int M, int N, int K, void* stream);
 QG_API int  qg_gemm_e4m3(const void* A, const void* B, float alpha, void* C, int out_type,
                          int M, int N, int K, void* stream);
+/* The same product with fp32 operands on the CUDA cores (fp32 FMAs, no tf32
+ * rounding): K % 4 == 0, A, B, C 16-byte aligned; out_type bf16, f16 or f32.
+ * Replaces: cuBLASLt's SGEMM of the furnace's fp32 type
+ *   (kernels/common/vendor_gemm.h:296-316, R_32F operands with COMPUTE_32F). */
+QG_API int  qg_gemm_f32(const void* A, const void* B, float alpha, void* C, int out_type,
+                        int M, int N, int K, void* stream);
 
 /* FP8 e4m3 with fp32 block scales:
  *   C[m,n] = out( sum_kb P_kb[m,n] * sa[m,kb] * sb[n/128,kb] ),
@@ -291,10 +298,11 @@ QG_API int  qg_gen_uniform_f32(void* out, uint64_t n, float lo, float hi,
                         uint64_t seed, uint32_t tensor_id, void* stream);
 /* out[i] = standard normal deviate (seed, tensor_id, i), fp32. */
 QG_API int  qg_gen_normal_f32(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream);
-/* Dense tensor-furnace operands (format QG_FMT_BF16 / FP16 / TF32 / E4M3):
+/* Dense tensor-furnace operands (format QG_FMT_BF16 / FP16 / TF32 / E4M3 / FP32):
  * out[i] = fmt_rn(j / 32768 - 1), j = top 16 bits of hash(seed, tensor_id, i);
  * bf16 / fp16 / e4m3 (saturating) round to nearest even; tf32 is the fp32
- * word rounded to nearest even at 10 mantissa bits, low 13 bits zero.
+ * word rounded to nearest even at 10 mantissa bits, low 13 bits zero; fp32
+ * keeps the value as it is (exact).
  * Replaces: pantheon_gemm_fill (kernels/common/vendor_gemm.h:184-191), whose
  * operands are uniform on [-1, 1) in steps of 2^-15. */
 QG_API int  qg_gen_dense(int format, void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, void* stream);

@@ -322,6 +322,7 @@ void qgo_gen_dense(int fmt, void* out, uint64_t n, uint64_t seed, uint32_t tenso
             case QGO_FMT_BF16: ((uint16_t*)out)[i] = qgo_f32_to_bf16(v); break;
             case QGO_FMT_FP16: ((uint16_t*)out)[i] = qgo_f32_to_f16(v); break;
             case QGO_FMT_TF32: ((uint32_t*)out)[i] = qgo_f32_to_tf32_bits(v); break;
+            case QGO_FMT_FP32: ((float*)out)[i] = v; break;
             default: ((uint8_t*)out)[i] = qgo_f32_to_e4m3(v); break;
         }
     }
@@ -329,7 +330,8 @@ void qgo_gen_dense(int fmt, void* out, uint64_t n, uint64_t seed, uint32_t tenso
 
 /* ------------------------------------------------------------------------
  * Tensor-furnace GEMMs: C = alpha * A B^T with bf16 (kind 1), e4m3 (kind 2),
- * fp16 (kind 3) or tf32 (kind 4, fp32 words holding tf32 values) operands;
+ * fp16 (kind 3), tf32 (kind 4, fp32 words holding tf32 values) or fp32
+ * (kind 5) operands;
  * the exact products are summed in double, rounded to fp32, scaled by alpha
  * in fp32, then stored as bf16 (out_type 0), fp32 (1) or fp16 (3).  Rows
  * rows[0..nrows) of C (all when rows is NULL), compact.
@@ -338,7 +340,7 @@ static float dense_operand(int kind, const void* X, size_t i, const float* lut) 
     switch (kind) {
         case 1: return qgo_bf16_to_f32(((const uint16_t*)X)[i]);
         case 3: return qgo_f16_to_f32(((const uint16_t*)X)[i]);
-        case 4: return u2f(((const uint32_t*)X)[i]);
+        case 4: case 5: return u2f(((const uint32_t*)X)[i]);
         default: return lut[((const uint8_t*)X)[i]];
     }
 }

@@ -117,10 +117,11 @@ void qgo_set_threads(int n);
 #define QGO_FMT_FP16 5
 #define QGO_FMT_TF32 6
 #define QGO_FMT_E4M3 7
+#define QGO_FMT_FP32 8
 uint32_t qgo_f32_to_tf32_bits(float x);   /* nearest even at 10 mantissa bits, low 13 bits zero */
 float    qgo_dense_value(uint64_t h);     /* j / 32768 - 1, j = h >> 48 */
 void     qgo_gen_dense(int fmt, void* out, uint64_t n, uint64_t seed, uint32_t tensor_id);
-/* kind 1 bf16, 2 e4m3, 3 fp16, 4 tf32 (fp32 words); out_type 0 bf16, 1 f32, 3 fp16 */
+/* kind 1 bf16, 2 e4m3, 3 fp16, 4 tf32 (fp32 words), 5 fp32; out_type 0 bf16, 1 f32, 3 fp16 */
 void qgo_gemm_dense(int kind, const void* A, const void* B, float alpha, int M, int N, int K,
                     const int32_t* rows, int nrows, int out_type, void* C);
 

@@ -172,11 +172,12 @@ def gemm_fp8(A, B, sa, sb, out_type: int = 0, rows=None):
 
 
 # Dense (tensor-furnace) formats: workload format id -> (GEMM kind, storage dtype).
-FMT_BF16, FMT_FP16, FMT_TF32, FMT_E4M3 = 4, 5, 6, 7
-KIND_BF16, KIND_E4M3, KIND_F16, KIND_TF32 = 1, 2, 3, 4
+FMT_BF16, FMT_FP16, FMT_TF32, FMT_E4M3, FMT_FP32 = 4, 5, 6, 7, 8
+KIND_BF16, KIND_E4M3, KIND_F16, KIND_TF32, KIND_F32 = 1, 2, 3, 4, 5
 DENSE_FORMATS = {FMT_BF16: (KIND_BF16, np.uint16), FMT_FP16: (KIND_F16, np.uint16),
-                 FMT_TF32: (KIND_TF32, np.uint32), FMT_E4M3: (KIND_E4M3, np.uint8)}
-_KIND_DTYPE = {KIND_BF16: np.uint16, KIND_F16: np.uint16, KIND_TF32: np.uint32, KIND_E4M3: np.uint8}
+                 FMT_TF32: (KIND_TF32, np.uint32), FMT_E4M3: (KIND_E4M3, np.uint8), FMT_FP32: (KIND_F32, np.uint32)}
+_KIND_DTYPE = {KIND_BF16: np.uint16, KIND_F16: np.uint16, KIND_TF32: np.uint32, KIND_E4M3: np.uint8,
+               KIND_F32: np.uint32}
 _OUT_DTYPE = {0: np.uint16, 1: np.float32, 3: np.uint16}
 
 
@@ -195,8 +196,8 @@ def dense_operands(fmt: int, M: int, N: int, K: int, seed: int, copy: int = 0):
 
 def gemm_dense(kind: int, A, B, alpha: float = 1.0, out_type: int = 0, rows=None):
     """Oracle tensor-furnace GEMM C = alpha * A B^T: kind 1 = bf16, 3 = fp16 (A, B as uint16
-    bits), 4 = tf32 (uint32 fp32 words), 2 = e4m3 (uint8); out_type 0 = bf16 bits, 1 = f32,
-    3 = fp16 bits."""
+    bits), 4 = tf32 and 5 = fp32 (uint32 fp32 words), 2 = e4m3 (uint8); out_type 0 = bf16 bits,
+    1 = f32, 3 = fp16 bits."""
     dt = _KIND_DTYPE[kind]
     A = np.ascontiguousarray(A, dtype=dt)
     B = np.ascontiguousarray(B, dtype=dt)

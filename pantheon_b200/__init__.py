@@ -25,6 +25,7 @@ from ._lib import (  # noqa: F401
     QG_FMT_FP16,
     QG_FMT_TF32,
     QG_FMT_E4M3,
+    QG_FMT_FP32,
     QG_OUT_BF16,
     QG_OUT_F32,
     QG_OUT_S32,
@@ -39,6 +40,7 @@ from .ops import (  # noqa: F401
     gemm_bf16,
     gemm_f16,
     gemm_tf32,
+    gemm_f32,
     gemm_e4m3,
     gemm_i8,
     gemm_nvfp4,
@@ -57,10 +59,10 @@ from .ops import (  # noqa: F401
 
 __all__ = [
     "LIB_PATH", "BIN_PATH", "DECODE_BIN_PATH", "MMA_BIN_PATH", "QGError", "load_library", "Workload",
-    "device_status", "gemm_i8", "gemm_fp8_b128", "gemm_bf16", "gemm_f16", "gemm_tf32", "gemm_e4m3", "gen_dense",
+    "device_status", "gemm_i8", "gemm_fp8_b128", "gemm_bf16", "gemm_f16", "gemm_tf32", "gemm_f32", "gemm_e4m3", "gen_dense",
     "gen_fp8", "gemm_nvfp4", "gen_nvfp4", "nvfp4_sf_bytes", "gemv_w4a16", "gemv_w4a16_workspace_bytes",
     "gen_w4a16", "gen_i8", "gen_uniform_f32", "gen_normal_f32", "verify_words",
     "QG_FMT_INT8", "QG_FMT_FP8", "QG_FMT_NVFP4", "QG_FMT_W4A16",
-    "QG_FMT_BF16", "QG_FMT_FP16", "QG_FMT_TF32", "QG_FMT_E4M3",
+    "QG_FMT_BF16", "QG_FMT_FP16", "QG_FMT_TF32", "QG_FMT_E4M3", "QG_FMT_FP32",
     "QG_OUT_BF16", "QG_OUT_F32", "QG_OUT_S32", "QG_OUT_F16",
 ]

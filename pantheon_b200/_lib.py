@@ -19,7 +19,7 @@ QG_ERR_UNSUPPORTED = -3
 QG_ERR_DEVICE_TIMEOUT = 1
 
 QG_FMT_INT8, QG_FMT_FP8, QG_FMT_NVFP4, QG_FMT_W4A16 = 0, 1, 2, 3
-QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3 = 4, 5, 6, 7
+QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3, QG_FMT_FP32 = 4, 5, 6, 7, 8
 QG_OUT_BF16, QG_OUT_F32, QG_OUT_S32, QG_OUT_F16 = 0, 1, 2, 3
 
 
@@ -67,6 +67,7 @@ _SIGNATURES = {
     "qg_gemm_e4m3": (C.c_int, [_V, _V, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gemm_f16": (C.c_int, [_V, _V, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gemm_tf32": (C.c_int, [_V, _V, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
+    "qg_gemm_f32": (C.c_int, [_V, _V, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gen_dense": (C.c_int, [C.c_int, _V, C.c_uint64, C.c_uint64, C.c_uint32, _V]),
     "qg_pci_bus_id": (C.c_int, [C.c_int, C.c_char_p, C.c_int]),
     "qg_gen_fp8": (C.c_int, [_V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint32, _V]),

@@ -13,7 +13,7 @@ static int out_elem_bytes(int out_type) { return (out_type == QG_OUT_BF16 || out
 uint32_t dense_elem_bytes(int fmt) {
     switch (fmt) {
         case QG_FMT_BF16: case QG_FMT_FP16: return 2;
-        case QG_FMT_TF32: return 4;
+        case QG_FMT_TF32: case QG_FMT_FP32: return 4;
         case QG_FMT_E4M3: return 1;
         default: return 0;
     }
@@ -97,7 +97,8 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
         case QG_FMT_BF16:
         case QG_FMT_FP16:
         case QG_FMT_TF32:
-        case QG_FMT_E4M3: {
+        case QG_FMT_E4M3:
+        case QG_FMT_FP32: {
             // The tensor furnace: C = A B^T at 8192^3 by default, as the
             // reference's vendor GEMM (vendor_gemm.h:38).
             const uint32_t eb = dense_elem_bytes(cfg.format);
@@ -153,7 +154,8 @@ int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_inde
         case QG_FMT_BF16:
         case QG_FMT_FP16:
         case QG_FMT_TF32:
-        case QG_FMT_E4M3: {
+        case QG_FMT_E4M3:
+        case QG_FMT_FP32: {
             const uint32_t eb = dense_elem_bytes(cfg.format);
             if ((rc = gen_dense(cfg.format, cp.op[0], L.op_bytes[0] / eb, seed, base + 0, s))) return rc;
             return gen_dense(cfg.format, cp.op[1], L.op_bytes[1] / eb, seed, base + 1, s);
@@ -181,6 +183,8 @@ int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaS
         case QG_FMT_TF32:
         case QG_FMT_E4M3:
             return gemm_dense_format(cfg.format, cp.op[0], cp.op[1], 1.0f, cp.out, L.out_type, L.M, L.N, L.K, s);
+        case QG_FMT_FP32:
+            return gemm_f32(cp.op[0], cp.op[1], 1.0f, cp.out, L.out_type, L.M, L.N, L.K, s);
         default:
             set_error("format %d is not available in this build", cfg.format);
             return QG_ERR_ARG;

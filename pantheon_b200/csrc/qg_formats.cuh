@@ -47,6 +47,8 @@ int gen_dense(int fmt, void* out, uint64_t n, uint64_t seed, uint32_t tensor_id,
 int gemm_dense_format(int fmt, const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
                       cudaStream_t stream);
 uint32_t dense_elem_bytes(int fmt);
+int gemm_f32(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
+             cudaStream_t stream);
 int gen_uniform(void* out, uint64_t n, float lo, float hi, uint64_t seed, uint32_t tensor_id, cudaStream_t s);
 int gen_normal(void* out, uint64_t n, uint64_t seed, uint32_t tensor_id, cudaStream_t s);
 int gen_fp8(void* A, void* SA, void* B, void* SB, int M, int N, int K, uint64_t seed, uint32_t tid0, cudaStream_t s);

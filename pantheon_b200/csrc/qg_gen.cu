@@ -129,6 +129,7 @@ __global__ void gen_dense_kernel(void* out, uint64_t n, uint64_t key) {
         if constexpr (FMT == QG_FMT_BF16) static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
         else if constexpr (FMT == QG_FMT_FP16) static_cast<__half*>(out)[i] = __float2half_rn(v);
         else if constexpr (FMT == QG_FMT_TF32) static_cast<uint32_t*>(out)[i] = tf32_rn_bits(v);
+        else if constexpr (FMT == QG_FMT_FP32) static_cast<float*>(out)[i] = v;
         else static_cast<uint8_t*>(out)[i] = to_e4m3(v);
     }
 }
@@ -282,6 +283,7 @@ int gen_dense(int fmt, void* out, uint64_t n, uint64_t seed, uint32_t tensor_id,
         case QG_FMT_FP16: gen::gen_dense_kernel<QG_FMT_FP16><<<grid, 256, 0, s>>>(out, n, key); break;
         case QG_FMT_TF32: gen::gen_dense_kernel<QG_FMT_TF32><<<grid, 256, 0, s>>>(out, n, key); break;
         case QG_FMT_E4M3: gen::gen_dense_kernel<QG_FMT_E4M3><<<grid, 256, 0, s>>>(out, n, key); break;
+        case QG_FMT_FP32: gen::gen_dense_kernel<QG_FMT_FP32><<<grid, 256, 0, s>>>(out, n, key); break;
         default: set_error("qg_gen_dense: format %d is not a dense format", fmt); return QG_ERR_ARG;
     }
     QG_CUDA(cudaGetLastError());

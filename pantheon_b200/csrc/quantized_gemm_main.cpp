@@ -17,17 +17,17 @@
 // cuBLASLt GEMM chosen by the vendor-GEMM flags (kernels/common/vendor_gemm.h:
 // 32-55: --gemm_type bf16|fp16|tf32|fp32|fp8|auto, --gemm_size, --gemm_m/n/k,
 // --gemm_probe_ms, --gemm_margin, --gemm) and falls back to a WMMA loop.  Here
-// every format runs on this library's tcgen05 GEMMs; the WMMA knobs
+// the tensor-core formats run on this library's tcgen05 GEMMs and fp32 on its
+// CUDA-core GEMM (the reference's fp32 type is an SGEMM too); the WMMA knobs
 // (--block_size, --grid_size, --sync_mode, --mma_acc, --mma_groups,
 // --mma_reuse, --init_pattern, --kernel_loops) are accepted and ignored, as
-// the reference's vendor-GEMM path ignores them.  fp32 operands without tf32
-// rounding have no tensor-core path and are refused.
+// the reference's vendor-GEMM path ignores them.
 //
 // Process contract (kept from the reference):
 //   argv   <device> <duration_s> <mem_pct> [--verify] [--inject_error]
 //          [--block_size N] [--grid_size N] [--kernel_loops N] [--warmup_iters N]
 //          [--sync_mode N]                       (ai_workload_template.h:351-356)
-//          new: --format int8|fp8|nvfp4|w4a16|bf16|fp16|tf32|e4m3, --m/--n/--k N,
+//          new: --format int8|fp8|nvfp4|w4a16|bf16|fp16|tf32|e4m3|fp32, --m/--n/--k N,
 //          --seed S, --copies N
 //          Unknown flags are ignored, as the reference's parser ignores them.
 //   stdout "[PANTHEON] GPU <id>: ..." and "  -> ..." lines (kept in the runner's log),
@@ -103,7 +103,9 @@ struct Options {
     int probe_ms = 1500, margin_pct = 15;
 };
 
-bool is_dense(int f) { return f == QG_FMT_BF16 || f == QG_FMT_FP16 || f == QG_FMT_TF32 || f == QG_FMT_E4M3; }
+bool is_dense(int f) {
+    return f == QG_FMT_BF16 || f == QG_FMT_FP16 || f == QG_FMT_TF32 || f == QG_FMT_E4M3 || f == QG_FMT_FP32;
+}
 
 const char* format_name(int f) {
     switch (f) {
@@ -115,6 +117,7 @@ const char* format_name(int f) {
         case QG_FMT_FP16: return "FP16";
         case QG_FMT_TF32: return "TF32";
         case QG_FMT_E4M3: return "FP8 (E4M3)";
+        case QG_FMT_FP32: return "FP32";
         default: return "?";
     }
 }
@@ -128,6 +131,7 @@ int parse_format(const std::string& s) {
     if (s == "fp16") return QG_FMT_FP16;
     if (s == "tf32") return QG_FMT_TF32;
     if (s == "e4m3") return QG_FMT_E4M3;
+    if (s == "fp32") return QG_FMT_FP32;
     return -1;
 }
 
@@ -138,13 +142,14 @@ int parse_gemm_type(const std::string& s) {
     if (!strcasecmp(s.c_str(), "fp16")) return QG_FMT_FP16;
     if (!strcasecmp(s.c_str(), "tf32")) return QG_FMT_TF32;
     if (!strcasecmp(s.c_str(), "fp8")) return QG_FMT_E4M3;
+    if (!strcasecmp(s.c_str(), "fp32")) return QG_FMT_FP32;
     return -1;
 }
 
 // Output type of each dense format: the operand type, fp32 for tf32, bf16 for
 // fp8 (vendor_gemm.h:241).
 int dense_out_type(int f) {
-    return f == QG_FMT_FP16 ? QG_OUT_F16 : f == QG_FMT_TF32 ? QG_OUT_F32 : QG_OUT_BF16;
+    return f == QG_FMT_FP16 ? QG_OUT_F16 : (f == QG_FMT_TF32 || f == QG_FMT_FP32) ? QG_OUT_F32 : QG_OUT_BF16;
 }
 
 int fail(const std::string& why) {
@@ -214,7 +219,7 @@ qg_cfg dense_cfg(int fmt, int m, int n, int k, uint64_t seed) {
 // than margin_pct more power (the selection rule of vendor_gemm.h:426-505).
 // Without a meter the default is used.
 int pick_by_power(const Options& o, int m, int n, int k, uint64_t free_b) {
-    static const int order[] = {QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3};
+    static const int order[] = {QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3, QG_FMT_FP32};
     EnergyMeter meter;
     const bool metered = o.probe_ms > 0 && meter.open(o.device);
     if (!metered) std::cout << "  -> No energy meter (or --gemm_probe_ms 0): the default order decides" << std::endl;
@@ -329,12 +334,9 @@ int main(int argc, char* argv[]) {
     const bool auto_type = furnace && !strcasecmp(o.gemm_type.c_str(), "auto");
     if (furnace) {
         if (!auto_type && !o.gemm_type.empty()) {
-            if (!strcasecmp(o.gemm_type.c_str(), "fp32"))
-                return fail("--gemm_type fp32 has no tensor-core path on sm_100a (fp32 operands run on the "
-                            "tensor cores as tf32: --gemm_type tf32).");
             o.format = parse_gemm_type(o.gemm_type);
             if (o.format < 0)
-                return fail("Unknown --gemm_type '" + o.gemm_type + "'. Use auto, bf16, fp16, tf32 or fp8.");
+                return fail("Unknown --gemm_type '" + o.gemm_type + "'. Use auto, bf16, fp16, tf32, fp32 or fp8.");
         }
         if (o.gemm_m < 16 || o.gemm_n < 16 || o.gemm_k < 16) return fail("--gemm_m/n/k must each be at least 16.");
     }
@@ -394,8 +396,9 @@ int main(int argc, char* argv[]) {
     if (furnace) {
         std::cout << "  -> Duration (s):  " << o.duration << std::endl;
         std::cout << "  -> Warmup Iters:  " << o.warmup_iters << std::endl;
-        std::cout << "  -> Tensor Engine: tcgen05 GEMM (" << format_name(o.format) << " " << cfg.m << "x" << cfg.n
-                  << "x" << cfg.k << ", FP32 accumulate)" << std::endl;
+        std::cout << "  -> Tensor Engine: " << (o.format == QG_FMT_FP32 ? "CUDA-core FP32 GEMM (" : "tcgen05 GEMM (")
+                  << format_name(o.format) << " " << cfg.m << "x" << cfg.n << "x" << cfg.k << ", FP32 accumulate)"
+                  << std::endl;
         std::cout << "  -> Verify Mode:   " << (o.verify ? "ON" : "OFF") << std::endl;
     } else {
         std::cout << "[PANTHEON] GPU " << o.device << ": " << kWorkload << " (" << format_name(o.format)

@@ -11,7 +11,7 @@ import ctypes as C
 
 import torch
 
-from ._lib import (QG_FMT_INT8, QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3, QG_OUT_BF16, QG_OUT_F16,
+from ._lib import (QG_FMT_INT8, QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3, QG_FMT_FP32, QG_OUT_BF16, QG_OUT_F16,
                    QG_OUT_F32, QG_OUT_S32, QGCfg, QGMismatch, QGError, check,
                    last_error, load_library)
 
@@ -115,6 +115,12 @@ def gemm_tf32(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: in
     return _gemm_dense("qg_gemm_tf32", A, B, alpha, out_type, out)
 
 
+def gemm_f32(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: int = QG_OUT_F32,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """C = alpha * A @ B^T with fp32 operands and fp32 FMAs on the CUDA cores: A, B fp32 [M,K] / [N,K]."""
+    return _gemm_dense("qg_gemm_f32", A, B, alpha, out_type, out)
+
+
 def gemm_e4m3(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: int = QG_OUT_BF16,
               out: torch.Tensor | None = None) -> torch.Tensor:
     """C = alpha * A @ B^T (fp32 accumulate) on the tcgen05 e4m3 path: A, B e4m3 bytes [M,K] / [N,K]."""
@@ -122,7 +128,7 @@ def gemm_e4m3(A: torch.Tensor, B: torch.Tensor, alpha: float = 1.0, out_type: in
 
 
 _DENSE_DTYPES = {QG_FMT_BF16: torch.bfloat16, QG_FMT_FP16: torch.float16, QG_FMT_TF32: torch.float32,
-                 QG_FMT_E4M3: torch.uint8}
+                 QG_FMT_E4M3: torch.uint8, QG_FMT_FP32: torch.float32}
 
 
 def gen_dense(fmt: int, rows: int, cols: int, seed: int, tensor_id: int, device="cuda") -> torch.Tensor:

@@ -86,7 +86,7 @@ def test_library_rejects_bad_shapes_before_touching_a_device(qglib):
     assert b.value == 8192 * 8192 * 2 + 8 * 8192 + 2 * 8192 * 8192 * 2 + 2 * 4 * 8192 + 4096
 
 
-@pytest.mark.parametrize("gemm_type, why", [("fp32", "no tensor-core path"), ("int4", "Unknown --gemm_type")])
+@pytest.mark.parametrize("gemm_type, why", [("int4", "Unknown --gemm_type"), ("fp64", "Unknown --gemm_type")])
 def test_mma_virus_rejects_gemm_types_it_cannot_run(qglib, gemm_type, why):
     """vendor_gemm.h:525-529: an unknown --gemm_type is an error (exit 1), checked before any device call."""
     from pantheon_b200 import MMA_BIN_PATH

@@ -1,5 +1,5 @@
-"""Tensor-furnace GEMMs (bf16 / fp16 / tf32 / e4m3 operands, fp32 accumulate) on the
-tcgen05 path against the CPU oracle: f32 output within 1e-4 relative (accumulation
+"""Tensor-furnace GEMMs (bf16 / fp16 / tf32 / e4m3 operands on the tcgen05 path, fp32
+operands on the CUDA-core path; fp32 accumulate) against the CPU oracle: f32 output within 1e-4 relative (accumulation
 order), bf16 / fp16 output within 1e-2 (|y - ref| <= tol * max(|ref|, rms(ref))).
 M >= 256 runs on CTA pairs.  Also the dense workload contexts: operands from the
 generator bit-exact against the oracle's restatement, golden / verify / inject."""
@@ -19,6 +19,7 @@ KINDS = {
     "e4m3": (2, pb.gemm_e4m3),
     "fp16": (3, pb.gemm_f16),
     "tf32": (4, pb.gemm_tf32),
+    "fp32": (5, pb.gemm_f32),
 }
 
 
@@ -41,6 +42,9 @@ def _operands(name, M, N, K, seed):
         bits = t.view(torch.int16).numpy().view(np.uint16)
     elif name == "tf32":
         t = _tf32(x)
+        bits = t.view(torch.int32).numpy().view(np.uint32)
+    elif name == "fp32":
+        t = x.contiguous()
         bits = t.view(torch.int32).numpy().view(np.uint32)
     else:
         t = (x * 40).to(torch.float8_e4m3fn).view(torch.uint8)
@@ -83,11 +87,12 @@ def test_dense_gemm_is_reproducible(cuda_device):
 
 
 FORMATS = {pb.QG_FMT_BF16: (1, pb.QG_OUT_BF16, np.uint16), pb.QG_FMT_FP16: (3, pb.QG_OUT_F16, np.uint16),
-           pb.QG_FMT_TF32: (4, pb.QG_OUT_F32, np.uint32), pb.QG_FMT_E4M3: (2, pb.QG_OUT_BF16, np.uint8)}
+           pb.QG_FMT_TF32: (4, pb.QG_OUT_F32, np.uint32), pb.QG_FMT_E4M3: (2, pb.QG_OUT_BF16, np.uint8),
+           pb.QG_FMT_FP32: (5, pb.QG_OUT_F32, np.uint32)}
 _ORACLE_OUT = {pb.QG_OUT_BF16: 0, pb.QG_OUT_F32: 1, pb.QG_OUT_F16: 3}
 
 
-@pytest.mark.parametrize("fmt", list(FORMATS), ids=["bf16", "fp16", "tf32", "e4m3"])
+@pytest.mark.parametrize("fmt", list(FORMATS), ids=["bf16", "fp16", "tf32", "e4m3", "fp32"])
 def test_dense_workload_matches_oracle(cuda_device, oracle, fmt):
     """The workload's own operands (generator stream) bit-exact against the oracle's,
     its GEMM within tolerance on sampled rows, golden / verify / inject on the device."""

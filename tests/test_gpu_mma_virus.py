@@ -1,9 +1,9 @@
-"""The mma_virus drop-in binary (dense tcgen05 tensor furnace) on a B200, read the way the
+"""The mma_virus drop-in binary (dense tcgen05 tensor furnace; fp32 on the CUDA cores) on a B200, read the way the
 runner reads it.
 
 Same argv and vendor-GEMM flags as the reference's mma_virus (kernels/mma_virus/mma_virus.cpp:
 181-441 with kernels/common/vendor_gemm.h:32-55): default BF16 8192^3 with FP32 accumulate,
-`--gemm_type bf16|fp16|tf32|fp8|auto`, `--gemm_size` / `--gemm_m/n/k`; `Throughput: <x> TFLOPS`,
+`--gemm_type bf16|fp16|tf32|fp32|fp8|auto`, `--gemm_size` / `--gemm_m/n/k`; `Throughput: <x> TFLOPS`,
 every batch compared bitwise with the first GEMM's output, `Verification: PASS|FAIL (<n> errors)`,
 exit 1 on a mismatch.
 """
@@ -32,13 +32,15 @@ def test_default_furnace_verifies(cuda_device):
 
 
 @pytest.mark.parametrize("gemm_type, name", [("fp16", "FP16"), ("tf32", "TF32"), ("fp8", "FP8 (E4M3)"),
-                                             ("BF16", "BF16")])
+                                             ("BF16", "BF16"), ("fp32", "FP32")])
 def test_gemm_types_verify(cuda_device, gemm_type, name):
     p = _run(0, 1, 50, "--verify", "--gemm_type", gemm_type, "--gemm_size", 4096)
     assert p.returncode == 0, p.stdout + p.stderr
     t, unit, status, _, _ = parse_kernel_output(p.stdout, p.stderr, p.returncode, "mma_virus")
     assert status == "PASS" and unit == "TFLOPS" and t > 0
     assert f"({name} 4096x4096x4096" in p.stdout
+    engine = "CUDA-core FP32 GEMM" if name == "FP32" else "tcgen05 GEMM"
+    assert f"Tensor Engine: {engine} ({name} 4096x4096x4096" in p.stdout
 
 
 def test_gemm_shape_flags_round_to_16(cuda_device):
@@ -64,7 +66,7 @@ def test_auto_picks_a_format(cuda_device):
     assert p.returncode == 0, p.stdout + p.stderr
     assert "-> Selected " in p.stdout
     if "No energy meter" not in p.stdout:
-        for name in ("BF16", "FP16", "TF32", "FP8 (E4M3)"):
+        for name in ("BF16", "FP16", "TF32", "FP8 (E4M3)", "FP32"):
             assert f"-> Probe {name}:" in p.stdout
     assert parse_kernel_output(p.stdout, p.stderr, p.returncode, "mma_virus")[2] == "PASS"
 

@@ -1,4 +1,4 @@
-"""The tensor-furnace GEMM oracle (bf16 / fp16 / tf32 / e4m3 operands, fp32
+"""The tensor-furnace GEMM oracle (bf16 / fp16 / tf32 / e4m3 / fp32 operands, fp32
 accumulate) and the dense operand generator, checked against float64 numpy and
 torch's own format casts on the decoded operands (no GPU)."""
 import numpy as np
@@ -25,11 +25,13 @@ def _encode(kind, x):
     if kind == 4:
         v = _tf32_numpy(x)
         return v.view(np.uint32), v
+    if kind == 5:
+        return x.view(np.uint32), x
     q = (t * 40).to(torch.float8_e4m3fn)
     return q.view(torch.uint8).numpy(), q.float().numpy()
 
 
-@pytest.mark.parametrize("kind", [1, 2, 3, 4])
+@pytest.mark.parametrize("kind", [1, 2, 3, 4, 5])
 def test_dense_oracle_matches_numpy(oracle, kind):
     M, N, K = 5, 7, 96
     rng = np.random.default_rng(kind)
@@ -59,7 +61,7 @@ def test_tf32_rounding_matches_numpy(oracle):
     assert np.all(got & 0x1FFF == 0)
 
 
-@pytest.mark.parametrize("fmt", [4, 5, 6, 7])
+@pytest.mark.parametrize("fmt", [4, 5, 6, 7, 8])
 def test_dense_generator_values(oracle, fmt):
     """Every generated operand is fmt(j / 32768 - 1) for the element's own hash."""
     n, seed, tid = 3000, 11, 9
@@ -69,6 +71,8 @@ def test_dense_generator_values(oracle, fmt):
     assert np.all(v >= -1.0) and np.all(v < 1.0)
     if fmt == 6:
         np.testing.assert_array_equal(out, _tf32_numpy(v).view(np.uint32))
+    elif fmt == 8:
+        np.testing.assert_array_equal(out, v.view(np.uint32))
     else:
         kind = {4: 1, 5: 3, 7: 2}[fmt]
         if kind == 2:
