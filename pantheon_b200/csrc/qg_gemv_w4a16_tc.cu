@@ -102,6 +102,14 @@ constexpr int NA = 4;                         // A operand buffers in TMEM
 constexpr int A_COLS = UG * GROUP / 4;        // 64 columns per unit: 2 x 128 bytes per lane
 constexpr int ND = 4;                         // accumulator buffers in TMEM
 constexpr int D_COL0 = NA * A_COLS;
+// One MMA commit per unit, to mma_done[unit % DONE_RING]: the fold (its
+// accumulators), the dequant team (its A buffer, NA units later) and the X
+// producer (its X stage, X_STAGES units later) all wait on that one barrier.
+// Three commits per unit (one per consumer) slowed the issuing thread by ~20
+// cycles per MMA.  The ring is deeper than the MMA can run ahead of any
+// waiter (X_STAGES - 1 units), so no waiter sees a barrier two phases on.
+constexpr int DONE_RING = 16;
+static_assert(DONE_RING > X_STAGES && DONE_RING > NA && DONE_RING > ND, "mma_done ring depth");
 constexpr int TMEM_COLS = 512;
 static_assert(NA % TEAMS == 0, "each team cycles through its own A buffers");
 constexpr int SZ_AHEAD = 4;                   // units between an S/Z fetch and its fold
@@ -150,11 +158,9 @@ struct Barriers {
     uint64_t w_full[W_STAGES];
     uint64_t w_empty[W_STAGES];
     uint64_t x_full[X_STAGES];
-    uint64_t x_empty[X_STAGES];
     uint64_t a_full[NA];
-    uint64_t a_empty[NA];
-    uint64_t d_full[ND];
     uint64_t d_empty[ND];
+    uint64_t mma_done[DONE_RING];
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -241,9 +247,10 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < W_STAGES; ++s) { mbar_init(&bars->w_full[s], 1); mbar_init(&bars->w_empty[s], W_EMPTY_ARRIVALS); }
-        for (int s = 0; s < X_STAGES; ++s) { mbar_init(&bars->x_full[s], 1); mbar_init(&bars->x_empty[s], 1); }
-        for (int b = 0; b < NA; ++b) { mbar_init(&bars->a_full[b], DWARPS); mbar_init(&bars->a_empty[b], 1); }
-        for (int b = 0; b < ND; ++b) { mbar_init(&bars->d_full[b], 1); mbar_init(&bars->d_empty[b], FWARPS); }
+        for (int s = 0; s < X_STAGES; ++s) mbar_init(&bars->x_full[s], 1);
+        for (int b = 0; b < NA; ++b) mbar_init(&bars->a_full[b], DWARPS);
+        for (int b = 0; b < ND; ++b) mbar_init(&bars->d_empty[b], FWARPS);
+        for (int b = 0; b < DONE_RING; ++b) mbar_init(&bars->mma_done[b], 1);
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
         fence_barrier_init();
@@ -291,8 +298,12 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
         int i = 0;
         for (; i < nu; ++i, pos.next(p.upt)) {
             const int s = i % X_STAGES;
-            if (!warp_wait(&bars->x_empty[s], ((uint32_t)(i / X_STAGES) & 1u) ^ 1u, abort_flag, p.status, SITE_PRODUCER))
-                break;
+            if (i >= X_STAGES) {   // the MMA of the stage's previous unit is complete
+                const int j = i - X_STAGES;
+                if (!warp_wait(&bars->mma_done[j % DONE_RING], (uint32_t)(j / DONE_RING) & 1u, abort_flag, p.status,
+                               SITE_PRODUCER))
+                    break;
+            }
             const uint8_t* src = p.xprep + (size_t)pos.j * T::XT_BYTES;
             uint8_t* dst = xring + s * T::XT_BYTES;
 #pragma unroll
@@ -310,27 +321,36 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
         if (lane == 0) {
             constexpr uint32_t IDESC = make_idesc(/*s32*/ 2, /*s8*/ 1, /*s8*/ 1, TILE_N, T::MMA_N);
             bool ok = true, issued = false;
+            // Ring positions and operand addresses advance by additions only: forming
+            // each MMA's descriptors from the unit index (i % X_STAGES, ...) cost the
+            // issuing thread ~35 cycles per MMA, about as much as the MMA itself
+            // (M=128, N<=64: ~46 cycles).  The descriptor's address field is bits
+            // 0-13 (address >> 4), which the shared-memory offsets stay inside.
+            const uint64_t x_desc0 = make_sdesc_kmajor_sw128(smem_u32(xring));
+            uint64_t x_desc = x_desc0;
+            uint32_t a_tm = tmem_base, d_tm = tmem_base + D_COL0;
+            int s = 0, ab = 0, db = 0, r = 0;
+            uint32_t x_ph = 0, a_ph = 0, d_ph = 1;
             for (int i = 0; i < nu && ok; ++i) {
-                const int s = i % X_STAGES, ab = i % NA, db = i % ND;
-                if (!mbar_wait(&bars->x_full[s], (uint32_t)(i / X_STAGES) & 1u, abort_flag, p.status, SITE_MMA) ||
-                    !mbar_wait(&bars->a_full[ab], (uint32_t)(i / NA) & 1u, abort_flag, p.status, SITE_MMA) ||
-                    !mbar_wait(&bars->d_empty[db], ((uint32_t)(i / ND) & 1u) ^ 1u, abort_flag, p.status, SITE_MMA)) {
+                if (!mbar_wait(&bars->x_full[s], x_ph, abort_flag, p.status, SITE_MMA) ||
+                    !mbar_wait(&bars->a_full[ab], a_ph, abort_flag, p.status, SITE_MMA) ||
+                    !mbar_wait(&bars->d_empty[db], d_ph, abort_flag, p.status, SITE_MMA)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t xt = smem_u32(xring + s * T::XT_BYTES);
 #pragma unroll
                 for (int k = 0; k < GROUP / UMMA_K; ++k)
 #pragma unroll
                     for (int g = 0; g < UG; ++g)
-                        umma_i8_tmem_a(tmem_base + D_COL0 + db * T::D_COLS + g * T::MMA_N,
-                                       tmem_base + ab * A_COLS + g * (GROUP / 4) + k * (UMMA_K / 4),
-                                       make_sdesc_kmajor_sw128(xt + g * T::XT_GROUP + k * UMMA_K), IDESC, k > 0 ? 1u : 0u);
+                        umma_i8_tmem_a(d_tm + g * T::MMA_N, a_tm + g * (GROUP / 4) + k * (UMMA_K / 4),
+                                       x_desc + (uint64_t)((g * T::XT_GROUP + k * UMMA_K) >> 4), IDESC, k > 0 ? 1u : 0u);
                 issued = true;
-                umma_commit(&bars->d_full[db]);
-                umma_commit(&bars->a_empty[ab]);
-                umma_commit(&bars->x_empty[s]);
+                umma_commit(&bars->mma_done[r]);
+                if (++r == DONE_RING) r = 0;
+                if (++s == X_STAGES) { s = 0; x_desc = x_desc0; x_ph ^= 1u; } else { x_desc += T::XT_BYTES >> 4; }
+                if (++ab == NA) { ab = 0; a_tm = tmem_base; a_ph ^= 1u; } else { a_tm += A_COLS; }
+                if (++db == ND) { db = 0; d_tm = tmem_base + D_COL0; d_ph ^= 1u; } else { d_tm += T::D_COLS; }
             }
             if (!ok && issued) {
                 umma_commit(&bars->drain);
@@ -421,7 +441,8 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
         for (int i = 0; i < nu; ++i) {
             fetch_sz(i + SZ_AHEAD);
             const int db = i % ND;
-            if (!warp_wait(&bars->d_full[db], (uint32_t)(i / ND) & 1u, abort_flag, p.status, SITE_FOLD)) break;
+            if (!warp_wait(&bars->mma_done[i % DONE_RING], (uint32_t)(i / DONE_RING) & 1u, abort_flag, p.status, SITE_FOLD))
+                break;
             tc_fence_after();
             cp_async_wait<SZ_AHEAD>();
             __syncwarp();
@@ -444,6 +465,8 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int m = 4 * m4 + e;
+                        // (an I2F-free conversion through the 1.5 * 2^23 bit trick, exact for
+                        // these |D| < 2^21, measured slower: 49.5 against 46.7 us at M = 16)
                         const int sqx = 8 * (int)r[m] + ((int)r[T::MROWS + m] >> 4);   // sum_k q xi, exact
                         y[m] = fmaf(sc * xev[e], fmaf(-z, xsv[e], (float)sqx), y[m]);
                     }
@@ -465,9 +488,13 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
         const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
         for (int i = team; i < nu; i += TEAMS) {
             const int s = i % W_STAGES, ab = i % NA;
-            if (!warp_wait(&bars->w_full[s], (uint32_t)(i / W_STAGES) & 1u, abort_flag, p.status, SITE_DEQ) ||
-                !warp_wait(&bars->a_empty[ab], ((uint32_t)(i / NA) & 1u) ^ 1u, abort_flag, p.status, SITE_DEQ))
-                break;
+            if (!warp_wait(&bars->w_full[s], (uint32_t)(i / W_STAGES) & 1u, abort_flag, p.status, SITE_DEQ)) break;
+            if (i >= NA) {   // the MMA that read this A buffer (unit i - NA) is complete
+                const int j = i - NA;
+                if (!warp_wait(&bars->mma_done[j % DONE_RING], (uint32_t)(j / DONE_RING) & 1u, abort_flag, p.status,
+                               SITE_DEQ))
+                    break;
+            }
             tc_fence_after();
 #pragma unroll
             for (int g = 0; g < UG; ++g) {
