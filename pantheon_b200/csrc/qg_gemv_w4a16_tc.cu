@@ -210,6 +210,29 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return __all_sync(0xffffffffu, ok);
 }
 
+// Two fp32 lanes per instruction, each rounded exactly as its scalar form:
+// (d0, d1) = (a0, a1) * (b0, b1) + (c0, c1), and (d0, d1) = (a0, a1) * (b0, b1).
+__device__ __forceinline__ void fma_x2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                       float c1) {
+    asm("{\n\t.reg .b64 a, b, c;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %5};\n\t"
+        "mov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 c, a, b, c;\n\t"
+        "mov.b64 {%0, %1}, c;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void mul_x2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 a, b;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %5};\n\t"
+        "mul.rn.f32x2 a, a, b;\n\t"
+        "mov.b64 {%0, %1}, a;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // Byte offset of (row, 16-byte chunk) in a 32-row x 128-byte K-major tile with
 // the 128-byte swizzle (chunk index XOR row % 8 inside each 8-row atom).
 __device__ __forceinline__ int xt_offset(int row, int chunk) {
@@ -463,12 +486,18 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
                     const float4 xs = xs4[m4], xe = xe4[m4];
                     const float xsv[4] = {xs.x, xs.y, xs.z, xs.w}, xev[4] = {xe.x, xe.y, xe.z, xe.w};
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
+                    for (int e = 0; e < 4; e += 2) {   // rows m, m + 1 as fp32 pairs
                         const int m = 4 * m4 + e;
-                        // (an I2F-free conversion through the 1.5 * 2^23 bit trick, exact for
-                        // these |D| < 2^21, measured slower: 49.5 against 46.7 us at M = 16)
-                        const int sqx = 8 * (int)r[m] + ((int)r[T::MROWS + m] >> 4);   // sum_k q xi, exact
-                        y[m] = fmaf(sc * xev[e], fmaf(-z, xsv[e], (float)sqx), y[m]);
+                        // sum_k q xi, exact (an I2F-free conversion through the 1.5 * 2^23
+                        // bit trick, exact for these |D| < 2^21, measured slower)
+                        const float f0 = (float)(8 * (int)r[m] + ((int)r[T::MROWS + m] >> 4));
+                        const float f1 = (float)(8 * (int)r[m + 1] + ((int)r[T::MROWS + m + 1] >> 4));
+                        // y += (sc * 2^e) * (sum q xi - z * sum xi), rounded as the scalar
+                        // fmaf(sc * xe, fmaf(-z, xs, f), y)
+                        float t0, t1, p0, p1;
+                        fma_x2(t0, t1, -z, -z, xsv[e], xsv[e + 1], f0, f1);
+                        mul_x2(p0, p1, sc, sc, xev[e], xev[e + 1]);
+                        fma_x2(y[m], y[m + 1], p0, p1, t0, t1, y[m], y[m + 1]);
                     }
                 }
             }
