@@ -261,6 +261,17 @@ QG_API int  qg_gemv_w4a16(const void* X, const void* W, const void* S, const voi
                           int out_type, int M, int N, int K,
                           void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* qg_gemv_w4a16 with flags.  QG_GEMV_WEIGHTS_CONST: the kernel that precedes
+ * this call on `stream` does not write W, S or Z (a decode loop over fixed
+ * weights, e.g. the previous GEMV call); the 1-2-row kernel then issues its
+ * first weight loads before waiting for that kernel to finish, overlapping
+ * the previous call's tail.  Other bits are rejected with QG_ERR_ARG.
+ * No counterpart in the reference. */
+#define QG_GEMV_WEIGHTS_CONST 1u
+QG_API int  qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, const void* Z, void* Y,
+                             int out_type, int M, int N, int K, void* workspace, uint64_t workspace_bytes,
+                             unsigned int flags, void* stream);
+
 /* qg_gemv_w4a16 without a caller-provided workspace, for callers that cannot
  * allocate device memory where they call it (a process whose device-memory
  * budget is already claimed, or a latency-critical decode path where an

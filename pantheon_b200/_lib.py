@@ -21,6 +21,7 @@ QG_ERR_DEVICE_TIMEOUT = 1
 QG_FMT_INT8, QG_FMT_FP8, QG_FMT_NVFP4, QG_FMT_W4A16 = 0, 1, 2, 3
 QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3, QG_FMT_FP32 = 4, 5, 6, 7, 8
 QG_OUT_BF16, QG_OUT_F32, QG_OUT_S32, QG_OUT_F16 = 0, 1, 2, 3
+QG_GEMV_WEIGHTS_CONST = 1
 
 
 class QGError(RuntimeError):
@@ -76,6 +77,8 @@ _SIGNATURES = {
     "qg_gen_nvfp4": (C.c_int, [_V, _V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint32, _V]),
     "qg_gemv_w4a16_workspace_bytes": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_uint64)]),
     "qg_gemv_w4a16": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V, C.c_uint64, _V]),
+    "qg_gemv_w4a16_ex": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V, C.c_uint64, C.c_uint,
+                                   _V]),
     "qg_gemv_w4a16_noalloc": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gen_w4a16": (C.c_int, [_V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint32, _V]),
     "qg_device_status": (C.c_int, [C.c_int]),

@@ -178,7 +178,11 @@ int qg_run(qg_ctx* c, int iters, void* stream) {
     QG_CHECK_ARG(c && iters >= 0, "qg_run: bad argument");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     for (int i = 0; i < iters; ++i) {
-        int rc = qg::launch_copy(c->cfg, c->layout, c->copies[(size_t)c->next_copy], s);
+        // From the second launch on, the kernel before each GEMV on this stream is
+        // the previous GEMV of this loop, which does not write the weights: their
+        // first loads may start before the dependency wait.
+        int rc = qg::launch_copy(c->cfg, c->layout, c->copies[(size_t)c->next_copy], s,
+                                 i > 0 ? QG_GEMV_WEIGHTS_CONST : 0u);
         if (rc) return fail(c, rc);
         c->next_copy = (c->next_copy + 1) % (int)c->copies.size();
     }

@@ -166,7 +166,7 @@ int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_inde
     }
 }
 
-int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaStream_t s) {
+int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaStream_t s, unsigned int gemv_flags) {
     switch (cfg.format) {
         case QG_FMT_INT8:
             return gemm_i8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, cp.cksum, L.M, L.N, L.K, s);
@@ -177,7 +177,7 @@ int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaS
                               L.M, L.N, L.K, s);
         case QG_FMT_W4A16:
             return gemv_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, cp.scratch,
-                              L.scratch_bytes, s);
+                              L.scratch_bytes, s, gemv_flags);
         case QG_FMT_BF16:
         case QG_FMT_FP16:
         case QG_FMT_TF32:

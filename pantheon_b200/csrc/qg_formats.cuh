@@ -36,7 +36,8 @@ struct CopyBuffers {
 
 int layout_for(const qg_cfg& cfg, Layout* L);
 int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_index, uint64_t seed, cudaStream_t s);
-int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaStream_t s);
+// `gemv_flags` (QG_GEMV_WEIGHTS_CONST or 0) is passed to the W4A16 GEMV.
+int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaStream_t s, unsigned int gemv_flags = 0);
 
 // Kernel entry points (one per kernel file).
 int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type, void* row_cksum,
@@ -62,7 +63,7 @@ int gemm_nvfp4(const void* A, const void* SFA, const void* B, const void* SFB, f
 int gen_w4a16(void* X, void* W, void* S, void* Z, int M, int N, int K, uint64_t seed, uint32_t tid0, cudaStream_t s);
 uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int sm_count);
 int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,
-               void* workspace, uint64_t workspace_bytes, cudaStream_t stream);
+               void* workspace, uint64_t workspace_bytes, cudaStream_t stream, unsigned int flags);
 int verify_words(const void* actual, const void* expected, uint64_t nwords, void* counters, void* log, int log_cap,
                  cudaStream_t s);
 int flip_bit(void* word, cudaStream_t s);

@@ -69,6 +69,7 @@ struct Params {
     int M, N, K;
     int splits;
     int out_type;
+    int early_w;             // QG_GEMV_WEIGHTS_CONST: first weight loads before the dependency wait
 };
 
 __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
@@ -113,11 +114,6 @@ gemv_w4a16_kernel(Params p) {
                                                ~static_cast<uintptr_t>(15));
     int4* xi = reinterpret_cast<int4*>(xdat);
 
-    // Launched with programmatic stream serialization: this CTA may be resident
-    // before the previous kernel on the stream has finished, so nothing global
-    // is read or written until that grid is complete (a no-op otherwise).
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-
     // The first two batches of weights are requested before anything else, so
     // they stream in while the prologue below stages activations and scales.
     const int n0 = col0 + threadIdx.x * CPT;
@@ -130,7 +126,18 @@ gemv_w4a16_kernel(Params p) {
         for (int d = 0; d < DEPTH; ++d)
             if (base + d < len) dst[d] = ld_stream(wp + (size_t)(base + d) * row_stride);
     };
-    if (active) {
+    // Launched with programmatic stream serialization: this CTA may be resident
+    // before the previous kernel on the stream has finished, so nothing global
+    // is read or written until that grid is complete (a no-op otherwise) --
+    // except, when the caller declares the weights constant (the previous
+    // kernel does not write W), the first weight batches, which then overlap
+    // the previous call's tail.
+    if (p.early_w && active) {
+        load_batch(wa, 0);
+        if (DEPTH < len) load_batch(wb, DEPTH);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (!p.early_w && active) {
         load_batch(wa, 0);
         if (DEPTH < len) load_batch(wb, DEPTH);
     }
@@ -399,8 +406,9 @@ uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int /*sm_count*/) {
 }
 
 int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,
-               void* workspace, uint64_t workspace_bytes, cudaStream_t stream) {
+               void* workspace, uint64_t workspace_bytes, cudaStream_t stream, unsigned int flags) {
     QG_CHECK_ARG(X && W && S && Z && Y, "qg_gemv_w4a16: null operand");
+    QG_CHECK_ARG((flags & ~(unsigned int)QG_GEMV_WEIGHTS_CONST) == 0, "qg_gemv_w4a16: unknown flags 0x%x", flags);
     QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemv_w4a16: empty shape %dx%dx%d", M, N, K);
     QG_CHECK_ARG(K % w4::GROUP == 0, "qg_gemv_w4a16: K=%d must be a multiple of 128 (group size)", K);
     QG_CHECK_ARG(N % 4 == 0, "qg_gemv_w4a16: N=%d must be a multiple of 4", N);
@@ -443,6 +451,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         p.K = K;
         p.splits = splits;
         p.out_type = out_type;
+        p.early_w = (flags & QG_GEMV_WEIGHTS_CONST) ? 1 : 0;
         const size_t smem = w4::smem_bytes(mt, K, splits);
         QG_CHECK_ARG(smem <= 200 * 1024, "qg_gemv_w4a16: K slice too large for shared memory");
         dim3 grid(w4::col_blocks_for(mt, N), splits);
@@ -474,7 +483,14 @@ extern "C" int qg_gemv_w4a16_workspace_bytes(int M, int N, int K, uint64_t* byte
 extern "C" int qg_gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M,
                              int N, int K, void* workspace, uint64_t workspace_bytes, void* stream) {
     return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, workspace, workspace_bytes,
-                          static_cast<cudaStream_t>(stream));
+                          static_cast<cudaStream_t>(stream), 0u);
+}
+
+extern "C" int qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type,
+                                int M, int N, int K, void* workspace, uint64_t workspace_bytes, unsigned int flags,
+                                void* stream) {
+    return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, workspace, workspace_bytes,
+                          static_cast<cudaStream_t>(stream), flags);
 }
 
 // ---------------------------------------------------------------------------
@@ -542,5 +558,5 @@ extern "C" int qg_gemv_w4a16_noalloc(const void* X, const void* W, const void* S
     // The array keeps whatever the previous call (of any shape) left in it,
     // and the tickets must start at zero: clear this call's part first.
     QG_CUDA(cudaMemsetAsync(scratch, 0, (size_t)need, s));
-    return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, scratch, kNoAllocScratchBytes, s);
+    return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, scratch, kNoAllocScratchBytes, s, 0u);
 }

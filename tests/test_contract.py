@@ -97,6 +97,15 @@ def test_mma_virus_rejects_gemm_types_it_cannot_run(qglib, gemm_type, why):
     assert "Throughput:" not in proc.stdout
 
 
+def test_gemv_rejects_unknown_flags(qglib):
+    """qg_gemv_w4a16_ex checks its flags before touching the device."""
+    import pantheon_b200 as pb
+    fake = 1 << 20   # aligned, never dereferenced: the call returns before any device access
+    assert qglib.qg_gemv_w4a16_ex(fake, fake, fake, fake, fake, pb.QG_OUT_BF16, 1, 128, 128, fake, 1 << 20, 2,
+                                  None) == pb._lib.QG_ERR_ARG
+    assert "unknown flags" in pb._lib.last_error()
+
+
 def test_mma_virus_rejects_small_gemm_dims(qglib):
     """vendor_gemm.h:530-533: --gemm_m/n/k below 16 is an error."""
     from pantheon_b200 import MMA_BIN_PATH

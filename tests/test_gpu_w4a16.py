@@ -78,6 +78,20 @@ def test_full_size_config3(cuda_device, oracle, M):
         assert pb.device_status(0) == 0
 
 
+@pytest.mark.parametrize("M", [1, 2, 8])
+def test_weights_const_flag_is_bit_identical(cuda_device, oracle, M):
+    """QG_GEMV_WEIGHTS_CONST only moves the first weight loads before the dependency wait:
+    back-to-back calls over fixed weights give the same bits as the default path."""
+    N, K = 4096, 2048
+    host, dev = _operands(oracle, M, N, K, seed=11, dev=cuda_device)
+    ref = pb.gemv_w4a16(*dev, out_type=pb.QG_OUT_F32)
+    outs = [pb.gemv_w4a16(*dev, out_type=pb.QG_OUT_F32, weights_const=True) for _ in range(6)]
+    torch.cuda.synchronize()
+    for y in outs:
+        assert torch.equal(y.view(torch.int32), ref.view(torch.int32))
+    assert oracle.max_rel_err(_np(ref), oracle.gemv_w4a16(*host, out_type=1), 1) < 1e-4
+
+
 @pytest.mark.parametrize("M", [2, 8])
 def test_workspace_reusable_and_checked(cuda_device, oracle, M):
     N, K = 2048, 2048
