@@ -141,6 +141,11 @@ gemv_w4a16_kernel(Params p) {
         load_batch(wa, 0);
         if (DEPTH < len) load_batch(wb, DEPTH);
     }
+    // The next call on the stream may launch once every CTA of this one has
+    // passed this point (so all of them are resident: none can be starved of
+    // an SM by the next grid); its CTAs take SMs as these exit, and wait for
+    // this grid before touching anything it writes.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // Scales and zero points of this CTA's groups, staged once with 64-bit
     // loads (rows of S and Z are 8-byte aligned because N % 4 == 0): the group
@@ -286,11 +291,6 @@ gemv_w4a16_kernel(Params p) {
             run_batch(wb, base + DEPTH);
         }
     }
-
-    // every CTA of this call is resident by now: the next call on the stream may
-    // launch and take SMs as they free up (it waits for this grid before any
-    // global access)
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // ---- publish: directly when K is not split, else partial + ticket
     auto store_row = [&](int m, const float* v) {
