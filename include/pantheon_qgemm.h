@@ -288,6 +288,14 @@ QG_API int  qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, const 
 QG_API int  qg_gemv_w4a16_noalloc(const void* X, const void* W, const void* S, const void* Z, void* Y,
                                   int out_type, int M, int N, int K, void* stream);
 
+/* Whether this library's kernels can run on `device`: QG_OK on an sm_100
+ * (B200) device, QG_ERR_UNSUPPORTED on any other GPU (the message names its
+ * architecture), QG_ERR_CUDA when there is no usable device.  The binaries
+ * turn QG_ERR_UNSUPPORTED into the runner's deliberate skip ("Skipping:
+ * <reason>" on stdout, exit 0).
+ * Replaces: the platform checks before pantheon_skip (kernels/common/common.h:444-460). */
+QG_API int  qg_device_check(int device);
+
 /* Bounded-wait status of the most recent kernel on this device (QG_OK or
  * QG_ERR_DEVICE_TIMEOUT); clears the flag. Synchronous. */
 QG_API int  qg_device_status(int device);

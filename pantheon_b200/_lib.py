@@ -71,6 +71,7 @@ _SIGNATURES = {
     "qg_gemm_f32": (C.c_int, [_V, _V, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gen_dense": (C.c_int, [C.c_int, _V, C.c_uint64, C.c_uint64, C.c_uint32, _V]),
     "qg_pci_bus_id": (C.c_int, [C.c_int, C.c_char_p, C.c_int]),
+    "qg_device_check": (C.c_int, [C.c_int]),
     "qg_gen_fp8": (C.c_int, [_V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint32, _V]),
     "qg_gemm_nvfp4": (C.c_int, [_V, _V, _V, _V, C.c_float, C.c_float, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_nvfp4_sf_bytes": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_uint64)]),

@@ -312,6 +312,12 @@ int qg_mem_info(int device, uint64_t* free_bytes, uint64_t* total_bytes) {
     return QG_OK;
 }
 
+int qg_device_check(int device) {
+    QG_CUDA(cudaSetDevice(device));
+    qg::DeviceInfo* info = nullptr;
+    return qg::current_device_info(&info);
+}
+
 int qg_pci_bus_id(int device, char* buf, int len) {
     QG_CHECK_ARG(buf && len >= 16, "qg_pci_bus_id: buffer of at least 16 bytes required");
     QG_CUDA(cudaDeviceGetPCIBusId(buf, len, device));

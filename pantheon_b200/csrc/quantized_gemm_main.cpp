@@ -157,6 +157,14 @@ int fail(const std::string& why) {
     return 1;
 }
 
+// A deliberate skip (common.h:444-460): the device cannot run this workload,
+// which is not a failure of the device.
+int skip(int device, const std::string& reason) {
+    std::cout << "[PANTHEON] GPU " << device << ": Skipping " << kWorkload << " (" << reason << ")." << std::endl;
+    std::cout << "Skipping: " << reason << std::endl;
+    return 0;
+}
+
 int fail_ctx(qg_ctx* ctx, const char* what) {
     char buf[512];
     qg_last_error(ctx, buf, sizeof(buf));
@@ -341,6 +349,13 @@ int main(int argc, char* argv[]) {
         if (o.gemm_m < 16 || o.gemm_n < 16 || o.gemm_k < 16) return fail("--gemm_m/n/k must each be at least 16.");
     }
 
+    const int support = qg_device_check(o.device);
+    if (support == QG_ERR_UNSUPPORTED) {
+        char buf[512];
+        qg_last_error(nullptr, buf, sizeof(buf));
+        return skip(o.device, buf);
+    }
+    if (support != QG_OK) return fail_ctx(nullptr, "device query failed");
     uint64_t free_b = 0, total_b = 0;
     if (qg_mem_info(o.device, &free_b, &total_b) != QG_OK) return fail_ctx(nullptr, "device query failed");
 

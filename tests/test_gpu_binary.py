@@ -19,6 +19,11 @@ def _run(*args, timeout=600):
     return subprocess.run([str(BIN_PATH), *map(str, args)], capture_output=True, text=True, timeout=timeout)
 
 
+def test_device_check_accepts_the_b200(cuda_device, qglib):
+    """qg_device_check is QG_OK on the sm_100 device (elsewhere the binaries print Skipping: and exit 0)."""
+    assert qglib.qg_device_check(0) == 0
+
+
 def test_clean_verify_passes(cuda_device):
     p = _run(0, 2, 50, "--verify", "--m", 2048, "--n", 2048, "--k", 2048)
     assert p.returncode == 0, p.stdout + p.stderr
