@@ -14,7 +14,7 @@ The fixtures pin the CPU oracle against independent implementations:
     fp32 values, from torch / numpy casts (the oracle's converters are checked
     against these).
   * dense.json -- the tensor-furnace GEMM (mma_virus) of each operand format
-    (bf16, fp16, tf32, e4m3) on the dense generator's operands: C = A B^T from
+    (bf16, fp16, tf32, e4m3, fp32) on the dense generator's operands: C = A B^T from
     numpy's float64 matmul of the decoded operands, which is exact here (every
     operand is a multiple of 2^-15 of magnitude at most 1, so every product is a
     multiple of 2^-30 and a K <= 256 sum fits a double's 53 bits), rounded to
@@ -118,6 +118,7 @@ DENSE = {  # format id: (name, storage dtype, decoder, output type name)
     5: ("fp16", np.uint16, lambda b: b.view(np.float16).astype(np.float32), "f16"),
     6: ("tf32", np.uint32, lambda b: b.view(np.float32), "f32"),
     7: ("e4m3", np.uint8, lambda b: torch.from_numpy(b).view(torch.float8_e4m3fn).float().numpy(), "bf16"),
+    8: ("fp32", np.uint32, lambda b: b.view(np.float32), "f32"),
 }
 
 

@@ -92,7 +92,7 @@ def test_dense_oracle_matches_golden_known_answers(oracle):
     from pathlib import Path
     sha = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
     cases = json.loads((Path(__file__).parent / "golden" / "dense.json").read_text())["cases"]
-    assert {c["name"] for c in cases} == {"bf16", "fp16", "tf32", "e4m3"}
+    assert {c["name"] for c in cases} == {"bf16", "fp16", "tf32", "e4m3", "fp32"}
     for c in cases:
         kind = oracle.DENSE_FORMATS[c["format"]][0]
         A, B = oracle.dense_operands(c["format"], c["M"], c["N"], c["K"], c["seed"])
