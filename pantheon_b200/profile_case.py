@@ -1,6 +1,6 @@
 """Run a few launches of one workload kernel, for profilers (ncu) and quick timing.
 
-    python -m pantheon_b200.profile_case --format int8|fp8|nvfp4|w4a16|bf16|fp16|tf32|e4m3
+    python -m pantheon_b200.profile_case --format int8|fp8|nvfp4|w4a16|bf16|fp16|tf32|e4m3|fp32
                                          [--m M --n N --k K] [--iters 3] [--copies 1]
 
 Fills the operands, computes the golden result (one launch), then runs
@@ -17,9 +17,10 @@ import torch
 import pantheon_b200 as pb
 
 FORMATS = {"int8": pb.QG_FMT_INT8, "fp8": pb.QG_FMT_FP8, "nvfp4": pb.QG_FMT_NVFP4, "w4a16": pb.QG_FMT_W4A16,
-           "bf16": pb.QG_FMT_BF16, "fp16": pb.QG_FMT_FP16, "tf32": pb.QG_FMT_TF32, "e4m3": pb.QG_FMT_E4M3}
-# output type of each format (the dense furnace formats write their own type, tf32 fp32, e4m3 bf16)
-OUT_TYPES = {"fp16": pb.QG_OUT_F16, "tf32": pb.QG_OUT_F32}
+           "bf16": pb.QG_FMT_BF16, "fp16": pb.QG_FMT_FP16, "tf32": pb.QG_FMT_TF32, "e4m3": pb.QG_FMT_E4M3,
+           "fp32": pb.QG_FMT_FP32}
+# output type of each format (the dense furnace formats write their own type, tf32 / fp32 fp32, e4m3 bf16)
+OUT_TYPES = {"fp16": pb.QG_OUT_F16, "tf32": pb.QG_OUT_F32, "fp32": pb.QG_OUT_F32}
 
 
 def main(argv=None) -> int:
