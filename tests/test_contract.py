@@ -97,6 +97,17 @@ def test_mma_virus_rejects_gemm_types_it_cannot_run(qglib, gemm_type, why):
     assert "Throughput:" not in proc.stdout
 
 
+def test_device_check_without_a_gpu(qglib):
+    """qg_device_check reports a missing device as a CUDA error (the binaries then FAIL with the
+    reason on stderr); only a GPU that is present but not sm_100 gives QG_ERR_UNSUPPORTED (SKIP)."""
+    import torch
+    import pantheon_b200 as pb
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert qglib.qg_device_check(0) == pb._lib.QG_ERR_CUDA
+    assert pb._lib.last_error()
+
+
 def test_gemv_rejects_unknown_flags(qglib):
     """qg_gemv_w4a16_ex checks its flags before touching the device."""
     import pantheon_b200 as pb
