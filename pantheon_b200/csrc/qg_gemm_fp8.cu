@@ -196,10 +196,11 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     sa_next = row_ok ? __ldg(sa_row + kb + 1) : 0.0f;
                     sb_next = nb_ok ? __ldg(sb_row + kb + 1) : 0.0f;
                 }
-                int w_ok = 1;
-                if (lane == 0) w_ok = mbar_wait(&bars->part_full[buf], pph, abort_flag, p.status, SITE_EPI) ? 1 : 0;
-                w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-                if (!w_ok) { ok = false; break; }
+                // every lane waits (no divergent branch around the wait)
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->part_full[buf], pph, abort_flag, p.status, SITE_EPI))) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t t_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * PART_COLS + half * COLS_PER_EPI;
                 // two 16-column loads in flight: the next chunk loads while this one is promoted
