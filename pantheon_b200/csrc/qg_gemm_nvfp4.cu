@@ -231,9 +231,12 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             for (int kb = 0; kb < nk; ++kb) {
-                int got = 1;
-                if (lane == 0) got = mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_SF) ? 1 : 0;
-                if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
+                // every lane waits: a lane-0 poll with a shuffle after it cost the FP8
+                // GEMM's per-K-block waits ~15 %
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_SF))) {
+                    ok = false;
+                    break;
+                }
                 // lane i takes bytes [16 i, 16 i + 16) of each atom: TMEM columns
                 // 4k..4k+3 (A) and 16 + 8k + 4h .. +3 (B) of this stage's region
                 const uint4* sfa = reinterpret_cast<const uint4*>(sSFA + stage * SFA_BYTES) + lane;
