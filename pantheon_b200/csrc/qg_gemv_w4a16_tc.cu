@@ -112,6 +112,11 @@ constexpr int DONE_RING = 16;
 static_assert(DONE_RING > X_STAGES && DONE_RING > NA && DONE_RING > ND, "mma_done ring depth");
 constexpr int TMEM_COLS = 512;
 static_assert(NA % TEAMS == 0, "each team cycles through its own A buffers");
+// Likewise each W stage must belong to one team: with an odd stage count the
+// other team would wait on a stage's w_full for a unit two loads ahead, and a
+// parity wait that far ahead passes at once (a timing copy with 3 stages read
+// W before it landed and failed to launch cleanly).
+static_assert(W_STAGES % TEAMS == 0, "each team cycles through its own W stages");
 constexpr int SZ_AHEAD = 4;                   // units between an S/Z fetch and its fold
 constexpr int SZ_RING = 8;                    // >= SZ_AHEAD + 1
 static_assert(SZ_RING >= SZ_AHEAD + 1, "ring depth");
