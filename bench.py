@@ -25,15 +25,24 @@ Printed by rank 0, one JSON line:
             (the default run), the burst one for a short region; both
             fractions are reported;
   cpu_baseline  the CPU oracle's INT8 GEMM (OpenMP, all host threads) on a
-            bounded sample of rows of the same GEMM, rank 0 at N=1 only.
+            bounded sample of rows of the same GEMM, rank 0 at N=1 only;
+  secondary the other configurations, measured after the headline in the same
+            process (the headline's timed region is untouched): the INT8 GEMM
+            looped for ~1 s at the power cap (sustained), configs[2] FP8,
+            configs[3] W4A16 at M=1, 8 and 16 (4 rotating weight sets) and
+            configs[4] NVFP4 16384^3, each with its device-timed value,
+            roofline, clocks and mismatch count; at N > 1 each also lists every
+            rank's rate and mismatch count ("per_rank").
 Multi-GPU: one process per GPU (torchrun), each an independent instance with
-no data-path collective ("scaling": "weak"); NCCL carries only the barrier and
-the max of the timings.
+no data-path collective ("scaling": "weak"); NCCL carries only the barrier,
+the max of the timings and the per-rank figures.
 
 --impl reference times the reference side on the host cores: the reference
 has no INT8 GEMM (its quantized_gemm is a synthetic hash loop), so the arm is
-the oracle's CPU port of the GEMM, plus, for context, the reference's own MOCK
-binary of the path when it was built into oracle/_ref.
+the oracle's CPU port of the GEMM on the same configuration (the whole GEMM
+per step when the run fits in about two minutes, else a stated sample of its
+rows), plus, for context, the reference's own MOCK binary of the path when it
+was built into oracle/_ref.
 """
 from __future__ import annotations
 
@@ -75,10 +84,11 @@ def _traffic(key: str):
     return None
 
 
-def workload_spec(args, pb):
+def workload_spec(name: str, m: int = 0):
     """What one step runs.  Default: configs[1] (INT8 8192^3), the metric's headline workload."""
-    if args.workload == "w4a16":
-        m = args.m or 1
+    from pantheon_b200 import _lib as pb   # format constants only
+    if name == "w4a16":
+        m = m or 1
         return {"name": "w4a16", "fmt": pb.QG_FMT_W4A16, "shape": (m, 28672, 8192), "copies": 4, "seed": 3,
                 "unit": "GB/s", "bound": "hbm", "dtype": "bf16 x int4 (fp32 acc)",
                 # per 16-row chunk: one CUDA-core launch (1-2 rows), or the X pre-pass + the tensor-core GEMV
@@ -87,21 +97,21 @@ def workload_spec(args, pb):
                 "config": {"workload": f"configs[3] W4A16 group-128 GEMV M={m} K=8192 N=28672, bf16 out",
                            "M": m, "N": 28672, "K": 8192, "seed": 3, "operand_sets": 4,
                            "l2": "inputs larger than L2: 4 rotating weight sets of 125 MB each"}}
-    if args.workload == "fp8":
+    if name == "fp8":
         return {"name": "fp8", "fmt": pb.QG_FMT_FP8, "shape": (8192, 8192, 16384), "copies": 1, "seed": 2,
                 "unit": "TOPS", "bound": "tensor", "dtype": "e4m3 (fp32 acc, fp32 block scales)", "launches_per_step": 1,
                 "traffic_key": "gemm_fp8_8192_16384",
                 "config": {"workload": "configs[2] FP8 e4m3 GEMM M=N=8192 K=16384, 1x128 / 128x128 fp32 scales, bf16 out",
                            "M": 8192, "N": 8192, "K": 16384, "seed": 2, "operand_sets": 1,
                            "l2": "inputs larger than L2: A + B = 256 MiB"}}
-    if args.workload == "nvfp4":
+    if name == "nvfp4":
         return {"name": "nvfp4", "fmt": pb.QG_FMT_NVFP4, "shape": (16384, 16384, 16384), "copies": 1, "seed": 4,
                 "unit": "TOPS", "bound": "tensor", "dtype": "e2m1 x ue4m3/16 (fp32 acc)", "launches_per_step": 1,
                 "traffic_key": "gemm_nvfp4_16384", "peak_mult": 4.0,
                 "config": {"workload": "configs[4] NVFP4 GEMM M=N=K=16384, ue4m3 scale per 16 + fp32 per-tensor, bf16 out",
                            "M": 16384, "N": 16384, "K": 16384, "seed": 4, "operand_sets": 1,
                            "l2": "inputs larger than L2: A + B = 256 MiB"}}
-    if args.workload == "bf16":
+    if name == "bf16":
         return {"name": "bf16", "fmt": pb.QG_FMT_BF16, "shape": (8192, 8192, 8192), "copies": 2, "seed": 5,
                 "unit": "TFLOPS", "bound": "tensor", "dtype": "bf16 (fp32 acc)", "launches_per_step": 1,
                 "traffic_key": "gemm_bf16_8192", "peak_mult": 1.0,
@@ -217,6 +227,11 @@ def reference_mock_rate():
 
 
 def run_reference(args, rank: int):
+    """The reference arm: the path's CPU implementation on the host cores, on the same
+    configuration, metric and unit as our arm.  The reference has no INT8 GEMM, so this is
+    the oracle's port of it (OpenMP over all host threads).  Each step computes the whole
+    8192^3 GEMM when the run fits in about two minutes of CPU time, else the leading rows
+    that do (the sample is stated)."""
     if rank != 0:
         return 0
     steps = max(1, args.steps)
@@ -225,9 +240,8 @@ def run_reference(args, rank: int):
     from oracle import qg_oracle as O
     O.set_threads(O.host_threads())   # torchrun sets OMP_NUM_THREADS=1; the arm uses every host thread
     A, B, sa, sb = O.int8_operands(M, N, K, seed=1)
-    # bounded sample per step: the leading rows that keep the whole run near a minute
     per_row = _oracle_row_rate(O, A, B, sa, sb)
-    nrows = int(max(1, min(M, 60.0 / (steps + warm) / max(per_row, 1e-9))))
+    nrows = int(max(1, min(M, 120.0 / (steps + warm) / max(per_row, 1e-9))))
     rows = np.arange(nrows, dtype=np.int32)
     for _ in range(warm):
         O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
@@ -236,14 +250,16 @@ def run_reference(args, rank: int):
         O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
     dt = time.perf_counter() - t0
     tops = 2.0 * len(rows) * N * K * steps / dt / 1e12
+    wl = workload_spec("int8")
+    sample = (f"the whole {M}x{N}x{K} GEMM per step" if nrows == M else
+              f"{nrows} of {M} output rows of the {M}x{N}x{K} GEMM per step") + f", {steps} steps"
     line = {
         "impl": "reference", "metric": METRIC, "value": tops, "unit": "TOPS", "n_gpus": args.gpus,
         "steps": steps, "warmup": warm, "ms_per_step": dt / steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "configs[1] INT8 W8A8 GEMM 8192x8192x8192, bf16 out, fp32 row/col scales",
-                   "M": M, "N": N, "K": K, "seed": 1, "cpu_rows_per_step": nrows},
-        "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": O.threads(), "kind": "port",
-                         "sample": f"{len(rows)} of 8192 output rows per step, {steps} steps"},
+        "config": dict(wl["config"], parallelism=f"replicas x{args.gpus} (independent instance per GPU)"),
+        "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": O.threads(), "kind": "port", "sample": sample,
+                         "rows_per_step": nrows},
         "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "reference_mock": reference_mock_rate(),
         "gpu_launches": 0,
@@ -331,6 +347,110 @@ def e2e_loop(w, host_ops, out_bytes: int, copies: int, steps: int, dev, barrier)
                                  f"{nbuf} device operand sets and three streams")
 
 
+def roofline(wl, work: float, per_launch_s: float, timed_s: float, peaks: dict, traffic=None) -> dict:
+    """Achieved rate of one launch against the measured peak of its bound.
+
+    Tensor-bound: `work` = tera-ops per launch; the peak is mult x the measured bf16
+    dense figure (INT8 / FP8 2x, FP4 4x, BF16 1x: the datasheet ratios), the sustained
+    figure when the timed region is a loop of 0.2 s or more (it then runs at the
+    power cap), the burst one otherwise; both fractions and the datasheet one are
+    reported.  HBM-bound: `work` = GB per launch against the measured copy bandwidth."""
+    achieved = work / per_launch_s
+    if wl["bound"] == "tensor":
+        mult = wl.get("peak_mult", 2.0)
+        sustained = timed_s >= 0.2
+        base = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+        peak = mult * base
+        src = (f"{mult:g} x {peaks['source']} bf16 dense {'sustained' if sustained else 'burst'} "
+               f"({base} TFLOP/s; timed region {timed_s:.2f} s)")
+        datasheet = mult / 2.0 * DATASHEET_INT8_TOPS
+        extra = {f"frac_of_datasheet_{datasheet:g}": achieved / datasheet,
+                 "frac_of_measured_burst": achieved / (mult * peaks["bf16_tflops"]),
+                 "frac_of_measured_sustained": achieved / (mult * peaks["bf16_tflops_sustained"])}
+    else:
+        peak = peaks["hbm_gbs"]
+        src = f"{peaks['source']} HBM copy bandwidth"
+        extra = {"frac_of_datasheet_8000": achieved / 8000.0}
+    roof = {"bound": wl["bound"], "achieved": achieved, "peak": peak, "unit": wl["unit"], "frac": achieved / peak,
+            "traffic": traffic if traffic is not None else _traffic(wl["traffic_key"]), "peak_source": src}
+    roof.update(extra)
+    return roof
+
+
+def gather_over_ranks(values, world: int, device=None):
+    """Every rank's `values` (a list of floats), as a list of per-rank lists; the same
+    collective on every rank, none for a single process."""
+    import torch
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if world == 1:
+        return [t.tolist()]
+    import torch.distributed as dist
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+
+# Measured after the headline, in the same process, each on its own context:
+# the other configurations of BASELINE.json, and the headline GEMM looped long
+# enough to run at the power cap (its "looped for 60 s" figure, sustained).
+SECONDARY = (("int8_sustained", "int8", 0, 1.0), ("fp8", "fp8", 0, 0.5), ("w4a16_m1", "w4a16", 1, 0.1),
+             ("w4a16_m8", "w4a16", 8, 0.1), ("w4a16_m16", "w4a16", 16, 0.1), ("nvfp4", "nvfp4", 0, 0.5))
+
+
+def run_secondary(args, world: int, rank: int, local_rank: int, dev, barrier, uuid, peaks):
+    """Device-timed value, roofline, clocks and per-rank mismatch counts of each SECONDARY
+    configuration.  At N > 1 every rank runs its own instance; the entry's value is the
+    whole-job rate (units of all ranks / the slowest rank's time) and `per_rank` lists each
+    rank's rate and mismatch count (configs[4] reports exactly this to the verdict)."""
+    import torch
+    import pantheon_b200 as pb
+    out = {}
+    for key, name, m, region_s in SECONDARY:
+        wl = workload_spec(name, m)
+        w = pb.Workload(wl["fmt"], *wl["shape"], copies=wl["copies"], seed=wl["seed"], device=local_rank)
+        try:
+            w.fill(wl["seed"])
+            w.golden()
+            stream = torch.cuda.current_stream(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            w.run(3, stream)
+            e0.record(stream)
+            w.run(3, stream)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            per = max(e0.elapsed_time(e1) / 3.0 / 1e3, 1e-7)
+            n = int(min(20000, max(args.steps, -(-region_s // per))))
+            n = int(max_over_ranks([n], world, dev)[0])          # the same launch count on every rank
+            with ClockSampler(uuid) as clk:
+                barrier()
+                torch.cuda.synchronize(dev)
+                e0.record(stream)
+                w.run(n, stream)
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+                barrier()
+            ms = e0.elapsed_time(e1)
+            mism = w.verify()
+            status = pb.device_status(local_rank)
+            work = (w.ops_per_launch / 1e12) if wl["bound"] == "tensor" else (w.bytes_per_launch / 1e9)
+            ranks = gather_over_ranks([work * n / (ms / 1e3), float(mism), float(status != 0), ms], world, dev)
+            if rank == 0:
+                ms_max = max(r[3] for r in ranks)
+                entry = {"config": wl["config"], "value": work * n * world / (ms_max / 1e3), "unit": wl["unit"],
+                         "launches": n, "ms_per_launch": ms / n, "dtype": wl["dtype"],
+                         "roofline": roofline(wl, work, ms / 1e3 / n, ms / 1e3, peaks),
+                         "clocks": clk.summary(),
+                         "mismatches": int(sum(r[1] for r in ranks)),
+                         "device_timeouts": int(sum(r[2] for r in ranks))}
+                if world > 1:
+                    entry["per_rank"] = [{"rank": i, "value": r[0], "unit": wl["unit"], "mismatches": int(r[1])}
+                                         for i, r in enumerate(ranks)]
+                out[key] = entry
+        finally:
+            w.close()
+    return out
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -348,7 +468,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     steps = max(1, args.steps)
     warm = max(3, args.warmup)
-    wl = workload_spec(args, pb)
+    wl = workload_spec(args.workload, args.m)
     w = pb.Workload(wl["fmt"], *wl["shape"], copies=wl["copies"], seed=wl["seed"], device=local_rank)
     w.fill(wl["seed"])
     w.golden()
@@ -390,45 +510,27 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # download not overlapped) stay a few percent of the timed region
     e2e_steps = max(3, min(steps, 40))
     e2e_ms, e2e_path = e2e_loop(w, host_ops, out_bytes, wl["copies"], e2e_steps, dev, barrier)
+    w.close()
+    del host_ops
 
     ms_max, e2e_max, mm_max, bad = max_over_ranks([ms, e2e_ms, float(mismatches), float(status != 0)], world, dev)
+    peaks = _peaks()
+    secondary = None
+    if not args.no_secondary and args.workload == "int8":
+        secondary = run_secondary(args, world, rank, local_rank, dev, barrier, uuid, peaks)
 
     result = None
     if rank == 0:
-        peaks = _peaks()
         per_launch_s = ms / 1e3 / steps
-        if wl["bound"] == "tensor":
-            work = ops / 1e12
-            mult = wl.get("peak_mult", 2.0)   # dense INT8/FP8 = 2x bf16, FP4 = 4x bf16, BF16 = 1x on this part
-            # the timed region is a back-to-back loop of ~1 s under the 1 kW cap:
-            # the sustained figure is the denominator, the burst one is reported beside it
-            timed_s = ms / 1e3
-            sustained = timed_s >= 0.2
-            base = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
-            peak = mult * base
-            peak_src = (f"{mult:g} x {peaks['source']} bf16 dense {'sustained' if sustained else 'burst'} "
-                        f"({base} TFLOP/s; timed region {timed_s:.2f} s)")
-            datasheet = mult / 2.0 * DATASHEET_INT8_TOPS
-            extra = {f"frac_of_datasheet_{datasheet:g}": work / per_launch_s / datasheet,
-                     "frac_of_measured_burst": work / per_launch_s / (mult * peaks["bf16_tflops"]),
-                     "frac_of_measured_sustained": work / per_launch_s / (mult * peaks["bf16_tflops_sustained"])}
-        else:
-            work = nbytes / 1e9
-            peak = peaks["hbm_gbs"]
-            peak_src = f"{peaks['source']} HBM copy bandwidth"
-            extra = {"frac_of_datasheet_8000": work / per_launch_s / 8000.0}
-        achieved = work / per_launch_s
+        work = ops / 1e12 if wl["bound"] == "tensor" else nbytes / 1e9
         value = work * steps * world / (ms_max / 1e3)
         e2e_value = work * e2e_steps * world / (e2e_max / 1e3)
-        roof = {"bound": wl["bound"], "achieved": achieved, "peak": peak, "unit": wl["unit"],
-                "frac": achieved / peak, "traffic": _traffic(wl["traffic_key"]), "peak_source": peak_src}
-        roof.update(extra)
         result = {
             "metric": METRIC, "value": value, "unit": wl["unit"], "n_gpus": world, "steps": steps, "warmup": warm,
             "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": wl["dtype"], "data": "synthetic",
             "config": dict(wl["config"], parallelism=f"replicas x{world} (independent instance per GPU)"),
-            "roofline": roof,
+            "roofline": roofline(wl, work, per_launch_s, ms / 1e3, peaks),
             "e2e": {"value": e2e_value, "unit": wl["unit"], "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_bytes,
                     "path": e2e_path, "steps": e2e_steps},
             "clocks": clocks,
@@ -436,9 +538,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "mismatches": int(mm_max),
             "device_timeouts": int(bad),
         }
+        if secondary is not None:
+            result["secondary"] = secondary
         if world == 1 and not args.no_cpu_baseline and wl["name"] == "int8":
             result["cpu_baseline"] = cpu_baseline()
-    w.close()
     if world > 1:
         dist.destroy_process_group()
     if result is not None:
@@ -453,6 +556,8 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the configs measured after the headline (FP8, W4A16 M=1/8/16, NVFP4, INT8 sustained)")
     ap.add_argument("--workload", choices=["int8", "fp8", "nvfp4", "w4a16", "bf16"], default="int8",
                     help="int8 = configs[1] (default, the headline); w4a16 = configs[3] GEMV; "
                          "bf16 = the mma_virus furnace GEMM")
