@@ -87,11 +87,17 @@ constexpr int kDefaultWarmup = 3;
 
 // Launch-knob clamps with the reference's bounds (common.h:248-311).
 constexpr int kMaxKernelLoops = 1000000;
+// Longest one timed batch (launches between two synchronisations and two
+// verifications) may run, whatever --kernel_loops asks: a batch is the unit of
+// verification and of the runner's progress, so it must stay well inside both
+// the run's duration and the runner's duration*2+300 s kill (pantheon.py:4018).
+constexpr double kMaxBatchSeconds = 1.0;
 
 struct Options {
     int device = 0, duration = 1, mem_pct = 99;
     bool verify = false, inject = false;
-    int kernel_loops = 0;        // launches per timed batch; 0 = size a batch to ~200 ms
+    int kernel_loops = 0;        // launches per timed batch; 0 (flag absent) = size a batch to ~200 ms
+    bool loops_given = false;
     int warmup_iters = kDefaultWarmup;
     int format = kDefaultFormat;
     bool format_given = false;
@@ -296,7 +302,7 @@ int main(int argc, char* argv[]) {
         auto next = [&](void) -> const char* { return (i + 1 < argc) ? argv[++i] : nullptr; };
         if (a == "--verify") o.verify = true;
         else if (a == "--inject_error") o.inject = true;
-        else if (a == "--kernel_loops") { if (const char* v = next()) o.kernel_loops = atoi(v); }
+        else if (a == "--kernel_loops") { if (const char* v = next()) { o.kernel_loops = atoi(v); o.loops_given = true; } }
         else if (a == "--warmup_iters") { if (const char* v = next()) o.warmup_iters = atoi(v); }
         else if (a == "--block_size" || a == "--grid_size" || a == "--sync_mode" || a == "--mma_acc" ||
                  a == "--mma_groups" || a == "--mma_reuse" || a == "--init_pattern" || a == "--gemm") { next(); }
@@ -323,11 +329,14 @@ int main(int argc, char* argv[]) {
     }
     if (kFurnace) {
         o.kernel_loops = 0;   // a WMMA knob there; the GEMM batch is sized to ~200 ms
-    } else if (o.kernel_loops < 0) {
-        std::cerr << "[PANTHEON] Warning: invalid kernel_loops " << o.kernel_loops << "; using auto." << std::endl;
-        o.kernel_loops = 0;
+        o.loops_given = false;
+    } else if (o.loops_given && o.kernel_loops < 1) {
+        std::cerr << "[PANTHEON] Warning: invalid kernel_loops " << o.kernel_loops << "; using 1." << std::endl;
+        o.kernel_loops = 1;
     } else if (o.kernel_loops > kMaxKernelLoops) {
-        std::cerr << "[PANTHEON] Warning: kernel_loops " << o.kernel_loops << " clamped to " << kMaxKernelLoops << "." << std::endl;
+        std::cerr << "[PANTHEON] Warning: kernel_loops " << o.kernel_loops
+                  << " would make a single batch effectively unbounded; clamping to " << kMaxKernelLoops << "."
+                  << std::endl;
         o.kernel_loops = kMaxKernelLoops;
     }
     if (o.warmup_iters < 0) {
@@ -432,23 +441,31 @@ int main(int argc, char* argv[]) {
         if (qg_golden(ctx) != QG_OK || qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "qg_golden");
     }
 
-    // Warm-up, then a timing probe to size the batch (~200 ms per sync, as the
-    // reference's vendor GEMM batches: vendor_gemm.h:560-571).  The probe runs
-    // after one untimed launch, so first-use costs do not shrink the batch.
+    // Warm-up, then a timing probe: without --kernel_loops it sizes the batch
+    // (~200 ms per sync, as the reference's vendor GEMM batches:
+    // vendor_gemm.h:560-571); with it, it caps the batch at kMaxBatchSeconds.
+    // The probe runs after one untimed launch, so first-use costs do not
+    // shrink the batch.
     int loops = o.kernel_loops;
     {
         Phase ph("qg:warmup");
         if (o.warmup_iters > 0 && (qg_run(ctx, o.warmup_iters, nullptr) != QG_OK || qg_synchronize(ctx) != QG_OK))
             return fail_ctx(ctx, "warm-up");
+        if (qg_run(ctx, 1, nullptr) != QG_OK || qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "warm-up");
+        const int probe = 4;
+        auto t0 = std::chrono::high_resolution_clock::now();
+        if (qg_run(ctx, probe, nullptr) != QG_OK || qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "warm-up");
+        const double per = std::chrono::duration<double>(std::chrono::high_resolution_clock::now() - t0).count() / probe;
         if (loops == 0) {
-            if (qg_run(ctx, 1, nullptr) != QG_OK || qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "warm-up");
-            const int probe = 4;
-            auto t0 = std::chrono::high_resolution_clock::now();
-            if (qg_run(ctx, probe, nullptr) != QG_OK || qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "warm-up");
-            const double per =
-                std::chrono::duration<double>(std::chrono::high_resolution_clock::now() - t0).count() / probe;
             const double l = per > 0 ? 0.2 / per : 1.0;
             loops = (int)(l < 1 ? 1 : (l > 100000 ? 100000 : l));
+        } else if (per > 0 && loops * per > kMaxBatchSeconds) {
+            const double l = kMaxBatchSeconds / per;
+            const int capped = (int)(l < 1 ? 1 : l);
+            std::cerr << "[PANTHEON] Warning: kernel_loops " << loops << " would make one batch last "
+                      << loops * per << " s; capping to " << capped << " (about " << kMaxBatchSeconds
+                      << " s per batch)." << std::endl;
+            loops = capped;
         }
     }
     std::cout << "  -> Kernel Loops:  " << loops << std::endl;

@@ -68,3 +68,38 @@ def test_other_formats_verify(cuda_device, fmt, shape):
     assert status == "PASS" and t > 0 and unit == ("GB/s" if fmt == "w4a16" else "TOPS")
     pi = _run(0, 1, 50, "--verify", "--inject_error", "--format", fmt, "--m", m, "--n", n, "--k", k)
     assert pi.returncode != 0 and "[SDC FAULT]" in pi.stdout
+
+
+def _loops(stdout: str) -> int:
+    return int(next(line for line in stdout.splitlines() if "-> Kernel Loops:" in line).split(":")[1])
+
+
+@pytest.mark.parametrize("value", [-1, 0])
+def test_invalid_kernel_loops_use_one(cuda_device, value):
+    """normalize_kernel_launch_config (common.h:285-288): kernel_loops < 1 warns and uses 1."""
+    p = _run(0, 1, 50, "--verify", "--m", 512, "--n", 512, "--k", 512, "--kernel_loops", value)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert f"invalid kernel_loops {value}; using 1." in p.stderr
+    assert _loops(p.stdout) == 1
+    assert "Verification: PASS" in p.stdout
+
+
+def test_huge_kernel_loops_clamped_and_batch_bounded(cuda_device):
+    """Above 1e6 the reference clamps to 1e6 (common.h:289-297); a batch is further capped at
+    about one second of measured launch time, so a batch (the unit of verification) always
+    ends well inside the run's duration and the runner's kill timeout."""
+    p = _run(0, 1, 50, "--verify", "--m", 2048, "--n", 2048, "--k", 2048, "--kernel_loops", 2000000000)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "clamping to 1000000." in p.stderr
+    assert "per batch)." in p.stderr
+    loops = _loops(p.stdout)
+    assert 1 <= loops < 1000000
+    assert "Verification: PASS" in p.stdout
+
+
+def test_invalid_warmup_iters_use_zero(cuda_device):
+    """common.h:300-304: warmup_iters < 0 warns and uses 0."""
+    p = _run(0, 1, 50, "--verify", "--m", 512, "--n", 512, "--k", 512, "--warmup_iters", -1)
+    assert p.returncode == 0, p.stdout + p.stderr
+    assert "invalid warmup_iters -1; using 0." in p.stderr
+    assert "Verification: PASS" in p.stdout
