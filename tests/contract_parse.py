@@ -8,8 +8,12 @@ Follows parse_kernel_output (pantheon.py:3421-3513) and find_skip_reason
   * "[SDC FAULT]" anywhere is a FAIL;
   * "Verification: FAIL..." is a FAIL even with exit code 0;
   * "Skipping..." with no error is a SKIP; a zero throughput without a skip is a FAIL;
-  * "[PANTHEON]" lines and lines starting with "->" are kept for the log.
-Written for the tests only; the runner itself is not part of this repository.
+  * "[PANTHEON]" lines and lines starting with "->" are kept for the log, with
+    the runner's own notes (non-finite score, zero score, skip reason) and,
+    after a non-zero exit, stderr.
+Written for the tests only: the GPU tests read live binary output with it where
+the runner module is not available.  tests/test_reference_runner.py pins it to
+the runner's own decisions on recorded B200 runs (tests/golden/runner_readings.json).
 """
 from __future__ import annotations
 
@@ -42,6 +46,9 @@ def parse_kernel_output(out: str, err: str, returncode: int, test_name: str | No
             except (ValueError, IndexError):
                 continue
             if not math.isfinite(value):
+                if not had_error:
+                    lines_kept.append(f"[PANTHEON] Workload reported a non-finite throughput ({parts[0]}); "
+                                      "recorded as a failure.")
                 throughput, unit, status, had_error = 0.0, "ERR", "FAIL", True
                 continue
             if not had_error:
@@ -60,6 +67,12 @@ def parse_kernel_output(out: str, err: str, returncode: int, test_name: str | No
             lines_kept.append(line.strip())
     if skipped and not had_error:
         throughput, unit, status = 0.0, "SKIP", "SKIP"
+        if skipped not in lines_kept:
+            lines_kept.append(skipped)
     elif not had_error and throughput_line and throughput == 0.0 and test_name not in (None, "baseline_metrics"):
         unit, status, had_error = "ERR", "FAIL", True
+        lines_kept.append("[PANTHEON] Workload reported zero throughput without saying it skipped; "
+                          "recorded as a failure.")
+    if err and returncode != 0:
+        lines_kept.append(err.strip())
     return throughput, unit, status, had_error, lines_kept
