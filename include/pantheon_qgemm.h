@@ -111,15 +111,39 @@ QG_API int  qg_fill(qg_ctx* ctx, uint64_t seed);
 QG_API int  qg_golden(qg_ctx* ctx);
 
 /* Launch `iters` GEMMs (or GEMVs), rotating over the operand copies, on `stream`.
+ * After qg_golden every launch also checks itself (all formats but fp32): a GEMM
+ * folds the output words of each row segment it stores (256 columns for INT8
+ * and the dense tensor formats, 128 for FP8 and NVFP4; INT8 also folds its
+ * INT32 accumulators) into a fingerprint and compares it with the one the
+ * golden launch recorded; the GEMV compares every output word it writes with
+ * the golden output.  Differences are counted on the device for qg_verify, so
+ * a corruption in any launch of a batch is seen, not only in the last.
  * Replaces: the ai_workload_kernel launch of the timed loop
  *           (ai_workload_template.h:370). Asynchronous. */
 QG_API int  qg_run(qg_ctx* ctx, int iters, void* stream);
 
 /* Compare every copy's latest output (and checksums) with the golden result on
- * the device; `*mismatches` receives the number of differing 32-bit words.
+ * the device; `*mismatches` receives the number of differing 32-bit words plus
+ * the differences the per-launch checks of qg_run counted since the previous
+ * qg_verify (qg_verify_detail gives the two apart).
  * Replaces: ai_verify_output (ai_workload_template.h:343-349) and
  *           verify_mma_kernel (kernels/mma_virus/mma_virus.cpp:156-173). Synchronous. */
 QG_API int  qg_verify(qg_ctx* ctx, uint64_t* mismatches);
+
+/* The parts of the last qg_verify: differing output words of the final
+ * compare, differences found by the per-launch checks (row segments of a GEMM,
+ * output elements of the GEMV), and how many launches ran with a check.
+ * Replaces: the error count of verify_mma_kernel (mma_virus.cpp:156-173), split by source. */
+QG_API int  qg_verify_detail(const qg_ctx* ctx, uint64_t* words, uint64_t* launch_diffs,
+                             uint64_t* launches_checked);
+
+/* Flip bit `bit` (0-7) of byte `byte` of operand `slot` (qg_tensor's slots
+ * 0..3, or 0..3 of NVFP4's five) of copy `copy`, on `stream`, so the launches
+ * that read it compute a wrong result; flipping it again restores the operand.
+ * Used to show that the per-launch check catches a corruption in one launch of
+ * a batch that later launches overwrite.
+ * Replaces: the input corruption of --inject_error (ai_workload_template.h:90-92). */
+QG_API int  qg_flip_operand_bit(qg_ctx* ctx, int copy, int slot, uint64_t byte, int bit, void* stream);
 
 /* Copy out up to `cap` recorded mismatches of the last qg_verify; returns how many. */
 QG_API int  qg_mismatch_log(qg_ctx* ctx, qg_mismatch* out, int cap);
@@ -150,7 +174,8 @@ QG_API int  qg_download(qg_ctx* ctx, int copy, void* host_out, void* stream);
 QG_API int  qg_tensor(qg_ctx* ctx, int copy, int slot, void** ptr, uint64_t* bytes);
 
 /* Launch one GEMM (or GEMV) on copy `copy` (end-to-end path: qg_upload,
- * qg_run_copy, qg_download). Asynchronous. */
+ * qg_run_copy, qg_download). Asynchronous.  No per-launch check: the operands
+ * are the caller's, so the golden result need not apply to them. */
 QG_API int  qg_run_copy(qg_ctx* ctx, int copy, void* stream);
 
 /* Wait for all work on the context's device; returns QG_ERR_DEVICE_TIMEOUT if
@@ -299,6 +324,27 @@ QG_API int  qg_device_check(int device);
 /* Bounded-wait status of the most recent kernel on this device (QG_OK or
  * QG_ERR_DEVICE_TIMEOUT); clears the flag. Synchronous. */
 QG_API int  qg_device_status(int device);
+
+/* qg_device_status with its detail: `site` = (kernel id << 16) | wait site of
+ * the first wait that gave up (0 = none), `waits_expired` = how many waits gave
+ * up, `ctas_drained` = how many CTAs then let their copies and MMAs in flight
+ * land, freed their TMEM and returned.  Any pointer may be NULL; clears all three.
+ * Replaces: the CHECK / fault-log reporting of a kernel that failed
+ *           (kernels/common/common.h:231-240, kernels/common/fault_log.h:36-50). */
+QG_API int  qg_device_status_detail(int device, uint32_t* site, uint32_t* waits_expired,
+                                    uint32_t* ctas_drained);
+
+/* Fault drill of the bounded waits (no GPU fault, no hang): one INT8 GEMM
+ * (bf16 out, M < 256, the single-CTA kernel) whose producers stop before K
+ * block `withhold_kb` (< 4) of their first tile, with every wait limited to
+ * `wait_ns` (1e5 .. 2e9 ns).  The wait for the withheld block expires; each CTA
+ * records the site, drains and frees its TMEM and returns, so the call ends
+ * after about `wait_ns` and qg_device_status_detail then reports
+ * QG_ERR_DEVICE_TIMEOUT with ctas_drained = the grid's CTAs.  The device and
+ * the process stay usable for the next launch.  For tests of the failure path.
+ * No counterpart in the reference (its kernels have no bounded waits). */
+QG_API int  qg_fault_drill_i8(const void* A, const void* B, const void* sa, const void* sb, void* C,
+                              int M, int N, int K, uint64_t wait_ns, int withhold_kb, void* stream);
 
 /* Compare two word arrays on the device.  `count` is a device uint64[2]:
  * count[0] += number of differing 32-bit words, count[1] += number of

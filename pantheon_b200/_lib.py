@@ -49,6 +49,8 @@ _SIGNATURES = {
     "qg_golden": (C.c_int, [_V]),
     "qg_run": (C.c_int, [_V, C.c_int, _V]),
     "qg_verify": (C.c_int, [_V, C.POINTER(C.c_uint64)]),
+    "qg_verify_detail": (C.c_int, [_V, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    "qg_flip_operand_bit": (C.c_int, [_V, C.c_int, C.c_int, C.c_uint64, C.c_int, _V]),
     "qg_mismatch_log": (C.c_int, [_V, C.POINTER(QGMismatch), C.c_int]),
     "qg_inject": (C.c_int, [_V]),
     "qg_ops_per_launch": (C.c_double, [_V]),
@@ -83,6 +85,9 @@ _SIGNATURES = {
     "qg_gemv_w4a16_noalloc": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     "qg_gen_w4a16": (C.c_int, [_V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_uint32, _V]),
     "qg_device_status": (C.c_int, [C.c_int]),
+    "qg_device_status_detail": (C.c_int, [C.c_int, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                          C.POINTER(C.c_uint32)]),
+    "qg_fault_drill_i8": (C.c_int, [_V, _V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_int, _V]),
     "qg_verify_words": (C.c_int, [_V, _V, C.c_uint64, _V, _V, C.c_int, _V]),
     "qg_gen_i8": (C.c_int, [_V, C.c_uint64, C.c_uint64, C.c_uint32, _V]),
     "qg_gen_uniform_f32": (C.c_int, [_V, C.c_uint64, C.c_float, C.c_float, C.c_uint64, C.c_uint32, _V]),

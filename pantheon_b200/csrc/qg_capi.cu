@@ -17,10 +17,13 @@ struct qg_ctx {
     qg::Layout layout{};
     std::vector<qg::CopyBuffers> copies;
     unsigned long long* counters = nullptr;   // [0] mismatching words, [1] log entries
+    unsigned long long* launch_diffs = nullptr;   // per-launch check differences since the last qg_verify
     qg_mismatch* log = nullptr;
     int log_cap = 64;
     int next_copy = 0;
     bool golden_ready = false;
+    uint64_t launches_checked = 0;            // launches run with the per-launch check since the last qg_verify
+    uint64_t last_words = 0, last_launch_diffs = 0, last_launches = 0;   // split of the last qg_verify
     cudaStream_t stream = nullptr;            // internal stream for fill / golden / verify
     std::string err;
 };
@@ -50,12 +53,31 @@ void free_ctx_memory(qg_ctx* c) {
         if (cp.cksum) cudaFree(cp.cksum);
         if (cp.golden_cksum) cudaFree(cp.golden_cksum);
         if (cp.scratch) cudaFree(cp.scratch);
+        if (cp.check_fp) cudaFree(cp.check_fp);
     }
     c->copies.clear();
     if (c->counters) cudaFree(c->counters);
+    if (c->launch_diffs) cudaFree(c->launch_diffs);
     if (c->log) cudaFree(c->log);
     c->counters = nullptr;
+    c->launch_diffs = nullptr;
     c->log = nullptr;
+}
+
+// The per-launch check of a timed launch of copy `cp` (qg_check.cuh): GEMMs
+// compare their row-segment fingerprints with the golden launch's, the GEMV
+// compares its output words with the golden output.  Nothing before qg_golden.
+qg::LaunchCheck run_check(const qg_ctx* c, const qg::CopyBuffers& cp) {
+    qg::LaunchCheck k;
+    if (!c->golden_ready) return k;
+    if (c->layout.check_bytes) {
+        k.expect = static_cast<const uint32_t*>(cp.check_fp);
+        k.count = c->launch_diffs;
+    } else if (c->cfg.format == QG_FMT_W4A16) {
+        k.expect = static_cast<const uint32_t*>(cp.golden);
+        k.count = c->launch_diffs;
+    }
+    return k;
 }
 
 uint64_t out_alloc_bytes(const qg::Layout& L) { return (L.out_bytes + 15) / 16 * 16; }
@@ -78,7 +100,7 @@ int qg_required_bytes(const qg_cfg* cfg, uint64_t* bytes) {
     const int copies = cfg->copies > 0 ? cfg->copies : 1;
     uint64_t per = 0;
     for (int i = 0; i < L.n_ops; ++i) per += L.op_bytes[i];
-    per += 2 * out_alloc_bytes(L) + 2 * L.cksum_bytes + L.scratch_bytes;
+    per += 2 * out_alloc_bytes(L) + 2 * L.cksum_bytes + L.scratch_bytes + L.check_bytes;
     *bytes = per * (uint64_t)copies + 4096;
     return QG_OK;
 }
@@ -118,8 +140,11 @@ int qg_create(qg_ctx** out, int device, const qg_cfg* cfg) {
         if ((rc = alloc(&cp.cksum, L.cksum_bytes))) goto oom;
         if ((rc = alloc(&cp.golden_cksum, L.cksum_bytes))) goto oom;
         if ((rc = alloc(&cp.scratch, L.scratch_bytes))) goto oom;
+        if ((rc = alloc(&cp.check_fp, L.check_bytes))) goto oom;
     }
     if ((rc = alloc(reinterpret_cast<void**>(&c->counters), 2 * sizeof(unsigned long long)))) goto oom;
+    if ((rc = alloc(reinterpret_cast<void**>(&c->launch_diffs), sizeof(unsigned long long)))) goto oom;
+    if (cudaMemset(c->launch_diffs, 0, sizeof(unsigned long long)) != cudaSuccess) { rc = QG_ERR_CUDA; goto oom; }
     if ((rc = alloc(reinterpret_cast<void**>(&c->log), sizeof(qg_mismatch) * (size_t)c->log_cap))) goto oom;
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
         qg::set_error("qg_create: cudaStreamCreate failed");
@@ -159,7 +184,9 @@ int qg_golden(qg_ctx* c) {
     QG_CHECK_ARG(c, "qg_golden: null context");
     CTX_CUDA(c, cudaSetDevice(c->device));
     for (auto& cp : c->copies) {
-        int rc = qg::launch_copy(c->cfg, c->layout, cp, c->stream);
+        qg::LaunchCheck record;   // the golden launch records its fingerprints for the later launches
+        record.record = static_cast<uint32_t*>(cp.check_fp);
+        int rc = qg::launch_copy(c->cfg, c->layout, cp, c->stream, 0u, record);
         if (rc) return fail(c, rc);
         CTX_CUDA(c, cudaMemcpyAsync(cp.golden, cp.out, c->layout.out_bytes, cudaMemcpyDeviceToDevice, c->stream));
         if (c->layout.cksum_bytes)
@@ -169,6 +196,8 @@ int qg_golden(qg_ctx* c) {
     CTX_CUDA(c, cudaStreamSynchronize(c->stream));
     int st = qg_device_status(c->device);
     if (st) return fail(c, st);
+    CTX_CUDA(c, cudaMemset(c->launch_diffs, 0, sizeof(unsigned long long)));
+    c->launches_checked = 0;
     c->golden_ready = true;
     c->next_copy = 0;
     return QG_OK;
@@ -181,9 +210,11 @@ int qg_run(qg_ctx* c, int iters, void* stream) {
         // From the second launch on, the kernel before each GEMV on this stream is
         // the previous GEMV of this loop, which does not write the weights: their
         // first loads may start before the dependency wait.
-        int rc = qg::launch_copy(c->cfg, c->layout, c->copies[(size_t)c->next_copy], s,
-                                 i > 0 ? QG_GEMV_WEIGHTS_CONST : 0u);
+        const qg::CopyBuffers& cp = c->copies[(size_t)c->next_copy];
+        const qg::LaunchCheck chk = run_check(c, cp);
+        int rc = qg::launch_copy(c->cfg, c->layout, cp, s, i > 0 ? QG_GEMV_WEIGHTS_CONST : 0u, chk);
         if (rc) return fail(c, rc);
+        if (chk.count) ++c->launches_checked;
         c->next_copy = (c->next_copy + 1) % (int)c->copies.size();
     }
     return QG_OK;
@@ -205,13 +236,38 @@ int qg_verify(qg_ctx* c, uint64_t* mismatches) {
             if (rc) return fail(c, rc);
         }
     }
-    unsigned long long h[2] = {0, 0};
+    unsigned long long h[2] = {0, 0}, d = 0;
     CTX_CUDA(c, cudaMemcpyAsync(h, c->counters, sizeof(h), cudaMemcpyDeviceToHost, c->stream));
+    CTX_CUDA(c, cudaMemcpyAsync(&d, c->launch_diffs, sizeof(d), cudaMemcpyDeviceToHost, c->stream));
+    CTX_CUDA(c, cudaMemsetAsync(c->launch_diffs, 0, sizeof(d), c->stream));
     CTX_CUDA(c, cudaStreamSynchronize(c->stream));
     int st = qg_device_status(c->device);
     if (st) return fail(c, st);
-    *mismatches = h[0];
+    c->last_words = h[0];
+    c->last_launch_diffs = d;
+    c->last_launches = c->launches_checked;
+    c->launches_checked = 0;
+    *mismatches = h[0] + d;
     return QG_OK;
+}
+
+int qg_verify_detail(const qg_ctx* c, uint64_t* words, uint64_t* launch_diffs, uint64_t* launches_checked) {
+    QG_CHECK_ARG(c && words && launch_diffs && launches_checked, "qg_verify_detail: null argument");
+    *words = c->last_words;
+    *launch_diffs = c->last_launch_diffs;
+    *launches_checked = c->last_launches;
+    return QG_OK;
+}
+
+int qg_flip_operand_bit(qg_ctx* c, int copy, int slot, uint64_t byte, int bit, void* stream) {
+    QG_CHECK_ARG(c && copy >= 0 && copy < (int)c->copies.size(), "qg_flip_operand_bit: bad copy");
+    QG_CHECK_ARG(slot >= 0 && slot < c->layout.n_ops && byte < c->layout.op_bytes[slot] && bit >= 0 && bit < 8,
+                 "qg_flip_operand_bit: no byte %llu bit %d in operand slot %d", (unsigned long long)byte, bit, slot);
+    QG_CHECK_ARG(!(c->cfg.format == QG_FMT_NVFP4 && slot == 4),
+                 "qg_flip_operand_bit: the NVFP4 per-tensor scales are passed by value; flip another slot");
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    int rc = qg::flip_bit_at(c->copies[(size_t)copy].op[slot], byte, bit, static_cast<cudaStream_t>(stream));
+    return rc ? fail(c, rc) : QG_OK;
 }
 
 int qg_mismatch_log(qg_ctx* c, qg_mismatch* out, int cap) {

@@ -105,16 +105,22 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 
 } // namespace qg
 
-extern "C" int qg_device_status(int device) {
+extern "C" int qg_device_status_detail(int device, uint32_t* site, uint32_t* waits_expired, uint32_t* ctas_drained) {
     QG_CUDA(cudaSetDevice(device));
     qg::DeviceStatus* p = nullptr;
     int rc = qg::device_status_ptr(&p);
     if (rc) return rc;
     qg::DeviceStatus h{};
     QG_CUDA(cudaMemcpy(&h, p, sizeof(h), cudaMemcpyDeviceToHost));
-    if (h.code == 0) return QG_OK;
-    qg::set_error("device wait expired: site 0x%08x (%u waits gave up)", h.code, h.count);
+    if (site) *site = h.code;
+    if (waits_expired) *waits_expired = h.count;
+    if (ctas_drained) *ctas_drained = h.drained;
+    if (h.code == 0 && h.drained == 0) return QG_OK;
+    qg::set_error("device wait expired: site 0x%08x (%u waits gave up, %u CTAs drained and freed TMEM)", h.code,
+                  h.count, h.drained);
     qg::DeviceStatus z{};
     QG_CUDA(cudaMemcpy(p, &z, sizeof(z), cudaMemcpyHostToDevice));
-    return QG_ERR_DEVICE_TIMEOUT;
+    return h.code ? QG_ERR_DEVICE_TIMEOUT : QG_OK;
 }
+
+extern "C" int qg_device_status(int device) { return qg_device_status_detail(device, nullptr, nullptr, nullptr); }

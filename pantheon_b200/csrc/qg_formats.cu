@@ -38,6 +38,7 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
             l.op_bytes[3] = 4ull * l.N;
             l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
             l.cksum_bytes = 4ull * l.M;
+            l.check_bytes = 4ull * gemm_i8_check_slots(l.M, l.N);
             l.ops = 2.0 * l.M * (double)l.N * l.K;
             l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes + l.cksum_bytes);
             break;
@@ -54,6 +55,7 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
             l.op_bytes[2] = 4ull * l.M * (l.K / 128);
             l.op_bytes[3] = 4ull * ((l.N + 127) / 128) * (l.K / 128);
             l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
+            l.check_bytes = 4ull * gemm_fp8_check_slots(l.M, l.N);
             l.ops = 2.0 * l.M * (double)l.N * l.K;
             l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes);
             break;
@@ -71,6 +73,7 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
             l.op_bytes[3] = nvfp4_sf_bytes(l.N, l.K);
             l.op_bytes[4] = 16;
             l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
+            l.check_bytes = 4ull * gemm_nvfp4_check_slots(l.M, l.N);
             l.scratch_bytes = 16;
             l.ops = 2.0 * l.M * (double)l.N * l.K;
             l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes);
@@ -112,6 +115,8 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
             l.op_bytes[0] = (uint64_t)l.M * l.K * eb;
             l.op_bytes[1] = (uint64_t)l.N * l.K * eb;
             l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
+            // the fp32 CUDA-core GEMM has no per-launch check: its output is compared per batch only
+            if (cfg.format != QG_FMT_FP32) l.check_bytes = 4ull * gemm_i8_check_slots(l.M, l.N);
             l.ops = 2.0 * l.M * (double)l.N * l.K;
             l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.out_bytes);
             break;
@@ -166,23 +171,24 @@ int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_inde
     }
 }
 
-int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaStream_t s, unsigned int gemv_flags) {
+int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaStream_t s, unsigned int gemv_flags,
+                const LaunchCheck& chk) {
     switch (cfg.format) {
         case QG_FMT_INT8:
-            return gemm_i8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, cp.cksum, L.M, L.N, L.K, s);
+            return gemm_i8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, cp.cksum, L.M, L.N, L.K, s, chk);
         case QG_FMT_FP8:
-            return gemm_fp8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, s);
+            return gemm_fp8(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, s, chk);
         case QG_FMT_NVFP4:
             return gemm_nvfp4(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.global_a, cp.global_b, cp.out, L.out_type,
-                              L.M, L.N, L.K, s);
+                              L.M, L.N, L.K, s, chk);
         case QG_FMT_W4A16:
             return gemv_w4a16(cp.op[0], cp.op[1], cp.op[2], cp.op[3], cp.out, L.out_type, L.M, L.N, L.K, cp.scratch,
-                              L.scratch_bytes, s, gemv_flags);
+                              L.scratch_bytes, s, gemv_flags, chk);
         case QG_FMT_BF16:
         case QG_FMT_FP16:
         case QG_FMT_TF32:
         case QG_FMT_E4M3:
-            return gemm_dense_format(cfg.format, cp.op[0], cp.op[1], 1.0f, cp.out, L.out_type, L.M, L.N, L.K, s);
+            return gemm_dense_format(cfg.format, cp.op[0], cp.op[1], 1.0f, cp.out, L.out_type, L.M, L.N, L.K, s, chk);
         case QG_FMT_FP32:
             return gemm_f32(cp.op[0], cp.op[1], 1.0f, cp.out, L.out_type, L.M, L.N, L.K, s);
         default:

@@ -21,6 +21,7 @@
 //               last K block converts and stores its row segment.
 // All barrier waits are bounded (qg_ptx.cuh).
 #include "qg_common.cuh"
+#include "qg_check.cuh"
 
 #include <cuda_bf16.h>
 
@@ -66,6 +67,7 @@ struct Params {
     const float* sb;     // [ceil(N/128), K/128]
     void* C;
     DeviceStatus* status;
+    LaunchCheck chk;     // per-launch check: one fingerprint per (row, 128-column segment)
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
@@ -171,6 +173,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         const int half = (warp - EPI_WARP0) >> 2;        // column half 0 / 1 of the tile
         const int row = quarter * 32 + lane;
         const int sb_rows = (p.N + 127) / 128;
+        const bool fold = p.chk.record != nullptr || p.chk.expect != nullptr;
         uint32_t pcount = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
@@ -226,9 +229,12 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 if (lane == 0) mbar_arrive(&bars->part_empty[buf]);
             }
             if (!ok) break;
-            // store this row's 128-column segment
+            // store this row's 128-column segment, folding the stored words into
+            // its fingerprint in a golden or checked launch (qg_check.cuh)
             const int n0 = nt * BN + half * COLS_PER_EPI;
-            if (row_ok && n0 < p.N) {
+            const bool seg_ok = row_ok && n0 < p.N;
+            uint32_t ofp = 0;
+            if (seg_ok) {
                 const bool full_seg = (n0 + COLS_PER_EPI <= p.N);
                 if (OUT == QG_OUT_F32) {
                     float* dst = static_cast<float*>(p.C) + (size_t)m * p.N + n0;
@@ -241,6 +247,12 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                         for (int i = 0; i < COLS_PER_EPI; ++i)
                             if (n0 + i < p.N) dst[i] = acc[i];
                     }
+                    if (fold) {
+#pragma unroll
+                        for (int i = 0; i < COLS_PER_EPI; ++i)
+                            if (full_seg || n0 + i < p.N)
+                                ofp += __float_as_uint(acc[i]) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                    }
                 } else {
                     __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
                     if (full_seg && (p.N % 8) == 0) {
@@ -251,16 +263,25 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                             for (int j = 0; j < 4; ++j) {
                                 __nv_bfloat162 h = __floats2bfloat162_rn(acc[i + 2 * j], acc[i + 2 * j + 1]);
                                 w[j] = *reinterpret_cast<uint32_t*>(&h);
+                                if (fold) ofp += w[j] * check_weight((uint32_t)m, (uint32_t)(n0 + i + 2 * j));
                             }
                             *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
                         }
                     } else {
 #pragma unroll
                         for (int i = 0; i < COLS_PER_EPI; ++i)
-                            if (n0 + i < p.N) dst[i] = __float2bfloat16_rn(acc[i]);
+                            if (n0 + i < p.N) {
+                                const __nv_bfloat16 h = __float2bfloat16_rn(acc[i]);
+                                dst[i] = h;
+                                if (fold)
+                                    ofp += (uint32_t)__bfloat16_as_ushort(h) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                            }
                     }
                 }
             }
+            if (fold)
+                check_segment(p.chk, seg_ok, (uint64_t)m * (uint64_t)((p.N + COLS_PER_EPI - 1) / COLS_PER_EPI) +
+                                                 (uint64_t)(nt * 2 + half), ofp);
         }
     }
 
@@ -274,7 +295,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 
 template <int OUT>
 static int launch(const void* A, const void* B, const float* sa, const float* sb, void* C, int M, int N, int K,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, const LaunchCheck& chk) {
     DeviceInfo* info = nullptr;
     int rc = current_device_info(&info);
     if (rc) return rc;
@@ -295,7 +316,7 @@ static int launch(const void* A, const void* B, const float* sa, const float* sb
         QG_CUDA(cudaFuncSetAttribute(gemm_fp8_kernel<QG_OUT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         attr_set[dev & 63] = true;
     }
-    Params p{M, N, K, sa, sb, C, status};
+    Params p{M, N, K, sa, sb, C, status, chk};
     const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
     const int grid = tiles < info->sm_count ? tiles : info->sm_count;
     gemm_fp8_kernel<OUT><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, p);
@@ -305,16 +326,18 @@ static int launch(const void* A, const void* B, const float* sa, const float* sb
 
 } // namespace f8
 
+uint64_t gemm_fp8_check_slots(int M, int N) { return (uint64_t)M * (uint64_t)((N + f8::COLS_PER_EPI - 1) / f8::COLS_PER_EPI); }
+
 int gemm_fp8(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type, int M, int N, int K,
-             cudaStream_t stream) {
+             cudaStream_t stream, const LaunchCheck& chk) {
     QG_CHECK_ARG(A && B && sa && sb && C, "qg_gemm_fp8_b128: null operand");
     QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemm_fp8_b128: empty shape %dx%dx%d", M, N, K);
     QG_CHECK_ARG(K % 128 == 0, "qg_gemm_fp8_b128: K=%d must be a multiple of 128 (scale block)", K);
     const float* fsa = static_cast<const float*>(sa);
     const float* fsb = static_cast<const float*>(sb);
     switch (out_type) {
-        case QG_OUT_BF16: return f8::launch<QG_OUT_BF16>(A, B, fsa, fsb, C, M, N, K, stream);
-        case QG_OUT_F32: return f8::launch<QG_OUT_F32>(A, B, fsa, fsb, C, M, N, K, stream);
+        case QG_OUT_BF16: return f8::launch<QG_OUT_BF16>(A, B, fsa, fsb, C, M, N, K, stream, chk);
+        case QG_OUT_F32: return f8::launch<QG_OUT_F32>(A, B, fsa, fsb, C, M, N, K, stream, chk);
         default: set_error("qg_gemm_fp8_b128: bad out_type %d", out_type); return QG_ERR_ARG;
     }
 }
@@ -323,5 +346,5 @@ int gemm_fp8(const void* A, const void* B, const void* sa, const void* sb, void*
 
 extern "C" int qg_gemm_fp8_b128(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type,
                                 int M, int N, int K, void* stream) {
-    return qg::gemm_fp8(A, B, sa, sb, C, out_type, M, N, K, static_cast<cudaStream_t>(stream));
+    return qg::gemm_fp8(A, B, sa, sb, C, out_type, M, N, K, static_cast<cudaStream_t>(stream), qg::LaunchCheck{});
 }

@@ -20,6 +20,7 @@
 // the site in the device status word, drains its in-flight copies and MMAs,
 // frees TMEM and returns.
 #include "qg_common.cuh"
+#include "qg_check.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -110,7 +111,18 @@ struct Params {
     uint32_t* row_cksum;
     DeviceStatus* status;
     float alpha;            // output scale of the f32-accumulating kinds
+    LaunchCheck chk;        // per-launch check: one fingerprint per (row, 256-column tile)
+    // Fault drill (qg_fault_drill_i8, single-CTA kernel only): every bounded wait
+    // gives up after wait_ns, and the producer of each CTA stops before the
+    // withhold_kb-th K block of its first tile, so the MMA's wait for it expires.
+    uint64_t wait_ns = QG_WAIT_LIMIT_NS;
+    int withhold_kb = -1;
 };
+
+// Fingerprint slot of row m, column tile nt (qg_check.cuh).
+__device__ __forceinline__ uint64_t seg_index(int m, int nt, int N) {
+    return (uint64_t)m * (uint64_t)((N + BN - 1) / BN) + (uint64_t)nt;
+}
 
 template <int GROUP_M>
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
@@ -129,12 +141,15 @@ __device__ __forceinline__ uint32_t cksum_weight(uint32_t m, uint32_t n) {
 
 // One 32-column chunk of an accumulator row: checksum fold, then the s32 /
 // dequantised f32 / bf16 store (ragged edges handled per element).
+// `fold` (uniform: a golden or checked launch) adds every stored output word,
+// times its odd weight, to `ofp`; the INT8 kind then also folds its
+// accumulators into `ck` (the row checksum's fold) even without row checksums.
 template <int KIND, int OUT>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, int n0, bool row_ok, float sam,
-                                               const Params& p, uint32_t& ck) {
+                                               const Params& p, uint32_t& ck, bool fold, uint32_t& ofp) {
     if (!row_ok || n0 >= p.N) return;
     const bool full_chunk = (n0 + 32 <= p.N);
-    if (p.row_cksum) {
+    if (KIND == KIND_I8 && (p.row_cksum || fold)) {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
             if (full_chunk || n0 + i < p.N) ck += r[i] * cksum_weight((uint32_t)m, (uint32_t)(n0 + i));
@@ -149,6 +164,11 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
 #pragma unroll
             for (int i = 0; i < 32; ++i)
                 if (n0 + i < p.N) dst[i] = (int32_t)r[i];
+        }
+        if (fold) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (full_chunk || n0 + i < p.N) ofp += r[i] * check_weight((uint32_t)m, (uint32_t)(n0 + i));
         }
         return;
     }
@@ -182,6 +202,11 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
             for (int i = 0; i < 32; ++i)
                 if (n0 + i < p.N) dst[i] = f[i];
         }
+        if (fold) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (full_chunk || n0 + i < p.N) ofp += __float_as_uint(f[i]) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+        }
     } else if (OUT == QG_OUT_F16) {
         __half* dst = static_cast<__half*>(p.C) + (size_t)m * p.N + n0;
         if (full_chunk && (p.N % 8) == 0) {
@@ -194,10 +219,18 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
 #pragma unroll
             for (int i = 0; i < 16; i += 4)
                 *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+            if (fold) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) ofp += w[i] * check_weight((uint32_t)m, (uint32_t)(n0 + 2 * i));
+            }
         } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-                if (n0 + i < p.N) dst[i] = __float2half_rn(f[i]);
+                if (n0 + i < p.N) {
+                    const __half h = __float2half_rn(f[i]);
+                    dst[i] = h;
+                    if (fold) ofp += (uint32_t)__half_as_ushort(h) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                }
         }
     } else {
         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
@@ -211,10 +244,18 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
 #pragma unroll
             for (int i = 0; i < 16; i += 4)
                 *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+            if (fold) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) ofp += w[i] * check_weight((uint32_t)m, (uint32_t)(n0 + 2 * i));
+            }
         } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-                if (n0 + i < p.N) dst[i] = __float2bfloat16_rn(f[i]);
+                if (n0 + i < p.N) {
+                    const __nv_bfloat16 h = __float2bfloat16_rn(f[i]);
+                    dst[i] = h;
+                    if (fold) ofp += (uint32_t)__bfloat16_as_ushort(h) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                }
         }
     }
 }
@@ -266,7 +307,8 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             int mt, nt;
             tile_coords<group_m(KIND)>(t, tiles_m, tiles_n, mt, nt);
             for (int kb = 0; kb < nk; ++kb) {
-                if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER)) { ok = false; break; }
+                if (kb == p.withhold_kb && t == (int)blockIdx.x) { ok = false; break; }   // fault drill only
+                if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER, p.wait_ns)) { ok = false; break; }
                 mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
                 tma_load_2d(sA + stage * A_BYTES, &tmA, &bars->full[stage], kb * BK, mt * BM);
                 tma_load_2d(sB + stage * B_BYTES, &tmB, &bars->full[stage], kb * BK, nt * BN);
@@ -289,11 +331,11 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++iter) {
             const uint32_t acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
-            if (!mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.status, SITE_MMA_TMEM)) { ok = false; break; }
+            if (!mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.status, SITE_MMA_TMEM, p.wait_ns)) { ok = false; break; }
             tc_fence_after();
             const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
             for (int kb = 0; kb < nk; ++kb) {
-                if (!mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_MMA_FULL)) { ok = false; break; }
+                if (!mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_MMA_FULL, p.wait_ns)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
                 const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
@@ -318,6 +360,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // ------------------------------------------------------------ epilogue
         const int ew = warp - EPI_WARP0;               // TMEM lane quarter of this warp
         const int row = ew * 32 + lane;
+        const bool fold = p.chk.record != nullptr || p.chk.expect != nullptr;
         int iter = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
             int mt, nt;
@@ -325,7 +368,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const uint32_t acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
             int ok = 1;
-            if (lane == 0) ok = mbar_wait(&bars->tmem_full[acc], acc_phase, abort_flag, p.status, SITE_EPI) ? 1 : 0;
+            if (lane == 0) ok = mbar_wait(&bars->tmem_full[acc], acc_phase, abort_flag, p.status, SITE_EPI, p.wait_ns) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
@@ -333,7 +376,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int m = mt * BM + row;
             const bool row_ok = m < p.M;
             const float sam = (KIND == KIND_I8 && OUT != QG_OUT_S32 && row_ok) ? __ldg(p.sa + m) : 0.0f;
-            uint32_t ck = 0;
+            uint32_t ck = 0, ofp = 0;
             const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * ACC_COLS;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
@@ -341,11 +384,12 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 __syncwarp();
                 tmem_ld_32x32b_x32(t_row + c, r);
                 tmem_ld_wait_regs(r);
-                epilogue_chunk<KIND, OUT>(r, m, nt * BN + c, row_ok, sam, p, ck);
+                epilogue_chunk<KIND, OUT>(r, m, nt * BN + c, row_ok, sam, p, ck, fold, ofp);
             }
             tc_fence_before();
             mbar_arrive(&bars->tmem_empty[acc]);
             if (p.row_cksum && row_ok) atomicAdd(p.row_cksum + m, ck);
+            if (fold) check_segment(p.chk, row_ok, seg_index(m, nt, p.N), ck + ofp);
         }
     }
 
@@ -354,6 +398,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (warp == 2) {
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
+        if (lane == 0 && *abort_flag) atomicAdd(&p.status->drained, 1u);   // gave up, drained, TMEM freed
     }
 }
 
@@ -439,7 +484,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             int mt, nt;
             tile_coords<group_m(KIND)>(t, tiles_m, tiles_n, mt, nt);
             for (int kb = 0; kb < nk; ++kb) {
-                if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER)) { ok = false; break; }
+                if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER, p.wait_ns)) { ok = false; break; }
                 if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * P_STAGE_BYTES);
                 const uint32_t full_leader = mapa_shared(smem_u32(&bars->full[stage]), 0);
                 tma_load_2d_pair(sA + stage * PA_BYTES, &tmA, full_leader, kb * BK, mt * 2 * BM + (int)rank * BM);
@@ -463,11 +508,11 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         for (int t = pair; t < tiles && ok; t += pairs, ++iter) {
             const uint32_t acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
-            if (!mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.status, SITE_MMA_TMEM)) { ok = false; break; }
+            if (!mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.status, SITE_MMA_TMEM, p.wait_ns)) { ok = false; break; }
             tc_fence_after();
             const uint32_t d_tmem = tmem_base + acc * ACC_COLS;
             for (int kb = 0; kb < nk; ++kb) {
-                if (!mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_MMA_FULL)) { ok = false; break; }
+                if (!mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_MMA_FULL, p.wait_ns)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t a_addr = smem_u32(sA + stage * PA_BYTES);
                 const uint32_t b_addr = smem_u32(sB + stage * PB_BYTES);
@@ -495,6 +540,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         // ------------------------------------------------------------ epilogue (both CTAs)
         const int ew = warp - EPI_WARP0;
         const int row = ew * 32 + lane;
+        const bool fold = p.chk.record != nullptr || p.chk.expect != nullptr;
         int iter = 0;
         for (int t = pair; t < tiles; t += pairs, ++iter) {
             int mt, nt;
@@ -502,14 +548,14 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             const uint32_t acc = iter & 1;
             const uint32_t acc_phase = (iter >> 1) & 1;
             int ok = 1;
-            if (lane == 0) ok = mbar_wait(&bars->tmem_full[acc], acc_phase, abort_flag, p.status, SITE_EPI) ? 1 : 0;
+            if (lane == 0) ok = mbar_wait(&bars->tmem_full[acc], acc_phase, abort_flag, p.status, SITE_EPI, p.wait_ns) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
             const int m = mt * 2 * BM + (int)rank * BM + row;
             const bool row_ok = m < p.M;
             const float sam = (KIND == KIND_I8 && OUT != QG_OUT_S32 && row_ok) ? __ldg(p.sa + m) : 0.0f;
-            uint32_t ck = 0;
+            uint32_t ck = 0, ofp = 0;
             const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * ACC_COLS;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
@@ -517,12 +563,13 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 __syncwarp();
                 tmem_ld_32x32b_x32(t_row + c, r);
                 tmem_ld_wait_regs(r);
-                epilogue_chunk<KIND, OUT>(r, m, nt * BN + c, row_ok, sam, p, ck);
+                epilogue_chunk<KIND, OUT>(r, m, nt * BN + c, row_ok, sam, p, ck, fold, ofp);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&bars->tmem_empty[acc]), 0));
             if (p.row_cksum && row_ok) atomicAdd(p.row_cksum + m, ck);
+            if (fold) check_segment(p.chk, row_ok, seg_index(m, nt, p.N), ck + ofp);
         }
     }
 
@@ -533,12 +580,14 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     if (warp == 2) {
         tc_fence_after();
         tmem_dealloc_pair(tmem_base, TMEM_COLS);
+        if (lane == 0 && *abort_flag) atomicAdd(&p.status->drained, 1u);   // gave up, drained, TMEM freed
     }
 }
 
 template <int KIND, int OUT>
 static int launch(const void* A, const void* B, const float* sa, const float* sb, float alpha, void* C,
-                  uint32_t* cksum, int M, int N, int K, cudaStream_t stream) {
+                  uint32_t* cksum, int M, int N, int K, cudaStream_t stream, const LaunchCheck& chk = LaunchCheck{},
+                  uint64_t wait_ns = QG_WAIT_LIMIT_NS, int withhold_kb = -1) {
     DeviceInfo* info = nullptr;
     int rc = current_device_info(&info);
     if (rc) return rc;
@@ -563,8 +612,8 @@ static int launch(const void* A, const void* B, const float* sa, const float* sb
     }
     if (cksum) QG_CUDA(cudaMemsetAsync(cksum, 0, sizeof(uint32_t) * (size_t)M, stream));
 
-    Params p{M, N, K, sa, sb, C, cksum, status, alpha};
-    if (M >= 2 * BM && info->sm_count >= 2) {
+    Params p{M, N, K, sa, sb, C, cksum, status, alpha, chk, wait_ns, withhold_kb};
+    if (M >= 2 * BM && info->sm_count >= 2 && withhold_kb < 0) {
         // CTA pairs: each CTA's B box is half a tile high
         CUtensorMap tmBh;
         if ((rc = make_tmap_2d(&tmBh, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, kb, (uint64_t)N, kb, BK, BN / 2,
@@ -602,7 +651,7 @@ static int launch(const void* A, const void* B, const float* sa, const float* sb
 } // namespace i8
 
 int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type, void* row_cksum,
-            int M, int N, int K, cudaStream_t stream) {
+            int M, int N, int K, cudaStream_t stream, const LaunchCheck& chk) {
     QG_CHECK_ARG(A && B && C, "qg_gemm_i8: null operand or output");
     QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemm_i8: empty shape %dx%dx%d", M, N, K);
     QG_CHECK_ARG(K % 16 == 0, "qg_gemm_i8: K=%d must be a multiple of 16 (TMA row stride)", K);
@@ -612,11 +661,32 @@ int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* 
     const float* fsb = static_cast<const float*>(sb);
     uint32_t* ck = static_cast<uint32_t*>(row_cksum);
     switch (out_type) {
-        case QG_OUT_BF16: return i8::launch<i8::KIND_I8, QG_OUT_BF16>(A, B, fsa, fsb, 1.0f, C, ck, M, N, K, stream);
-        case QG_OUT_F32: return i8::launch<i8::KIND_I8, QG_OUT_F32>(A, B, fsa, fsb, 1.0f, C, ck, M, N, K, stream);
-        case QG_OUT_S32: return i8::launch<i8::KIND_I8, QG_OUT_S32>(A, B, fsa, fsb, 1.0f, C, ck, M, N, K, stream);
+        case QG_OUT_BF16: return i8::launch<i8::KIND_I8, QG_OUT_BF16>(A, B, fsa, fsb, 1.0f, C, ck, M, N, K, stream, chk);
+        case QG_OUT_F32: return i8::launch<i8::KIND_I8, QG_OUT_F32>(A, B, fsa, fsb, 1.0f, C, ck, M, N, K, stream, chk);
+        case QG_OUT_S32: return i8::launch<i8::KIND_I8, QG_OUT_S32>(A, B, fsa, fsb, 1.0f, C, ck, M, N, K, stream, chk);
         default: set_error("qg_gemm_i8: unknown out_type %d", out_type); return QG_ERR_ARG;
     }
+}
+
+uint64_t gemm_i8_check_slots(int M, int N) { return (uint64_t)M * (uint64_t)((N + i8::BN - 1) / i8::BN); }
+
+// Fault drill: one INT8 GEMM (bf16 out) on the single-CTA kernel whose
+// producers stop before K block `withhold_kb` of their first tile, with every
+// bounded wait limited to `wait_ns`.  The MMA issuer's wait for the withheld
+// block expires; the kernel records the site, lets its copies and MMAs in
+// flight land, frees TMEM and returns.
+int fault_drill_i8(const void* A, const void* B, const void* sa, const void* sb, void* C, int M, int N, int K,
+                   uint64_t wait_ns, int withhold_kb, cudaStream_t stream) {
+    QG_CHECK_ARG(A && B && sa && sb && C, "qg_fault_drill_i8: null operand or output");
+    QG_CHECK_ARG(M > 0 && M < 2 * i8::BM && N > 0 && K > 0 && K % 16 == 0,
+                 "qg_fault_drill_i8: shape %dx%dx%d (M < 256 for the single-CTA kernel, K %% 16 == 0)", M, N, K);
+    QG_CHECK_ARG(withhold_kb >= 0 && withhold_kb < (K + i8::BK - 1) / i8::BK && withhold_kb < i8::STAGES,
+                 "qg_fault_drill_i8: withhold_kb %d must name a K block within the first %d of the tile",
+                 withhold_kb, i8::STAGES);
+    QG_CHECK_ARG(wait_ns >= 100000ull && wait_ns <= QG_WAIT_LIMIT_NS,
+                 "qg_fault_drill_i8: wait limit %llu ns outside [1e5, 2e9]", (unsigned long long)wait_ns);
+    return i8::launch<i8::KIND_I8, QG_OUT_BF16>(A, B, static_cast<const float*>(sa), static_cast<const float*>(sb),
+                                                1.0f, C, nullptr, M, N, K, stream, LaunchCheck{}, wait_ns, withhold_kb);
 }
 
 // Tensor-furnace GEMMs: C = alpha * A B^T with f32 accumulation; bf16, fp16,
@@ -624,11 +694,11 @@ int gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* 
 namespace {
 template <int KIND>
 int dense_out(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
-              cudaStream_t stream) {
+              cudaStream_t stream, const LaunchCheck& chk) {
     switch (out_type) {
-        case QG_OUT_BF16: return i8::launch<KIND, QG_OUT_BF16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
-        case QG_OUT_F16: return i8::launch<KIND, QG_OUT_F16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
-        default: return i8::launch<KIND, QG_OUT_F32>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream);
+        case QG_OUT_BF16: return i8::launch<KIND, QG_OUT_BF16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream, chk);
+        case QG_OUT_F16: return i8::launch<KIND, QG_OUT_F16>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream, chk);
+        default: return i8::launch<KIND, QG_OUT_F32>(A, B, nullptr, nullptr, alpha, C, nullptr, M, N, K, stream, chk);
     }
 }
 } // namespace
@@ -644,7 +714,7 @@ const char* dense_kind_entry(int kind) {
 }
 
 int gemm_dense(int kind, const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
-               cudaStream_t stream) {
+               cudaStream_t stream, const LaunchCheck& chk = LaunchCheck{}) {
     const char* name = dense_kind_entry(kind);
     QG_CHECK_ARG(kind == i8::KIND_BF16 || kind == i8::KIND_F16 || kind == i8::KIND_TF32 || kind == i8::KIND_E4M3,
                  "%s: unknown operand kind %d", name, kind);
@@ -654,20 +724,20 @@ int gemm_dense(int kind, const void* A, const void* B, float alpha, void* C, int
     QG_CHECK_ARG(out_type == QG_OUT_BF16 || out_type == QG_OUT_F16 || out_type == QG_OUT_F32,
                  "%s: out_type %d (bf16, f16 or f32)", name, out_type);
     switch (kind) {
-        case i8::KIND_BF16: return dense_out<i8::KIND_BF16>(A, B, alpha, C, out_type, M, N, K, stream);
-        case i8::KIND_F16: return dense_out<i8::KIND_F16>(A, B, alpha, C, out_type, M, N, K, stream);
-        case i8::KIND_TF32: return dense_out<i8::KIND_TF32>(A, B, alpha, C, out_type, M, N, K, stream);
-        default: return dense_out<i8::KIND_E4M3>(A, B, alpha, C, out_type, M, N, K, stream);
+        case i8::KIND_BF16: return dense_out<i8::KIND_BF16>(A, B, alpha, C, out_type, M, N, K, stream, chk);
+        case i8::KIND_F16: return dense_out<i8::KIND_F16>(A, B, alpha, C, out_type, M, N, K, stream, chk);
+        case i8::KIND_TF32: return dense_out<i8::KIND_TF32>(A, B, alpha, C, out_type, M, N, K, stream, chk);
+        default: return dense_out<i8::KIND_E4M3>(A, B, alpha, C, out_type, M, N, K, stream, chk);
     }
 }
 
 int gemm_dense_format(int fmt, const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const LaunchCheck& chk) {
     switch (fmt) {
-        case QG_FMT_BF16: return gemm_dense(i8::KIND_BF16, A, B, alpha, C, out_type, M, N, K, stream);
-        case QG_FMT_FP16: return gemm_dense(i8::KIND_F16, A, B, alpha, C, out_type, M, N, K, stream);
-        case QG_FMT_TF32: return gemm_dense(i8::KIND_TF32, A, B, alpha, C, out_type, M, N, K, stream);
-        case QG_FMT_E4M3: return gemm_dense(i8::KIND_E4M3, A, B, alpha, C, out_type, M, N, K, stream);
+        case QG_FMT_BF16: return gemm_dense(i8::KIND_BF16, A, B, alpha, C, out_type, M, N, K, stream, chk);
+        case QG_FMT_FP16: return gemm_dense(i8::KIND_F16, A, B, alpha, C, out_type, M, N, K, stream, chk);
+        case QG_FMT_TF32: return gemm_dense(i8::KIND_TF32, A, B, alpha, C, out_type, M, N, K, stream, chk);
+        case QG_FMT_E4M3: return gemm_dense(i8::KIND_E4M3, A, B, alpha, C, out_type, M, N, K, stream, chk);
         default: set_error("format %d is not a dense format", fmt); return QG_ERR_ARG;
     }
 }
@@ -676,7 +746,8 @@ int gemm_dense_format(int fmt, const void* A, const void* B, float alpha, void* 
 
 extern "C" int qg_gemm_i8(const void* A, const void* B, const void* sa, const void* sb, void* C, int out_type,
                           void* row_checksums, int M, int N, int K, void* stream) {
-    return qg::gemm_i8(A, B, sa, sb, C, out_type, row_checksums, M, N, K, static_cast<cudaStream_t>(stream));
+    return qg::gemm_i8(A, B, sa, sb, C, out_type, row_checksums, M, N, K, static_cast<cudaStream_t>(stream),
+                       qg::LaunchCheck{});
 }
 
 extern "C" int qg_gemm_bf16(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
@@ -697,4 +768,9 @@ extern "C" int qg_gemm_f16(const void* A, const void* B, float alpha, void* C, i
 extern "C" int qg_gemm_tf32(const void* A, const void* B, float alpha, void* C, int out_type, int M, int N, int K,
                             void* stream) {
     return qg::gemm_dense(qg::i8::KIND_TF32, A, B, alpha, C, out_type, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qg_fault_drill_i8(const void* A, const void* B, const void* sa, const void* sb, void* C, int M, int N,
+                                 int K, uint64_t wait_ns, int withhold_kb, void* stream) {
+    return qg::fault_drill_i8(A, B, sa, sb, C, M, N, K, wait_ns, withhold_kb, static_cast<cudaStream_t>(stream));
 }

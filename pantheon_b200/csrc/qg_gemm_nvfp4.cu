@@ -32,6 +32,7 @@
 //               scale by GA*GB, round, store.
 // All barrier waits are bounded (qg_ptx.cuh).
 #include "qg_common.cuh"
+#include "qg_check.cuh"
 
 #include <cuda_bf16.h>
 
@@ -101,6 +102,7 @@ struct Params {
     void* C;
     DeviceStatus* status;
     int group_m;          // row-tiles per rasterisation group
+    LaunchCheck chk;      // per-launch check: one fingerprint per (row, 128-column segment)
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& mt, int& nt) {
@@ -272,6 +274,7 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
         const int quarter = warp & 3;
         const int half = (warp - EPI_WARP0) >> 2;
         const int row = quarter * 32 + lane;
+        const bool fold = p.chk.record != nullptr || p.chk.expect != nullptr;
         int iter = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++iter) {
             int mt, nt;
@@ -284,6 +287,7 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
             const int m = mt * BM + row;
             const bool row_ok = m < p.M;
             const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * (BN / 2);
+            uint32_t ofp = 0;   // fingerprint of the words stored for this row segment (qg_check.cuh)
 #pragma unroll 1
             for (int c = 0; c < BN / 2; c += 32) {
                 uint32_t r[32];
@@ -306,6 +310,12 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                         for (int i = 0; i < 32; ++i)
                             if (n0 + i < p.N) dst[i] = f[i];
                     }
+                    if (fold) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (full_chunk || n0 + i < p.N)
+                                ofp += __float_as_uint(f[i]) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                    }
                 } else {
                     __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
                     if (full_chunk && (p.N % 8) == 0) {
@@ -316,19 +326,30 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                             for (int j = 0; j < 4; ++j) {
                                 __nv_bfloat162 h = __floats2bfloat162_rn(f[i + 2 * j], f[i + 2 * j + 1]);
                                 w[j] = *reinterpret_cast<uint32_t*>(&h);
+                                if (fold) ofp += w[j] * check_weight((uint32_t)m, (uint32_t)(n0 + i + 2 * j));
                             }
                             *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
                         }
                     } else {
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
-                            if (n0 + i < p.N) dst[i] = __float2bfloat16_rn(f[i]);
+                            if (n0 + i < p.N) {
+                                const __nv_bfloat16 h = __float2bfloat16_rn(f[i]);
+                                dst[i] = h;
+                                if (fold)
+                                    ofp += (uint32_t)__bfloat16_as_ushort(h) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                            }
                     }
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->tmem_empty);
+            if (fold) {
+                const int seg = nt * 2 + half;
+                check_segment(p.chk, row_ok && seg * (BN / 2) < p.N,
+                              (uint64_t)m * (uint64_t)((p.N + BN / 2 - 1) / (BN / 2)) + (uint64_t)seg, ofp);
+            }
         }
     }
 
@@ -342,7 +363,7 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 
 template <int OUT>
 static int launch(const void* A, const void* SFA, const void* B, const void* SFB, float gab, void* C, int M, int N,
-                  int K, cudaStream_t stream) {
+                  int K, cudaStream_t stream, const LaunchCheck& chk) {
     DeviceInfo* info = nullptr;
     int rc = current_device_info(&info);
     if (rc) return rc;
@@ -363,7 +384,8 @@ static int launch(const void* A, const void* SFA, const void* B, const void* SFB
         QG_CUDA(cudaFuncSetAttribute(gemm_nvfp4_kernel<QG_OUT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         attr_set[dev & 63] = true;
     }
-    Params p{M, N, K, static_cast<const uint8_t*>(SFA), static_cast<const uint8_t*>(SFB), gab, C, status, group_rows(K)};
+    Params p{M, N, K, static_cast<const uint8_t*>(SFA), static_cast<const uint8_t*>(SFB), gab, C, status, group_rows(K),
+             chk};
     const int tiles = ceil_div(M, BM) * ceil_div(N, BN);
     const int grid = tiles < info->sm_count ? tiles : info->sm_count;
     gemm_nvfp4_kernel<OUT><<<grid, THREADS, SMEM_BYTES, stream>>>(tmA, tmB, p);
@@ -375,16 +397,18 @@ static int launch(const void* A, const void* SFA, const void* B, const void* SFB
 
 uint64_t nvfp4_sf_bytes(int R, int K) { return (uint64_t)((R + 127) / 128) * (uint64_t)(K / 64) * 512; }
 
+uint64_t gemm_nvfp4_check_slots(int M, int N) { return (uint64_t)M * (uint64_t)((N + f4::BN / 2 - 1) / (f4::BN / 2)); }
+
 int gemm_nvfp4(const void* A, const void* SFA, const void* B, const void* SFB, float ga, float gb, void* C,
-               int out_type, int M, int N, int K, cudaStream_t stream) {
+               int out_type, int M, int N, int K, cudaStream_t stream, const LaunchCheck& chk) {
     QG_CHECK_ARG(A && SFA && B && SFB && C, "qg_gemm_nvfp4: null operand");
     QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemm_nvfp4: empty shape %dx%dx%d", M, N, K);
     QG_CHECK_ARG(K % 256 == 0, "qg_gemm_nvfp4: K=%d must be a multiple of 256", K);
     QG_CHECK_ARG(((uintptr_t)SFA & 15) == 0 && ((uintptr_t)SFB & 15) == 0, "qg_gemm_nvfp4: scale tensors must be 16-byte aligned");
     const float gab = ga * gb;
     switch (out_type) {
-        case QG_OUT_BF16: return f4::launch<QG_OUT_BF16>(A, SFA, B, SFB, gab, C, M, N, K, stream);
-        case QG_OUT_F32: return f4::launch<QG_OUT_F32>(A, SFA, B, SFB, gab, C, M, N, K, stream);
+        case QG_OUT_BF16: return f4::launch<QG_OUT_BF16>(A, SFA, B, SFB, gab, C, M, N, K, stream, chk);
+        case QG_OUT_F32: return f4::launch<QG_OUT_F32>(A, SFA, B, SFB, gab, C, M, N, K, stream, chk);
         default: set_error("qg_gemm_nvfp4: bad out_type %d", out_type); return QG_ERR_ARG;
     }
 }
@@ -393,7 +417,8 @@ int gemm_nvfp4(const void* A, const void* SFA, const void* B, const void* SFB, f
 
 extern "C" int qg_gemm_nvfp4(const void* A, const void* SFA, const void* B, const void* SFB, float ga, float gb,
                              void* C, int out_type, int M, int N, int K, void* stream) {
-    return qg::gemm_nvfp4(A, SFA, B, SFB, ga, gb, C, out_type, M, N, K, static_cast<cudaStream_t>(stream));
+    return qg::gemm_nvfp4(A, SFA, B, SFB, ga, gb, C, out_type, M, N, K, static_cast<cudaStream_t>(stream),
+                          qg::LaunchCheck{});
 }
 
 extern "C" int qg_nvfp4_sf_bytes(int rows, int K, uint64_t* bytes) {

@@ -43,8 +43,11 @@ uint64_t gemv_w4a16_tc_xprep_bytes(int K);
 
 // One call for `mrows` (1..16) activation rows (two launches: the X pre-pass,
 // then the GEMV); `partials`, `tickets` and `xprep` come from the caller's
-// workspace, tickets zero on entry (and on return).
+// workspace, tickets zero on entry (and on return).  With `golden` set, the
+// writer of each output element compares it with the same element of `golden`
+// and counts the differences into `check_count`.
 int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
-                  int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream);
+                  int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream,
+                  const void* golden = nullptr, unsigned long long* check_count = nullptr);
 
 } // namespace qg

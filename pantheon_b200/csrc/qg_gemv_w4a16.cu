@@ -35,6 +35,7 @@
 // llm_decode.cpp:28-46, a KV gather + FMA chain with no weights) is the decode
 // workload; this kernel is the weight-only quantized projection it is named for.
 #include "qg_common.cuh"
+#include "qg_check.cuh"
 #include "qg_gemv.cuh"
 
 #include <cuda_bf16.h>
@@ -70,6 +71,8 @@ struct Params {
     int splits;
     int out_type;
     int early_w;             // QG_GEMV_WEIGHTS_CONST: first weight loads before the dependency wait
+    const void* golden;      // per-launch check: the golden Y (same layout), or null
+    unsigned long long* check_count;   // differing output words found
 };
 
 __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
@@ -292,16 +295,29 @@ gemv_w4a16_kernel(Params p) {
         }
     }
 
-    // ---- publish: directly when K is not split, else partial + ticket
+    // ---- publish: directly when K is not split, else partial + ticket.  In a
+    // checked launch the writer compares each stored word with the golden output
+    // (qg_check.cuh) and `bad` counts the differing words of this thread.
+    uint32_t bad = 0;
     auto store_row = [&](int m, const float* v) {
         if (p.out_type == QG_OUT_F32) {
             float* dst = static_cast<float*>(p.Y) + (size_t)m * p.N + n0;
             *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+            if (p.golden) {
+                const uint4 g = __ldcg(reinterpret_cast<const uint4*>(static_cast<const float*>(p.golden) + (size_t)m * p.N + n0));
+                bad += (g.x != __float_as_uint(v[0])) + (g.y != __float_as_uint(v[1])) + (g.z != __float_as_uint(v[2])) +
+                       (g.w != __float_as_uint(v[3]));
+            }
         } else {
             __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.Y) + (size_t)m * p.N + n0;
             __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
             __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
-            *reinterpret_cast<uint2*>(dst) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+            const uint32_t wa0 = *reinterpret_cast<uint32_t*>(&a), wb0 = *reinterpret_cast<uint32_t*>(&b);
+            *reinterpret_cast<uint2*>(dst) = make_uint2(wa0, wb0);
+            if (p.golden) {
+                const uint2 g = __ldcg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.golden) + (size_t)m * p.N + n0));
+                bad += (g.x != wa0) + (g.y != wb0);
+            }
         }
     };
     if (p.splits == 1) {
@@ -309,6 +325,7 @@ gemv_w4a16_kernel(Params p) {
 #pragma unroll
             for (int m = 0; m < MT; ++m)
                 if (m < p.M) store_row(m, y[m]);
+        if (p.golden) check_count_warp(p.check_count, bad);
         return;
     }
     if (active) {
@@ -336,6 +353,7 @@ gemv_w4a16_kernel(Params p) {
             store_row(m, s);
         }
     }
+    if (p.golden) check_count_warp(p.check_count, bad);
     if (threadIdx.x == 0) p.tickets[blockIdx.x] = 0;   // ready for the next call
 }
 
@@ -406,7 +424,8 @@ uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int /*sm_count*/) {
 }
 
 int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,
-               void* workspace, uint64_t workspace_bytes, cudaStream_t stream, unsigned int flags) {
+               void* workspace, uint64_t workspace_bytes, cudaStream_t stream, unsigned int flags,
+               const LaunchCheck& chk) {
     QG_CHECK_ARG(X && W && S && Z && Y, "qg_gemv_w4a16: null operand");
     QG_CHECK_ARG((flags & ~(unsigned int)QG_GEMV_WEIGHTS_CONST) == 0, "qg_gemv_w4a16: unknown flags 0x%x", flags);
     QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemv_w4a16: empty shape %dx%dx%d", M, N, K);
@@ -428,11 +447,14 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
     const uint64_t xprep_off = tickets_off - xprep_bytes(M, K);
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mrows = (M - m0) < w4::MAX_M ? (M - m0) : w4::MAX_M;
+        const size_t y_off = (size_t)m0 * N * (out_type == QG_OUT_F32 ? 4 : 2);
+        const void* golden = chk.expect ? reinterpret_cast<const uint8_t*>(chk.expect) + y_off : nullptr;
         if (mrows >= kTensorMinRows) {
             rc = gemv_w4a16_tc(static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K, W, S, Z,
-                               static_cast<uint8_t*>(Y) + (size_t)m0 * N * (out_type == QG_OUT_F32 ? 4 : 2), out_type,
+                               static_cast<uint8_t*>(Y) + y_off, out_type,
                                mrows, N, K, reinterpret_cast<float*>(ws),
-                               reinterpret_cast<unsigned int*>(ws + tickets_off), ws + xprep_off, stream);
+                               reinterpret_cast<unsigned int*>(ws + tickets_off), ws + xprep_off, stream,
+                               golden, chk.count);
             if (rc) return rc;
             continue;
         }
@@ -452,6 +474,8 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         p.splits = splits;
         p.out_type = out_type;
         p.early_w = (flags & QG_GEMV_WEIGHTS_CONST) ? 1 : 0;
+        p.golden = golden;
+        p.check_count = chk.count;
         const size_t smem = w4::smem_bytes(mt, K, splits);
         QG_CHECK_ARG(smem <= 200 * 1024, "qg_gemv_w4a16: K slice too large for shared memory");
         dim3 grid(w4::col_blocks_for(mt, N), splits);
@@ -483,14 +507,14 @@ extern "C" int qg_gemv_w4a16_workspace_bytes(int M, int N, int K, uint64_t* byte
 extern "C" int qg_gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M,
                              int N, int K, void* workspace, uint64_t workspace_bytes, void* stream) {
     return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, workspace, workspace_bytes,
-                          static_cast<cudaStream_t>(stream), 0u);
+                          static_cast<cudaStream_t>(stream), 0u, qg::LaunchCheck{});
 }
 
 extern "C" int qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type,
                                 int M, int N, int K, void* workspace, uint64_t workspace_bytes, unsigned int flags,
                                 void* stream) {
     return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, workspace, workspace_bytes,
-                          static_cast<cudaStream_t>(stream), flags);
+                          static_cast<cudaStream_t>(stream), flags, qg::LaunchCheck{});
 }
 
 // ---------------------------------------------------------------------------
@@ -558,5 +582,5 @@ extern "C" int qg_gemv_w4a16_noalloc(const void* X, const void* W, const void* S
     // The array keeps whatever the previous call (of any shape) left in it,
     // and the tickets must start at zero: clear this call's part first.
     QG_CUDA(cudaMemsetAsync(scratch, 0, (size_t)need, s));
-    return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, scratch, kNoAllocScratchBytes, s, 0u);
+    return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, scratch, kNoAllocScratchBytes, s, 0u, qg::LaunchCheck{});
 }

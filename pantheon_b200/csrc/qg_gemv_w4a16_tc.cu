@@ -73,6 +73,7 @@
 // K/128) load as zeros and carry zero scales, so they add nothing.
 // All barrier waits are bounded (qg_ptx.cuh).
 #include "qg_common.cuh"
+#include "qg_check.cuh"
 #include "qg_gemv.cuh"
 
 #include <cuda_bf16.h>
@@ -191,6 +192,8 @@ struct Params {
     int maxp;                // most CTAs sharing one tile
     int out_type;
     DeviceStatus* status;
+    const void* golden;                  // per-launch check: the golden Y, or null
+    unsigned long long* check_count;     // differing output elements found
 };
 
 // The CTA whose unit range [c*U/C, (c+1)*U/C) holds unit u.
@@ -400,14 +403,26 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
             const long long gu = (long long)t * p.upt;
             const int first = owner(gu, p.units, ctas);
             const int np = owner(gu + p.upt - 1, p.units, ctas) - first + 1;
+            // every lane of the warp calls store (n past N stores nothing); in a
+            // checked launch each stored element is compared with the golden one
             auto store = [&](const float* v) {
-                if (n >= p.N) return;
+                uint32_t bad = 0;
+                if (n < p.N) {
 #pragma unroll
-                for (int m = 0; m < T::MROWS; ++m) {
-                    if (m >= p.M) break;
-                    if (p.out_type == QG_OUT_F32) static_cast<float*>(p.Y)[(size_t)m * p.N + n] = v[m];
-                    else static_cast<__nv_bfloat16*>(p.Y)[(size_t)m * p.N + n] = __float2bfloat16_rn(v[m]);
+                    for (int m = 0; m < T::MROWS; ++m) {
+                        if (m >= p.M) break;
+                        const size_t i = (size_t)m * p.N + n;
+                        if (p.out_type == QG_OUT_F32) {
+                            static_cast<float*>(p.Y)[i] = v[m];
+                            if (p.golden) bad += __ldcg(static_cast<const uint32_t*>(p.golden) + i) != __float_as_uint(v[m]);
+                        } else {
+                            const __nv_bfloat16 h = __float2bfloat16_rn(v[m]);
+                            static_cast<__nv_bfloat16*>(p.Y)[i] = h;
+                            if (p.golden) bad += __ldcg(static_cast<const unsigned short*>(p.golden) + i) != __bfloat16_as_ushort(h);
+                        }
+                    }
                 }
+                if (p.golden) check_count_warp(p.check_count, bad);
             };
             if (np == 1) {
                 store(y);
@@ -680,7 +695,8 @@ uint64_t gemv_w4a16_tc_xprep_bytes(int K) {
 }
 
 int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
-                  int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream) {
+                  int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream, const void* golden,
+                  unsigned long long* check_count) {
     QG_CHECK_ARG(mrows >= 1 && mrows <= w4tc::MAX_MROWS, "gemv_w4a16_tc: %d rows (1..16)", mrows);
     DeviceStatus* status = nullptr;
     int rc = device_status_ptr(&status);
@@ -717,6 +733,8 @@ int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, vo
     p.maxp = s.maxp;
     p.out_type = out_type;
     p.status = status;
+    p.golden = golden;
+    p.check_count = check_count;
     // 8-row tiles for up to 8 rows: half the X traffic and fold work of 16-row ones
     const __nv_bfloat16* Xb = static_cast<const __nv_bfloat16*>(X);
     uint8_t* xp = static_cast<uint8_t*>(xprep);

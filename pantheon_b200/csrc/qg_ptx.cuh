@@ -18,9 +18,12 @@ namespace qg {
 constexpr uint64_t QG_WAIT_LIMIT_NS = 2000000000ull;
 
 // Device-wide error word: 0 = ok; otherwise (kernel id << 16) | site.
+// `drained` counts CTAs that gave up after an expired wait, let their copies
+// and MMAs in flight land, freed their TMEM and returned.
 struct DeviceStatus {
     unsigned int code;
     unsigned int count;
+    unsigned int drained;
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -63,11 +66,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with parity `parity` to complete.  Returns false
-// (after recording `site` in `status` and raising `*abort`) on timeout, or at
-// once when another role already raised `*abort`.  `abort` and `status` may be
-// null (the drain waits of an aborting kernel use neither).
+// (after recording `site` in `status` and raising `*abort`) after `limit_ns`,
+// or at once when another role already raised `*abort`.  `abort` and `status`
+// may be null (the drain waits of an aborting kernel use neither).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          DeviceStatus* status, uint32_t site) {
+                                          DeviceStatus* status, uint32_t site,
+                                          uint64_t limit_ns = QG_WAIT_LIMIT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = globaltimer_ns();
     uint32_t spins = 0;
@@ -75,7 +79,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         if (mbar_try_wait(bar, parity)) return true;
         if ((++spins & 63u) == 0) {
             if (abort && *abort) return false;
-            if (globaltimer_ns() - t0 > QG_WAIT_LIMIT_NS) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 if (abort) *abort = 1;
                 if (status) {
                     atomicCAS(&status->code, 0u, site);

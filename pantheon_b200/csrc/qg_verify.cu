@@ -53,6 +53,8 @@ __global__ void verify_words_kernel(const uint32_t* __restrict__ actual, const u
 
 __global__ void flip_bit_kernel(uint32_t* word) { word[0] ^= 0x00000080u; }
 
+__global__ void flip_bit_at_kernel(uint8_t* base, uint64_t byte, uint32_t bit) { base[byte] ^= (uint8_t)(1u << bit); }
+
 } // namespace ver
 
 int verify_words(const void* actual, const void* expected, uint64_t nwords, void* counters, void* log, int log_cap,
@@ -77,6 +79,12 @@ int verify_words(const void* actual, const void* expected, uint64_t nwords, void
 
 int flip_bit(void* word, cudaStream_t s) {
     ver::flip_bit_kernel<<<1, 1, 0, s>>>(static_cast<uint32_t*>(word));
+    QG_CUDA(cudaGetLastError());
+    return QG_OK;
+}
+
+int flip_bit_at(void* base, uint64_t byte, int bit, cudaStream_t s) {
+    ver::flip_bit_at_kernel<<<1, 1, 0, s>>>(static_cast<uint8_t*>(base), byte, (uint32_t)bit);
     QG_CUDA(cudaGetLastError());
     return QG_OK;
 }

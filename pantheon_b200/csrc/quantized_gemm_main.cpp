@@ -286,6 +286,11 @@ void print_faults(qg_ctx* ctx) {
     for (int i = 0; i < nlog; ++i)
         printf("[SDC FAULT][%s] Output mismatch! Word: %llu | Exp: 0x%08x | Act: 0x%08x | XOR: 0x%08x\n", kFaultTag,
                (unsigned long long)log[i].index, log[i].expected, log[i].actual, log[i].expected ^ log[i].actual);
+    // differences the launches of the batch found in their own results (qg_run's per-launch check)
+    uint64_t words = 0, diffs = 0, launches = 0;
+    if (qg_verify_detail(ctx, &words, &diffs, &launches) == QG_OK && diffs)
+        printf("[SDC FAULT][%s] Per-launch check: %llu result segments differed from the golden run in a batch of "
+               "%llu checked launches\n", kFaultTag, (unsigned long long)diffs, (unsigned long long)launches);
     fflush(stdout);
 }
 
@@ -474,7 +479,7 @@ int main(int argc, char* argv[]) {
 
     uint64_t mismatches = 0;
     double busy = 0.0;
-    uint64_t launches = 0;
+    uint64_t launches = 0, checked = 0;
     auto start = std::chrono::high_resolution_clock::now();
     do {
         auto b0 = std::chrono::high_resolution_clock::now();
@@ -494,6 +499,8 @@ int main(int argc, char* argv[]) {
             }
             if (mm) print_faults(ctx);
             mismatches += mm;
+            uint64_t w = 0, d = 0, n = 0;
+            if (qg_verify_detail(ctx, &w, &d, &n) == QG_OK) checked += n;
         }
     } while (std::chrono::duration_cast<std::chrono::seconds>(std::chrono::high_resolution_clock::now() - start).count() <
              o.duration);
@@ -515,6 +522,8 @@ int main(int argc, char* argv[]) {
             print_faults(ctx);
             mismatches += mm;
         }
+        std::cout << "  -> Launches Checked: " << checked << " of " << launches
+                  << " (each launch checks its own result against the golden run)" << std::endl;
         std::cout << "  -> Mismatches:    " << mismatches << std::endl;
         std::cout << "Verification: " << (mismatches ? "FAIL" : "PASS") << " (" << mismatches
                   << (kFurnace ? " errors)" : " mismatches)") << std::endl;

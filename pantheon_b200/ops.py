@@ -336,6 +336,18 @@ class Workload:
         self._check("qg_verify", self.lib.qg_verify(self.ctx, C.byref(mm)))
         return mm.value
 
+    def verify_detail(self):
+        """(differing words of the last qg_verify's final compare, differences the per-launch
+        checks found, launches that ran with a check) -- the parts of the last verify()."""
+        w, d, n = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        self._check("qg_verify_detail", self.lib.qg_verify_detail(self.ctx, C.byref(w), C.byref(d), C.byref(n)))
+        return w.value, d.value, n.value
+
+    def flip_operand_bit(self, copy: int, slot: int, byte: int, bit: int, stream=None):
+        """Flip one bit of an operand of copy `copy` on `stream` (a second flip restores it)."""
+        s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)
+        self._check("qg_flip_operand_bit", self.lib.qg_flip_operand_bit(self.ctx, copy, slot, byte, bit, s))
+
     def mismatch_log(self, cap: int = 16):
         arr = (QGMismatch * cap)()
         n = self.lib.qg_mismatch_log(self.ctx, arr, cap)

@@ -82,8 +82,9 @@ def test_library_rejects_bad_shapes_before_touching_a_device(qglib):
     assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == pb._lib.QG_ERR_ARG
     cfg = pb._lib.QGCfg(pb.QG_FMT_INT8, 8192, 8192, 8192, 0, 1, 0)
     assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == 0
-    # A, B, sa, sb, C and golden (bf16), row checksums and golden checksums
-    assert b.value == 8192 * 8192 * 2 + 8 * 8192 + 2 * 8192 * 8192 * 2 + 2 * 4 * 8192 + 4096
+    # A, B, sa, sb, C and golden (bf16), row checksums and golden checksums, and the
+    # per-launch check's fingerprints (one uint32 per row and 256-column tile)
+    assert b.value == (8192 * 8192 * 2 + 8 * 8192 + 2 * 8192 * 8192 * 2 + 2 * 4 * 8192 + 4 * 8192 * 32 + 4096)
 
 
 @pytest.mark.parametrize("gemm_type, why", [("int4", "Unknown --gemm_type"), ("fp64", "Unknown --gemm_type")])
@@ -129,13 +130,18 @@ def test_dense_formats_size_and_validate(qglib):
     import ctypes as C
     import pantheon_b200 as pb
     b = C.c_uint64()
-    # A, B (bf16) and C, golden (bf16) at the 8192^3 default
+    # A, B (bf16) and C, golden (bf16) at the 8192^3 default, plus the per-launch
+    # check's fingerprints (one uint32 per row and 256-column tile)
     cfg = pb._lib.QGCfg(pb.QG_FMT_BF16, 0, 0, 0, pb.QG_OUT_BF16, 1, 0)
     assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == 0
-    assert b.value == 4 * 8192 * 8192 * 2 + 4096
+    assert b.value == 4 * 8192 * 8192 * 2 + 4 * 8192 * 32 + 4096
     cfg = pb._lib.QGCfg(pb.QG_FMT_TF32, 256, 256, 256, pb.QG_OUT_F32, 2, 0)
     assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == 0
-    assert b.value == 2 * (2 * 256 * 256 * 4 + 2 * 256 * 256 * 4) + 4096
+    assert b.value == 2 * (2 * 256 * 256 * 4 + 2 * 256 * 256 * 4 + 4 * 256) + 4096
+    # the fp32 CUDA-core GEMM has no per-launch check
+    cfg = pb._lib.QGCfg(pb.QG_FMT_FP32, 256, 256, 256, pb.QG_OUT_F32, 1, 0)
+    assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == 0
+    assert b.value == 2 * 256 * 256 * 4 + 2 * 256 * 256 * 4 + 4096
     cfg = pb._lib.QGCfg(pb.QG_FMT_FP16, 256, 256, 100, pb.QG_OUT_F16, 1, 0)   # 200-byte rows
     assert qglib.qg_required_bytes(C.byref(cfg), C.byref(b)) == pb._lib.QG_ERR_ARG
     cfg = pb._lib.QGCfg(pb.QG_FMT_E4M3, 256, 256, 256, pb.QG_OUT_S32, 1, 0)   # no integer output
