@@ -305,8 +305,9 @@ QG_API int  qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, const 
  * that loads the library holds until the process exits; shapes whose
  * workspace (qg_gemv_w4a16_workspace_bytes) exceeds 16 MiB are rejected with
  * QG_ERR_ARG (configs[3], M <= 16, K = 8192, N = 28672, fits).  The call
- * allocates nothing; it clears the part of the array it uses on `stream`
- * before the kernel runs.  All calls share the one array per device, so calls
+ * allocates nothing; before the kernel runs it zeroes, on `stream`, the few
+ * bytes of split-K tickets that must start at zero (everything else in the
+ * array is written by the call before the call reads it).  All calls share the one array per device, so calls
  * that overlap on the GPU (other streams, other threads) race: serialise them.
  * The first call on a device looks up the array's device address; make that
  * first call before any stream capture. */

@@ -579,8 +579,12 @@ extern "C" int qg_gemv_w4a16_noalloc(const void* X, const void* W, const void* S
     int rc = qg::w4::noalloc_scratch(&scratch);
     if (rc) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // The array keeps whatever the previous call (of any shape) left in it,
-    // and the tickets must start at zero: clear this call's part first.
-    QG_CUDA(cudaMemsetAsync(scratch, 0, (size_t)need, s));
+    // The array keeps whatever the previous call (of any shape) left in it.
+    // Only the tickets must start at zero: every split-K partial and every
+    // prepared activation tile is written by this call before this call reads
+    // it.  The tickets sit at the end of this shape's part of the array, where a
+    // call of another shape may have left partial sums, so clear just them.
+    const uint64_t tickets = qg::ticket_bytes(N);
+    QG_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(scratch) + (need - tickets), 0, (size_t)tickets, s));
     return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, scratch, kNoAllocScratchBytes, s, 0u, qg::LaunchCheck{});
 }

@@ -8,8 +8,10 @@ caller-provided workspace.
 
 The test calls it through the C ABI, twice in a row, and checks each output
 against the existing entry point (qg_gemv_w4a16 with its own workspace)
-within the tolerance the other GEMV tests use; it also checks that a shape
-whose scratch would exceed the built-in maximum is rejected.  This file is
+within the tolerance the other GEMV tests use; then a sequence of calls of
+different shapes, bf16 and fp32 out, each against the workspace entry point
+bit for bit; and that a shape whose scratch would exceed the built-in maximum
+is rejected.  This file is
 collected last, so a failure here comes after every other test has run; it
 passes on its own in a fresh process as well as after the rest of the suite.
 """
@@ -47,6 +49,25 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_device, oracle, qglib,
         assert rc == 0, pb._lib.last_error()
         torch.cuda.synchronize()
         assert oracle.max_rel_err(_bf16_bits(y), _bf16_bits(ref), 0) < RTOL
+
+
+@pytest.mark.parametrize("out_type", [pb.QG_OUT_BF16, pb.QG_OUT_F32])
+def test_noalloc_after_calls_of_other_shapes(cuda_device, qglib, out_type):
+    """Each call starts from what the previous call, of another shape, left in the shared
+    scratch: partial sums where this call keeps its tickets.  A sequence of shapes
+    (both GEMV kernels, 1 to 24 rows, so also two row chunks) must still give exactly
+    the output of the workspace entry point with a fresh zeroed workspace."""
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for M, N, K in [(16, 28672, 8192), (1, 4096, 2048), (8, 28672, 8192), (24, 4096, 4096), (2, 28672, 8192),
+                    (16, 28672, 8192)]:
+        X, W, S, Z = pb.gen_w4a16(M, N, K, seed=100 + M + N)
+        ref = pb.gemv_w4a16(X, W, S, Z, out_type=out_type)
+        y = torch.full_like(ref, float("nan"))
+        rc = qglib.qg_gemv_w4a16_noalloc(_ptr(X), _ptr(W), _ptr(S), _ptr(Z), _ptr(y), out_type, M, N, K, stream)
+        assert rc == 0, pb._lib.last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(y.view(torch.int16 if out_type == pb.QG_OUT_BF16 else torch.int32),
+                           ref.view(torch.int16 if out_type == pb.QG_OUT_BF16 else torch.int32)), (M, N, K)
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(cuda_device, qglib):
