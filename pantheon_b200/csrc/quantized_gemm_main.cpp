@@ -473,11 +473,19 @@ int main(int argc, char* argv[]) {
             loops = capped;
         }
     }
+    uint64_t mismatches = 0;
+    if (o.verify) {
+        // the warm-up launches checked themselves too: collect what they found
+        // before the timed batches, so every batch below reports its own launches
+        uint64_t mm = 0;
+        if (qg_verify(ctx, &mm) != QG_OK) return fail_ctx(ctx, "qg_verify");
+        if (mm) print_faults(ctx);
+        mismatches += mm;
+    }
     std::cout << "  -> Kernel Loops:  " << loops << std::endl;
     if (o.inject) std::cout << "[PANTHEON] Warning: SDC Fault Injection is ACTIVE!" << std::endl;
     std::cout << "[PANTHEON] Starting active telemetry phase..." << std::endl;
 
-    uint64_t mismatches = 0;
     double busy = 0.0;
     uint64_t launches = 0, checked = 0;
     auto start = std::chrono::high_resolution_clock::now();
