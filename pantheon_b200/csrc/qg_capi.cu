@@ -65,18 +65,15 @@ void free_ctx_memory(qg_ctx* c) {
 }
 
 // The per-launch check of a timed launch of copy `cp` (qg_check.cuh): GEMMs
-// compare their row-segment fingerprints with the golden launch's, the GEMV
-// compares its output words with the golden output.  Nothing before qg_golden.
+// and the tensor-core GEMV compare their fingerprints with the golden launch's,
+// the CUDA-core GEMV compares its output words with the golden output.
+// Nothing before qg_golden.
 qg::LaunchCheck run_check(const qg_ctx* c, const qg::CopyBuffers& cp) {
     qg::LaunchCheck k;
-    if (!c->golden_ready) return k;
-    if (c->layout.check_bytes) {
-        k.expect = static_cast<const uint32_t*>(cp.check_fp);
-        k.count = c->launch_diffs;
-    } else if (c->cfg.format == QG_FMT_W4A16) {
-        k.expect = static_cast<const uint32_t*>(cp.golden);
-        k.count = c->launch_diffs;
-    }
+    if (!c->golden_ready || !c->layout.check_bytes) return k;
+    k.expect = static_cast<const uint32_t*>(cp.check_fp);
+    k.count = c->launch_diffs;
+    if (c->cfg.format == QG_FMT_W4A16) k.golden = cp.golden;
     return k;
 }
 

@@ -12,11 +12,16 @@
 //           rounds away in bf16 still shows -- and, in the golden launch,
 //           records it; in every later launch it compares it with the recorded
 //           one;
-//   GEMV    the writer of each output compares it with the golden output word
-//           for word (the output is at most a few MB).
+//   GEMV    the CUDA-core kernel (1-2 rows) compares each output word it writes
+//           with the golden output; the tensor-core kernel (3-16 rows) folds
+//           the words of each output column into a fingerprint, recorded by
+//           the golden launch and compared by later launches, with the
+//           expected value loaded when the column's tile starts (a compare at
+//           the end would put a memory round trip per row on the fold's path).
 // Differences are counted with one atomic per warp (ballot + popc).  The
-// fingerprint is a sum of word * odd weight mod 2^32, so any change of a
-// single word always changes it.
+// fingerprint folds the words in a fixed order, fp = fp * kCheckMul + word
+// (mod 2^32, one multiply-add per word): word i enters multiplied by an odd
+// power of kCheckMul, so a change of any single word always changes it.
 #pragma once
 
 #include <cstdint>
@@ -25,14 +30,13 @@ namespace qg {
 
 struct LaunchCheck {
     uint32_t* record = nullptr;             // golden launch: fingerprints written here
-    const uint32_t* expect = nullptr;       // checked launch: fingerprints (GEMM) or golden words (GEMV)
+    const uint32_t* expect = nullptr;       // checked launch: fingerprints recorded by the golden launch
     unsigned long long* count = nullptr;    // checked launch: differences found
+    const void* golden = nullptr;           // checked GEMV launch: the golden output (CUDA-core kernel)
 };
 
-// Odd weight of word j of row m (odd: multiplication by it is invertible mod 2^32).
-__host__ __device__ __forceinline__ uint32_t check_weight(uint32_t m, uint32_t j) {
-    return ((m * 0x9E3779B1u) ^ (j * 0x85EBCA77u)) | 1u;
-}
+// Odd multiplier of the fold (odd: multiplication by it is invertible mod 2^32).
+constexpr uint32_t kCheckMul = 0x9E3779B1u;
 
 // Record or compare the fingerprint of segment `idx` (only where `valid`).  Every
 // lane of the warp calls it with the same `c`; at most one atomic per warp.

@@ -93,6 +93,8 @@ int layout_for(const qg_cfg& cfg, Layout* L) {
             l.op_bytes[3] = (uint64_t)l.K / 128 * l.N * 2;     // Z fp16
             l.out_bytes = (uint64_t)l.M * l.N * out_elem_bytes(l.out_type);
             l.scratch_bytes = gemv_w4a16_workspace_bytes(l.M, l.N, l.K, 148);
+            // per-launch check of the tensor-core chunks: one fingerprint per (16-row chunk, column)
+            l.check_bytes = 4ull * (uint64_t)((l.M + 15) / 16) * (uint64_t)l.N;
             l.ops = 2.0 * l.M * (double)l.N * l.K;
             l.bytes = (double)(l.op_bytes[0] + l.op_bytes[1] + l.op_bytes[2] + l.op_bytes[3] + l.out_bytes);
             break;

@@ -251,7 +251,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 #pragma unroll
                         for (int i = 0; i < COLS_PER_EPI; ++i)
                             if (full_seg || n0 + i < p.N)
-                                ofp += __float_as_uint(acc[i]) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                                ofp = ofp * kCheckMul + __float_as_uint(acc[i]);
                     }
                 } else {
                     __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
@@ -263,7 +263,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                             for (int j = 0; j < 4; ++j) {
                                 __nv_bfloat162 h = __floats2bfloat162_rn(acc[i + 2 * j], acc[i + 2 * j + 1]);
                                 w[j] = *reinterpret_cast<uint32_t*>(&h);
-                                if (fold) ofp += w[j] * check_weight((uint32_t)m, (uint32_t)(n0 + i + 2 * j));
+                                if (fold) ofp = ofp * kCheckMul + w[j];
                             }
                             *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
                         }
@@ -274,7 +274,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                 const __nv_bfloat16 h = __float2bfloat16_rn(acc[i]);
                                 dst[i] = h;
                                 if (fold)
-                                    ofp += (uint32_t)__bfloat16_as_ushort(h) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                                    ofp = ofp * kCheckMul + (uint32_t)__bfloat16_as_ushort(h);
                             }
                     }
                 }

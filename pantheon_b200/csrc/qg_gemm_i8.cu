@@ -168,7 +168,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
         if (fold) {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-                if (full_chunk || n0 + i < p.N) ofp += r[i] * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                if (full_chunk || n0 + i < p.N) ofp = ofp * kCheckMul + r[i];
         }
         return;
     }
@@ -205,7 +205,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
         if (fold) {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-                if (full_chunk || n0 + i < p.N) ofp += __float_as_uint(f[i]) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                if (full_chunk || n0 + i < p.N) ofp = ofp * kCheckMul + __float_as_uint(f[i]);
         }
     } else if (OUT == QG_OUT_F16) {
         __half* dst = static_cast<__half*>(p.C) + (size_t)m * p.N + n0;
@@ -221,7 +221,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
                 *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
             if (fold) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) ofp += w[i] * check_weight((uint32_t)m, (uint32_t)(n0 + 2 * i));
+                for (int i = 0; i < 16; ++i) ofp = ofp * kCheckMul + w[i];
             }
         } else {
 #pragma unroll
@@ -229,7 +229,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
                 if (n0 + i < p.N) {
                     const __half h = __float2half_rn(f[i]);
                     dst[i] = h;
-                    if (fold) ofp += (uint32_t)__half_as_ushort(h) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                    if (fold) ofp = ofp * kCheckMul + (uint32_t)__half_as_ushort(h);
                 }
         }
     } else {
@@ -246,7 +246,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
                 *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
             if (fold) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) ofp += w[i] * check_weight((uint32_t)m, (uint32_t)(n0 + 2 * i));
+                for (int i = 0; i < 16; ++i) ofp = ofp * kCheckMul + w[i];
             }
         } else {
 #pragma unroll
@@ -254,7 +254,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int m, i
                 if (n0 + i < p.N) {
                     const __nv_bfloat16 h = __float2bfloat16_rn(f[i]);
                     dst[i] = h;
-                    if (fold) ofp += (uint32_t)__bfloat16_as_ushort(h) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                    if (fold) ofp = ofp * kCheckMul + (uint32_t)__bfloat16_as_ushort(h);
                 }
         }
     }

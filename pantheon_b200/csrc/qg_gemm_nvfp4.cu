@@ -314,7 +314,7 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             if (full_chunk || n0 + i < p.N)
-                                ofp += __float_as_uint(f[i]) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                                ofp = ofp * kCheckMul + __float_as_uint(f[i]);
                     }
                 } else {
                     __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.C) + (size_t)m * p.N + n0;
@@ -326,7 +326,7 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                             for (int j = 0; j < 4; ++j) {
                                 __nv_bfloat162 h = __floats2bfloat162_rn(f[i + 2 * j], f[i + 2 * j + 1]);
                                 w[j] = *reinterpret_cast<uint32_t*>(&h);
-                                if (fold) ofp += w[j] * check_weight((uint32_t)m, (uint32_t)(n0 + i + 2 * j));
+                                if (fold) ofp = ofp * kCheckMul + w[j];
                             }
                             *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
                         }
@@ -337,7 +337,7 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                                 const __nv_bfloat16 h = __float2bfloat16_rn(f[i]);
                                 dst[i] = h;
                                 if (fold)
-                                    ofp += (uint32_t)__bfloat16_as_ushort(h) * check_weight((uint32_t)m, (uint32_t)(n0 + i));
+                                    ofp = ofp * kCheckMul + (uint32_t)__bfloat16_as_ushort(h);
                             }
                     }
                 }

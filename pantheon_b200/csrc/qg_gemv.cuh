@@ -43,11 +43,13 @@ uint64_t gemv_w4a16_tc_xprep_bytes(int K);
 
 // One call for `mrows` (1..16) activation rows (two launches: the X pre-pass,
 // then the GEMV); `partials`, `tickets` and `xprep` come from the caller's
-// workspace, tickets zero on entry (and on return).  With `golden` set, the
-// writer of each output element compares it with the same element of `golden`
-// and counts the differences into `check_count`.
+// workspace, tickets zero on entry (and on return).  Per-launch check
+// (qg_check.cuh): with `fp_record` the writer of each output column stores the
+// column's fingerprint (N entries); with `fp_expect` it compares it with the
+// recorded one and counts differing columns into `check_count`.
 int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
                   int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream,
-                  const void* golden = nullptr, unsigned long long* check_count = nullptr);
+                  uint32_t* fp_record = nullptr, const uint32_t* fp_expect = nullptr,
+                  unsigned long long* check_count = nullptr);
 
 } // namespace qg

@@ -448,13 +448,15 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mrows = (M - m0) < w4::MAX_M ? (M - m0) : w4::MAX_M;
         const size_t y_off = (size_t)m0 * N * (out_type == QG_OUT_F32 ? 4 : 2);
-        const void* golden = chk.expect ? reinterpret_cast<const uint8_t*>(chk.expect) + y_off : nullptr;
+        const void* golden = chk.golden ? static_cast<const uint8_t*>(chk.golden) + y_off : nullptr;
+        const size_t fp_off = (size_t)(m0 / w4::MAX_M) * N;   // per-column fingerprints of this row chunk
         if (mrows >= kTensorMinRows) {
             rc = gemv_w4a16_tc(static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K, W, S, Z,
                                static_cast<uint8_t*>(Y) + y_off, out_type,
                                mrows, N, K, reinterpret_cast<float*>(ws),
                                reinterpret_cast<unsigned int*>(ws + tickets_off), ws + xprep_off, stream,
-                               golden, chk.count);
+                               chk.record ? chk.record + fp_off : nullptr, chk.expect ? chk.expect + fp_off : nullptr,
+                               chk.count);
             if (rc) return rc;
             continue;
         }
