@@ -1,5 +1,15 @@
 """The drop-in boundary held to the reference runner itself (no GPU).
 
+* Real outputs of the three binaries on a B200 (tests/golden/binary_runs.json)
+  go through the runner's own parse_kernel_output and assess_gpu
+  (pantheon.py:3421-3513, 1303-1460): a clean --verify run is a PASS with the
+  workload's unit, an --inject_error run is a FAIL, and the GPU verdict is
+  WATCH with the runner as shipped and FAULT once pantheon_b200.runner_hook is
+  installed (pantheon.py:1220-1223 decides which failures are faults).
+* The restated reader the GPU tests use (tests/contract_parse.py) agrees with
+  the runner's decisions on those outputs, recorded in
+  tests/golden/runner_readings.json by make_runner_readings.py; this part
+  needs no reference tree.
 * pantheon_b200.install_dropin puts the binaries into a build cache that the
   runner's own is_build_cache_current accepts (pantheon.py:2606-2671), so the
   runner uses them instead of rebuilding.
@@ -11,10 +21,19 @@ from pathlib import Path
 
 import pytest
 
-from pantheon_b200 import install_dropin
+from pantheon_b200 import install_dropin, runner_hook
+from tests.contract_parse import parse_kernel_output
 from tests.reference_runner import load_runner
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _runs():
+    return json.loads((GOLDEN / "binary_runs.json").read_text())
+
+
+def _readings():
+    return {r["case"]: r for r in json.loads((GOLDEN / "runner_readings.json").read_text())}
 
 
 @pytest.fixture()
@@ -23,6 +42,68 @@ def runner():
     if mod is None:
         pytest.skip("reference runner (pantheon.py) not found; set PANTHEON_REFERENCE")
     return mod
+
+
+def test_recorded_runs_cover_every_binary_and_outcome():
+    runs = _runs()
+    assert {r["test"] for r in runs} == {"quantized_gemm", "llm_decode", "mma_virus"}
+    for r in runs:
+        clean = "--inject_error" not in r["argv"]
+        assert (r["returncode"] == 0) == clean, r["case"]
+        assert ("Verification: PASS" in r["stdout"]) == (clean and "--verify" in r["argv"]), r["case"]
+
+
+def test_restated_reader_matches_the_runner_on_real_runs():
+    """tests/contract_parse.py reads every recorded run exactly as the runner did."""
+    readings = _readings()
+    for run in _runs():
+        want = readings[run["case"]]
+        score, unit, status, had_error, lines = parse_kernel_output(run["stdout"], run["stderr"],
+                                                                    run["returncode"], run["test"])
+        assert (score, unit, status, had_error) == (want["score"], want["unit"], want["status"],
+                                                     want["had_error"]), run["case"]
+        assert lines == want["kept_lines"], run["case"]
+        assert runner_hook.row_fields(run["test"], run["stdout"]).get(runner_hook.ROW_FIELD) == want["sdc_mismatches"]
+
+
+def test_recorded_verdicts():
+    """Clean runs: PASS rows, HEALTHY GPU.  Injected faults: FAIL rows, WATCH as shipped
+    ("did not complete"), FAULT with the hook installed."""
+    units = {"quantized_gemm": {"TOPS", "GB/s"}, "llm_decode": {"GB/s"}, "mma_virus": {"TFLOPS"}}
+    readings = _readings()
+    for run in _runs():
+        r = readings[run["case"]]
+        if run["returncode"] == 0:
+            assert r["status"] == "PASS" and r["unit"] in units[run["test"]] and r["score"] > 0, run["case"]
+            assert r["verdict_shipped"] == r["verdict_with_hook"] == "HEALTHY", run["case"]
+        else:
+            assert r["status"] == "FAIL" and r["unit"] == "ERR", run["case"]
+            assert r["verdict_shipped"] == "WATCH" and r["verdict_with_hook"] == "FAULT", run["case"]
+            assert r["sdc_mismatches"] >= 1
+
+
+def test_runner_reads_real_runs_as_recorded(runner):
+    """The live runner module reproduces the committed readings."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("make_runner_readings", GOLDEN / "make_runner_readings.py")
+    mk = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mk)
+    assert mk.readings(runner, _runs()) == json.loads((GOLDEN / "runner_readings.json").read_text())
+
+
+def test_hook_turns_an_injected_fault_into_a_fault_verdict(runner):
+    run = next(r for r in _runs() if r["case"] == "quantized_gemm_inject")
+    score, unit, status, _, _ = runner.parse_kernel_output(run["stdout"], run["stderr"], run["returncode"],
+                                                           "quantized_gemm")
+    assert status == "FAIL"
+    row = runner.build_result_row("quantized_gemm", 3, 2, 50, score, unit, {}, status=status)
+    assert runner.assess_gpu([row], 3, "NVIDIA B200")["verdict"] == "WATCH"
+    assert runner_hook.install(runner) == {"quantized_gemm", "llm_decode", "mma_virus"}
+    row.update(runner_hook.row_fields("quantized_gemm", run["stdout"]))
+    verdict = runner.assess_gpu([row], 3, "NVIDIA B200")
+    assert verdict["verdict"] == "FAULT"
+    assert any("quantized_gemm failed" in f for f in verdict["findings"]["faults"])
+    assert row[runner_hook.ROW_FIELD] >= 1
 
 
 def _dropin_env(monkeypatch, tmp_path):
