@@ -294,6 +294,13 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                 __syncwarp();
                 tmem_ld_32x32b_x32(t_row + c, r);
                 tmem_ld_wait_regs(r);
+                if (c + 32 == BN / 2) {
+                    // the tile's last accumulator columns are in registers: the MMA of
+                    // the next tile may overwrite TMEM while this chunk is stored
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->tmem_empty);
+                }
                 const int n0 = nt * BN + half * (BN / 2) + c;
                 if (!row_ok || n0 >= p.N) continue;
                 const bool full_chunk = (n0 + 32 <= p.N);
@@ -342,9 +349,6 @@ gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
                     }
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->tmem_empty);
             if (fold) {
                 const int seg = nt * 2 + half;
                 check_segment(p.chk, row_ok && seg * (BN / 2) < p.N,
