@@ -268,14 +268,14 @@ QG_API int  qg_gemm_nvfp4(const void* A, const void* sfa, const void* B, const v
                           float ga, float gb, void* C, int out_type, int M, int N, int K, void* stream);
 QG_API int  qg_nvfp4_sf_bytes(int rows, int K, uint64_t* bytes);
 
-/* W4A16 group-128 decode GEMV / skinny GEMM (1-2 rows on the CUDA cores,
- * 3-16 rows on the tensor cores, more rows in chunks of 16):
+/* W4A16 group-128 decode GEMV / skinny GEMM (1 row on the CUDA cores, 2-8
+ * rows on warp MMAs, 9-16 rows on tcgen05, more rows in chunks of 16):
  *   Y[m,n] = sum_k X[m,k] * (q[k,n] - Z[k/128,n]) * S[k/128,n],  q = u - 8
  *   X bf16 [M,K]; W uint32 [K/8, N] with nibble j of word (k8, n) = u(8*k8+j, n)
  *   in [0,15]; S, Z fp16 [K/128, N]; Y bf16 or fp32 [M,N] (out_type).
  *   K % 128 == 0, N % 4 == 0; X, W, Y 16-byte and S, Z 8-byte aligned.
  *   `workspace` (qg_gemv_w4a16_workspace_bytes) holds the split-K partials,
- *   the tensor-core path's quantised activations and the per-column-block
+ *   the tcgen05 path's quantised activations and the per-column-block
  *   tickets: it must be zero-filled before its first use, and every call
  *   leaves its tickets zero, ready for the next call (calls sharing one
  *   workspace must not overlap on the GPU).

@@ -65,8 +65,9 @@ void free_ctx_memory(qg_ctx* c) {
 }
 
 // The per-launch check of a timed launch of copy `cp` (qg_check.cuh): GEMMs
-// and the tensor-core GEMV compare their fingerprints with the golden launch's,
-// the CUDA-core GEMV compares its output words with the golden output.
+// and the tcgen05 GEMV compare their fingerprints with the golden launch's,
+// the CUDA-core and warp-MMA GEMVs compare their output words with the golden
+// output.
 // Nothing before qg_golden.
 qg::LaunchCheck run_check(const qg_ctx* c, const qg::CopyBuffers& cp) {
     qg::LaunchCheck k;

@@ -1,6 +1,7 @@
-// qg_gemv.cuh -- what the two W4A16 GEMV kernels share: the SM count their
-// work split is sized for, and the tensor-core kernel's entry (used by the
-// C entry points in qg_gemv_w4a16.cu for 3..16 activation rows).
+// qg_gemv.cuh -- what the three W4A16 GEMV kernels share: the SM count their
+// work split is sized for, and the entries of the tcgen05 kernel (9..16
+// activation rows) and the warp-MMA kernel (2..8 rows), used by the C entry
+// points in qg_gemv_w4a16.cu.
 #pragma once
 
 #include "qg_common.cuh"
@@ -34,7 +35,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 // B200), so workspace sizes are functions of (M, N, K) alone.
 constexpr int kGemvSms = 148;
 
-// fp32 partial-sum bytes and ticket count of the tensor-core GEMV for N x K.
+// fp32 partial-sum bytes and ticket count of the tcgen05 GEMV for N x K.
 uint64_t gemv_w4a16_tc_partial_bytes(int N, int K);
 uint64_t gemv_w4a16_tc_ticket_count(int N);
 
@@ -51,5 +52,20 @@ int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, vo
                   int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream,
                   uint32_t* fp_record = nullptr, const uint32_t* fp_expect = nullptr,
                   unsigned long long* check_count = nullptr);
+
+// The warp-MMA GEMV for up to 8 rows (qg_gemv_w4a16_mma.cu): workspace parts
+// for `mrows` rows of N x K (fp32 partials, tickets).
+uint64_t gemv_w4a16_mma_partial_bytes(int mrows, int N, int K);
+uint64_t gemv_w4a16_mma_ticket_count(int N);
+
+// One call (one launch) for `mrows` (1..16) activation rows.  `partials`
+// (16-byte aligned) and `tickets` (zero on entry and on return) come from the
+// caller's workspace; `weights_const` is QG_GEMV_WEIGHTS_CONST (the kernel
+// ahead on the stream writes no W, S or Z).  With `golden` (a checked launch)
+// every stored output word is compared with the golden output and
+// differences are counted into `check_count`.
+int gemv_w4a16_mma(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
+                   int K, float* partials, unsigned int* tickets, bool weights_const, cudaStream_t stream,
+                   const void* golden = nullptr, unsigned long long* check_count = nullptr);
 
 } // namespace qg

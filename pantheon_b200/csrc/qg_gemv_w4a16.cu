@@ -1,7 +1,7 @@
 // qg_gemv_w4a16.cu -- weight-only W4A16 group-128 decode GEMV: the C entry
-// points, and the CUDA-core kernel for 1-2 activation rows (bandwidth-bound at
-// M = 1).  3-16 rows run on the tensor cores (qg_gemv_w4a16_tc.cu); larger M
-// is processed 16 rows at a time.
+// points, and the CUDA-core kernel for the single-row decode step
+// (bandwidth-bound).  2-8 rows run on warp MMAs (qg_gemv_w4a16_mma.cu), 9-16
+// on tcgen05 (qg_gemv_w4a16_tc.cu); larger M is processed 16 rows at a time.
 //
 //   Y[m, n] = sum_k X[m, k] * (q[k, n] - Z[k/128, n]) * S[k/128, n],  q = u - 8
 //
@@ -88,7 +88,7 @@ __device__ __forceinline__ float pow2(int e) { return __uint_as_float((uint32_t)
 template <int MT>
 __global__ void __launch_bounds__(THREADS, blocks_per_sm(MT))
 gemv_w4a16_kernel(Params p) {
-    static_assert(MT == 1 || MT == 2, "the CUDA-core kernel serves 1-2 rows");
+    static_assert(MT == 1 || MT == 2, "the kernel is written for 1-2 rows (the GEMV entry uses it for 1)");
     constexpr int DEPTH = load_depth(MT);
     constexpr int CPC = cols_per_cta(MT);
     using VT = uint4;
@@ -357,8 +357,6 @@ gemv_w4a16_kernel(Params p) {
     if (threadIdx.x == 0) p.tickets[blockIdx.x] = 0;   // ready for the next call
 }
 
-static int m_template(int M) { return M <= 1 ? 1 : 2; }
-
 static int col_blocks_for(int mt, int N) { return (N + cols_per_cta(mt) - 1) / cols_per_cta(mt); }
 
 // Shared-memory bytes for a K range of `len` packed rows (see the kernel's layout).
@@ -387,21 +385,36 @@ static size_t smem_bytes(int mt, int K, int splits) { return smem_bytes_len(mt, 
 
 } // namespace w4
 
-// Row chunks of up to 16 rows: 1-2 rows run on the CUDA cores (this file),
-// 3-16 on the tensor cores (qg_gemv_w4a16_tc.cu).
-constexpr int kTensorMinRows = 3;
+// Row chunks of up to 16 rows, each on the kernel that is fastest for its
+// row count (configs[3] shape, per call): 1 row on the CUDA cores (this file;
+// the decode step), 2-8 on register-fed warp MMAs (qg_gemv_w4a16_mma.cu:
+// 25.1 us at 2 rows against 33.9 us here, where the dp2a work doubles), 9-16
+// on the tcgen05 tensor cores (qg_gemv_w4a16_tc.cu).  At 9-16 rows the warp
+// MMAs would need 8 m16n8k32 per 32 x 32 weight tile (two activation digits
+// x 16 rows) at 0.5 per clock per SM, ~3/4 of the weight stream's time in the
+// MMA pipe alone; one tcgen05 M=128 N=32 K=32 MMA does 8x that work in ~45
+// cycles.
+constexpr int kMmaMinRows = 2;
+constexpr int kTcMinRows = 9;
 
-static uint64_t ticket_bytes(int N) {
-    const uint64_t a = (uint64_t)((N + 255) / 256), b = gemv_w4a16_tc_ticket_count(N);
-    return (a > b ? a : b) * 4;
+enum class Path { kCudaCore, kMma, kTc };
+static Path path_for(int mrows) {
+    return mrows >= kTcMinRows ? Path::kTc : (mrows >= kMmaMinRows ? Path::kMma : Path::kCudaCore);
 }
 
-// Workspace: fp32 partials for the largest row chunk, the tensor-core path's
-// prepared X (when any chunk takes it), then the tickets (shared by both
+static uint64_t ticket_bytes(int N) {
+    uint64_t most = (uint64_t)((N + 255) / 256);
+    const uint64_t counts[2] = {gemv_w4a16_mma_ticket_count(N), gemv_w4a16_tc_ticket_count(N)};
+    for (uint64_t c : counts) most = c > most ? c : most;
+    return most * 4;
+}
+
+// Workspace: fp32 partials for the largest row chunk, the tcgen05 path's
+// prepared X (when any chunk takes it), then the tickets (shared by all
 // kernels: each leaves them zero).
 static uint64_t xprep_bytes(int M, int K) {
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M)
-        if ((M - m0 < w4::MAX_M ? M - m0 : w4::MAX_M) >= kTensorMinRows)
+        if (path_for(M - m0 < w4::MAX_M ? M - m0 : w4::MAX_M) == Path::kTc)
             return (gemv_w4a16_tc_xprep_bytes(K) + 255) & ~255ull;
     return 0;
 }
@@ -412,11 +425,10 @@ uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int /*sm_count*/) {
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mrows = M - m0 < w4::MAX_M ? M - m0 : w4::MAX_M;
         uint64_t ws;
-        if (mrows >= kTensorMinRows) {
-            ws = gemv_w4a16_tc_partial_bytes(N, K);
-        } else {
-            const int mt = w4::m_template(mrows);
-            ws = (uint64_t)w4::choose_splits(mt, N, K) * mt * N * 4;
+        switch (path_for(mrows)) {
+            case Path::kTc: ws = gemv_w4a16_tc_partial_bytes(N, K); break;
+            case Path::kMma: ws = gemv_w4a16_mma_partial_bytes(mrows, N, K); break;
+            default: ws = (uint64_t)w4::choose_splits(1, N, K) * N * 4;
         }
         if (ws > partials) partials = ws;
     }
@@ -449,18 +461,26 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         const int mrows = (M - m0) < w4::MAX_M ? (M - m0) : w4::MAX_M;
         const size_t y_off = (size_t)m0 * N * (out_type == QG_OUT_F32 ? 4 : 2);
         const void* golden = chk.golden ? static_cast<const uint8_t*>(chk.golden) + y_off : nullptr;
-        const size_t fp_off = (size_t)(m0 / w4::MAX_M) * N;   // per-column fingerprints of this row chunk
-        if (mrows >= kTensorMinRows) {
+        const Path path = path_for(mrows);
+        if (path == Path::kTc) {
+            const size_t fp_off = (size_t)(m0 / w4::MAX_M) * N;   // per-column fingerprints of this row chunk
             rc = gemv_w4a16_tc(static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K, W, S, Z,
-                               static_cast<uint8_t*>(Y) + y_off, out_type,
-                               mrows, N, K, reinterpret_cast<float*>(ws),
+                               static_cast<uint8_t*>(Y) + y_off, out_type, mrows, N, K, reinterpret_cast<float*>(ws),
                                reinterpret_cast<unsigned int*>(ws + tickets_off), ws + xprep_off, stream,
                                chk.record ? chk.record + fp_off : nullptr, chk.expect ? chk.expect + fp_off : nullptr,
                                chk.count);
             if (rc) return rc;
             continue;
         }
-        const int mt = w4::m_template(mrows);
+        if (path == Path::kMma) {
+            rc = gemv_w4a16_mma(static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K, W, S, Z,
+                                static_cast<uint8_t*>(Y) + y_off, out_type, mrows, N, K, reinterpret_cast<float*>(ws),
+                                reinterpret_cast<unsigned int*>(ws + tickets_off),
+                                (flags & QG_GEMV_WEIGHTS_CONST) != 0, stream, golden, chk.count);
+            if (rc) return rc;
+            continue;
+        }
+        const int mt = 1;   // this kernel serves the single-row chunks
         const int splits = w4::choose_splits(mt, N, K);
         w4::Params p;
         p.X = static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K;
@@ -481,18 +501,10 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         const size_t smem = w4::smem_bytes(mt, K, splits);
         QG_CHECK_ARG(smem <= 200 * 1024, "qg_gemv_w4a16: K slice too large for shared memory");
         dim3 grid(w4::col_blocks_for(mt, N), splits);
-        switch (mt) {
-#define QG_W4_LAUNCH(MTV)                                                                                        \
-    case MTV:                                                                                                    \
-        if (smem > 48 * 1024)                                                                                    \
-            QG_CUDA(cudaFuncSetAttribute(w4::gemv_w4a16_kernel<MTV>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
-                                         (int)smem));                                                            \
-        QG_CUDA(launch_pdl(w4::gemv_w4a16_kernel<MTV>, grid, dim3(w4::THREADS), smem, stream, p));             \
-        break;
-            QG_W4_LAUNCH(1)
-            QG_W4_LAUNCH(2)
-#undef QG_W4_LAUNCH
-        }
+        if (smem > 48 * 1024)
+            QG_CUDA(cudaFuncSetAttribute(w4::gemv_w4a16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+        QG_CUDA(launch_pdl(w4::gemv_w4a16_kernel<1>, grid, dim3(w4::THREADS), smem, stream, p));
         QG_CUDA(cudaGetLastError());
     }
     return QG_OK;

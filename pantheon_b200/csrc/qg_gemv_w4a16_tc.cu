@@ -1,5 +1,7 @@
-// qg_gemv_w4a16_tc.cu -- W4A16 group-128 skinny GEMM for 3..16 activation rows
-// on the sm_100a tensor cores (tcgen05.mma kind::i8, A operand in TMEM).
+// qg_gemv_w4a16_tc.cu -- W4A16 group-128 skinny GEMM for up to 16 activation
+// rows on the sm_100a tensor cores (tcgen05.mma kind::i8, A operand in TMEM);
+// the GEMV entry routes 9..16 rows here (2..8 rows run faster on register-fed
+// warp MMAs, qg_gemv_w4a16_mma.cu).
 //
 //   Y[m, n] = sum_k X[m, k] * (q[k, n] - Z[k/128, n]) * S[k/128, n],  q = u - 8
 //
@@ -7,9 +9,11 @@
 // W uint32 [K/8, N] (nibble j of word (k8, n) is u(8*k8 + j, n)); S, Z fp16
 // [K/128, N]; Y bf16 or fp32 [M, N].
 //
-// At 8-16 rows a CUDA-core GEMV needs M FMAs per weight (3.8 GFMA per call at
-// M = 16, >= 100 us on the FP32 pipes against ~19 us of HBM time), so the
-// products go to the tensor cores with the weights as the MMA's M side:
+// At 9-16 rows a CUDA-core GEMV needs M FMAs per weight (3.8 GFMA per call at
+// M = 16, >= 100 us on the FP32 pipes against ~19 us of HBM time), and warp
+// MMAs need twice the MMA count of 8 rows (two activation digits x 16 rows =
+// 8 m16n8k32 per 32 x 32 weight tile), so the products go to tcgen05 with the
+// weights as the MMA's M side:
 // D[n, r] = sum_k Wt[n, k] * B[r, k], M = 128 weight columns, N = 32 rows.
 //
 // Integer arithmetic, exact up to the fold (the CUDA-core path's numerics):
@@ -54,11 +58,11 @@
 //               weight loads arrived ~7 us after issue, which with the ring
 //               refilled only after each MMA held the kernel to one unit per
 //               ~1500 cycles.
-//   warps 7-22  dequant, two teams of 8 taking alternate units (one team's
-//               barrier round trips overlap the other's): each warp owns a TMEM
-//               lane quarter and 8 of the 16 packed rows of a group; lane n
-//               turns each word into two TMEM columns of four 16q bytes, written
-//               with tcgen05.st as the MMA's A operand.
+//   warps 7-22  dequant, four teams of 4 taking units in turn (one team's
+//               barrier round trips overlap the others'): each warp owns a TMEM
+//               lane quarter; lane n turns each word of its column into two
+//               TMEM columns of four 16q bytes, written with tcgen05.st as the
+//               MMA's A operand.
 //   warp 1      TMEM allocator and MMA issuer: per group 4 x tcgen05.mma M=128
 //               N=32 K=32 into a 32-column int32 accumulator.
 //   warps 3-6   fold, one per lane quarter: per unit, read both groups'
@@ -98,7 +102,9 @@ constexpr int X_STAGES = 10;                              // prepared-X ring: 80
 constexpr int X_LAG = 4;                                  // units between an X copy and its publication
 static_assert(X_LAG < X_STAGES, "X ring depth");
 constexpr int X_RING_OFF = W_STAGES * W_BYTES;
-constexpr int TEAMS = 2;                      // dequant teams, alternate units
+// Four teams of four dequant warps, one unit each in turn (two teams of
+// eight took 1-2 % longer at 12 and 16 rows).
+constexpr int TEAMS = 4;                      // dequant teams, alternate units
 constexpr int NA = 4;                         // A operand buffers in TMEM
 constexpr int A_COLS = UG * GROUP / 4;        // 64 columns per unit: 2 x 128 bytes per lane
 constexpr int ND = 4;                         // accumulator buffers in TMEM
@@ -123,11 +129,11 @@ constexpr int SZ_RING = 8;                    // >= SZ_AHEAD + 1
 static_assert(SZ_RING >= SZ_AHEAD + 1, "ring depth");
 constexpr int XPW = 2;                        // X producer warp
 constexpr int FW0 = 3, FWARPS = 4;            // fold warps
-constexpr int DW0 = 7, DWARPS = 8;            // dequant warps per team
+constexpr int DW0 = 7, DWARPS = 4;            // dequant warps per team
 constexpr int THREADS = (DW0 + TEAMS * DWARPS) * 32;      // 736
 static_assert(FW0 + FWARPS == DW0, "the fold warps are the ones between the MMA warp and the dequant teams");
 // A warp reaches TMEM lanes 32 * (warp % 4) .. +31 only: the four fold warps and
-// each half-team of four dequant warps are consecutive, so they cover all four.
+// each team of four dequant warps are consecutive, so they cover all four.
 constexpr int SLICES = FWARPS;                // reduction slices of a tile = lane quarters
 constexpr int W_EMPTY_ARRIVALS = DWARPS;      // the dequant team of the unit
 constexpr int XPREP_THREADS = 128;            // prepass CTA: 16 rows x 2 groups x 4 quarters
@@ -542,10 +548,9 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
         }
         cp_async_wait<0>();
     } else {
-        // ------------------------------------------------------------ dequant (two teams)
+        // ------------------------------------------------------------ dequant (four teams)
         const int team = (warp - DW0) / DWARPS;
         const int q = warp & 3;                     // TMEM lane quarter = columns 32q .. 32q+31
-        const int h = ((warp - DW0) % DWARPS) >> 2; // packed rows 8h .. 8h+7 of each group
         const int n_local = q * 32 + lane;
         const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
         for (int i = team; i < nu; i += TEAMS) {
@@ -559,7 +564,8 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
             }
             tc_fence_after();
 #pragma unroll
-            for (int g = 0; g < UG; ++g) {
+            for (int gh = 0; gh < 2 * UG; ++gh) {   // group g, packed rows 8h .. 8h+7 of it
+                const int g = gh >> 1, h = gh & 1;
                 const uint32_t* wsm =
                     reinterpret_cast<const uint32_t*>(wring + s * W_BYTES) + (g * 16 + 8 * h) * TILE_N + n_local;
                 uint32_t a[16];

@@ -1,4 +1,5 @@
-"""W4A16 group-128 GEMV on the CUDA cores: parity with the CPU oracle, through the C ABI.
+"""W4A16 group-128 GEMV (1 row on the CUDA cores, 2-8 on warp MMAs, 9-16 on
+tcgen05): parity with the CPU oracle, through the C ABI.
 
 X bf16 [M in {1,8,16}, 8192] ~ N(0,1); W int4 [8192, 28672] uniform in
 [-8,7]; fp16 scale and zero per 128 along K; bf16 output; tolerance 1e-2 relative
@@ -39,7 +40,7 @@ def test_generator_matches_oracle(cuda_device, oracle):
     np.testing.assert_array_equal(_np(Z.view(torch.int16)).view(np.uint16), rZ)
 
 
-# 1-2 rows run on the CUDA cores, 3-16 on the tensor cores, more in chunks of 16
+# 1 row runs on the CUDA cores, 2-8 on warp MMAs, 9-16 on tcgen05, more in chunks of 16
 SHAPES = [(1, 512, 128), (1, 1028, 1024), (3, 2048, 2048), (8, 4096, 1024), (16, 1536, 4096),
           (17, 516, 256), (5, 28672, 256), (4, 300, 384), (12, 1028, 1024), (8, 128, 8192), (16, 36, 128),
           (34, 260, 512)]
@@ -58,10 +59,17 @@ def test_gemv_matches_oracle(cuda_device, oracle, shape):
     assert oracle.max_rel_err(_np(ybf.view(torch.int16)).view(np.uint16), refbf, 0) < RTOL
 
 
-@pytest.mark.parametrize("M", [1, 8, 16])
-def test_full_size_config3(cuda_device, oracle, M):
-    """configs[3] at full size; 256 sampled columns against the oracle, plus bitwise self-reproduction."""
-    N, K = 28672, 8192
+# configs[3] at M = 1, 8, 16, each row-count boundary of the three kernels, and
+# shapes whose warp-MMA grid runs in two waves (more groups per CTA than its
+# shared memory can hold at once in one wave): 8 x 57344 x 8192, 4 x 65536 x 8192.
+FULL = [(1, 28672, 8192), (2, 28672, 8192), (3, 28672, 8192), (4, 28672, 8192), (5, 28672, 8192),
+        (8, 28672, 8192), (9, 28672, 8192), (16, 28672, 8192), (8, 57344, 8192), (4, 65536, 8192)]
+
+
+@pytest.mark.parametrize("shape", FULL, ids=lambda s: "x".join(map(str, s)))
+def test_full_size_config3(cuda_device, oracle, shape):
+    """Full-size shapes; 256 sampled columns against the oracle, plus bitwise self-reproduction."""
+    M, N, K = shape
     with pb.Workload(pb.QG_FMT_W4A16, M, N, K, seed=3) as w:
         w.fill(3)
         w.golden()
