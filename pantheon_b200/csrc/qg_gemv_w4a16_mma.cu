@@ -283,19 +283,38 @@ gemv_w4a16_mma_kernel(Params p) {
     const int woff = t * 128 + ((g ^ (2 * t)) << 4);
     const size_t N = (size_t)p.N;
 
-    // Weights, scales and zero points of one iteration into ring slot `slot`:
-    // each lane copies its own word quad of every K step (and reads back only
-    // those), and one quarter of its column quad's scales / zero points.
-    auto issue = [&](int slot, int st, int grp) {
-        uint8_t* dst = ring + slot * SLOT;
-        const int col = st * ST_COLS + wcol;
-        const bool in = col < p.N;   // N % 4 == 0: a quad is wholly in or out
-        const uint32_t* src = p.W + (size_t)(grp * (GROUP / 8) + t) * N + (in ? col : 0);
+    // Weights, scales and zero points of the next iteration to copy (super-tile
+    // ast, group agrp) into ring slot islot: each lane copies its own word quad
+    // of every K step (and reads back only those), and one quarter of its
+    // column quad's scales / zero points.  Positions, slots and source
+    // addresses advance by additions (a division or modulo per iteration
+    // measured 1.3 % slower at 8 rows).
+    int ast = st0, agrp = grp0, islot = 0;
+    const uint32_t* wsrc = nullptr;
+    const __half* zsrc = nullptr;
+    bool ain = false;   // this lane's column quad lies inside N (N % 4 == 0: wholly in or out)
+    auto aim = [&]() {
+        const int col = ast * ST_COLS + wcol;
+        ain = col < p.N;
+        wsrc = p.W + (size_t)(agrp * (GROUP / 8) + t) * N + (ain ? col : 0);
+        zsrc = ((t >> 1) ? p.Z : p.S) + (ain ? (size_t)agrp * N + col + 2 * (t & 1) : 0);
+    };
+    aim();
+    auto issue = [&]() {
+        uint8_t* dst = ring + islot * SLOT;
 #pragma unroll
         for (int s = 0; s < STEPS; ++s)
-            cp_async_16z(dst + s * STEP_BYTES + woff, src + (size_t)(4 * s) * N, in ? 16u : 0u);
-        const __half* sz = ((t >> 1) ? p.Z : p.S) + (in ? (size_t)grp * N + col + 2 * (t & 1) : 0);
-        cp_async_4(dst + W_SLOT + g * 16 + t * 4, sz, in ? 4u : 0u);
+            cp_async_16z(dst + s * STEP_BYTES + woff, wsrc + (size_t)(4 * s) * N, ain ? 16u : 0u);
+        cp_async_4(dst + W_SLOT + g * 16 + t * 4, zsrc, ain ? 4u : 0u);
+        if (++islot == C::RING) islot = 0;
+        if (++agrp == p.G) {
+            agrp = 0;
+            ++ast;
+            aim();
+        } else if (ain) {
+            wsrc += (size_t)(GROUP / 8) * N;
+            zsrc += N;
+        }
     };
 
     // Prologue: the first RING - 1 groups.  Launched with programmatic stream
@@ -304,14 +323,10 @@ gemv_w4a16_mma_kernel(Params p) {
     // griddepcontrol.wait -- except, when the caller declares the weights
     // constant (the previous kernel writes no W, S or Z), these first weight
     // loads, which then overlap the previous call's tail.
-    int ast = st0, agrp = grp0;   // position of the next iteration to issue
     auto prologue = [&]() {
 #pragma unroll
         for (int j = 0; j < C::RING - 1; ++j) {
-            if (j < nit) {
-                issue(j, ast, agrp);
-                if (++agrp == p.G) { agrp = 0; ++ast; }
-            }
+            if (j < nit) issue();
             cp_async_commit();
         }
     };
@@ -408,20 +423,18 @@ gemv_w4a16_mma_kernel(Params p) {
     };
 
     int st = st0, grp = grp0;
+    int cslot = 0;                                                   // ring slot of iteration j
+    const uint8_t* xg = xsm + (size_t)(xall ? grp0 : 0) * C::XG;     // its staged activations
     for (int j = 0; j < nit; ++j) {
         // refill the slot iteration j - 1 used: every lane's reads of it
         // (its own weights; the scales and zero points of its column quad,
         // copied by four lanes) are complete past this barrier
         __syncwarp();
-        if (j + C::RING - 1 < nit) {
-            issue((j + C::RING - 1) % C::RING, ast, agrp);
-            if (++agrp == p.G) { agrp = 0; ++ast; }
-        }
+        if (j + C::RING - 1 < nit) issue();
         cp_async_commit();
         cp_async_wait<C::RING - 1>();   // this lane's copies of iteration j have landed
         __syncwarp();                   // ... and the other lanes' (scales, zero points)
-        const uint8_t* wsl = ring + (j % C::RING) * SLOT;
-        const uint8_t* xg = xsm + (size_t)(xall ? grp : j) * C::XG;
+        const uint8_t* wsl = ring + cslot * SLOT;
 
         // activation rows 4b + t of this group: 2^e, sum xi, 8 sum xi
         float xe[NB], xsum[NB];
@@ -483,7 +496,13 @@ gemv_w4a16_mma_kernel(Params p) {
                 }
         }
         if (grp == p.G - 1 || j == nit - 1) publish(st);
-        if (++grp == p.G) { grp = 0; ++st; }
+        if (++cslot == C::RING) cslot = 0;
+        xg += C::XG;
+        if (++grp == p.G) {
+            grp = 0;
+            ++st;
+            if (xall) xg = xsm;
+        }
     }
     cp_async_wait<0>();   // nothing may still be landing when the CTA exits
     if (p.golden) check_count_warp(p.check_count, bad);
