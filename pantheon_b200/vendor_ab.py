@@ -1,7 +1,7 @@
 """Interleaved A/B of this library's GEMMs against the vendor library (cuBLAS through
 torch) on the same operands and the same GPU, with the SM clock sampled per batch.
 
-    python -m pantheon_b200.vendor_ab --format nvfp4|bf16|fp16|e4m3|int8 [--m M --n N --k K]
+    python -m pantheon_b200.vendor_ab --format nvfp4|fp8|bf16|fp16|e4m3|int8 [--m M --n N --k K]
                                       [--batch 20] [--repeats 6]
 
 Each repeat runs one batch of ours then one batch of the vendor GEMM (the
@@ -28,7 +28,8 @@ import torch
 
 import pantheon_b200 as pb
 
-DEFAULT_SHAPES = {"nvfp4": (16384, 16384, 16384), "bf16": (8192, 8192, 8192), "fp16": (8192, 8192, 8192),
+DEFAULT_SHAPES = {"nvfp4": (16384, 16384, 16384), "fp8": (8192, 8192, 16384), "bf16": (8192, 8192, 8192),
+                  "fp16": (8192, 8192, 8192),
                   "e4m3": (8192, 8192, 8192), "int8": (8192, 8192, 8192)}
 
 
@@ -73,8 +74,9 @@ class ClockPoll:
 
 
 def setup(fmt: str, M: int, N: int, K: int):
-    """(ours, theirs, work) -- two callables that each launch one GEMM on the current
-    stream, on the same operands, and the useful operations of one launch."""
+    """(ours, theirs, work, out) -- two callables that each launch one GEMM on the
+    current stream, on the same operands; the useful operations of one launch;
+    the tensor ours() writes (theirs() returns its result)."""
     import torch.nn.functional as F
     dev = torch.device("cuda:0")
     if fmt == "nvfp4":
@@ -94,6 +96,21 @@ def setup(fmt: str, M: int, N: int, K: int):
                                swizzle_a=[F.SwizzleType.SWIZZLE_32_4_4, F.SwizzleType.NO_SWIZZLE],
                                swizzle_b=[F.SwizzleType.SWIZZLE_32_4_4, F.SwizzleType.NO_SWIZZLE],
                                output_dtype=torch.bfloat16)
+    elif fmt == "fp8":
+        # e4m3 with 1x128 (A) and 128x128 (B) fp32 block scales; the vendor
+        # GEMM takes A's scales M-fastest and B's as [K/128, N/128] K-fastest
+        A, B, sa, sb = pb.gen_fp8(M, N, K, seed=2)
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        a8, b8t = A.view(torch.float8_e4m3fn), B.view(torch.float8_e4m3fn).t()
+        sa_mf = sa.t().contiguous().t()
+        sb_kf = sb.t()
+
+        def ours():
+            pb.gemm_fp8_b128(A, B, sa, sb, out=out)
+
+        def theirs():
+            return F.scaled_mm(a8, b8t, [sa_mf], [F.ScalingType.BlockWise1x128], [sb_kf],
+                               [F.ScalingType.BlockWise128x128], output_dtype=torch.bfloat16)
     elif fmt == "int8":
         A = pb.gen_i8(M * K, seed=3, tensor_id=0)[:M * K].view(M, K)
         B = pb.gen_i8(N * K, seed=3, tensor_id=1)[:N * K].view(N, K)
@@ -130,7 +147,7 @@ def setup(fmt: str, M: int, N: int, K: int):
 
             def theirs():
                 return torch.matmul(A, Bt)
-    return ours, theirs, 2.0 * M * N * K
+    return ours, theirs, 2.0 * M * N * K, out
 
 
 def main(argv=None) -> int:
@@ -145,12 +162,18 @@ def main(argv=None) -> int:
     M, N, K = (a.m or DEFAULT_SHAPES[a.format][0], a.n or DEFAULT_SHAPES[a.format][1],
                a.k or DEFAULT_SHAPES[a.format][2])
     torch.cuda.set_device(0)
-    ours, theirs, work = setup(a.format, M, N, K)
+    ours, theirs, work, out = setup(a.format, M, N, K)
     s = torch.cuda.current_stream()
     for f in (ours, theirs):          # warm-up (and the vendor library's algorithm selection)
         for _ in range(3):
             f()
     torch.cuda.synchronize()
+    # the two results on the same operands: largest difference relative to the
+    # vendor result's rms (0 where both are bit-identical)
+    ref = theirs().float()
+    ours()
+    torch.cuda.synchronize()
+    agree = (out.float() - ref).abs().max().item() / max(ref.pow(2).mean().sqrt().item(), 1e-30)
     poll = ClockPoll(0)
     rates = {"ours": [], "vendor": []}
     per_ghz = {"ours": [], "vendor": []}
@@ -174,7 +197,8 @@ def main(argv=None) -> int:
     summary = {"format": a.format, "shape": [M, N, K], "batch": a.batch, "repeats": a.repeats,
                "ours_tops_median": statistics.median(rates["ours"]),
                "vendor_tops_median": statistics.median(rates["vendor"]),
-               "ratio_median": statistics.median(ratios), "ratio_min": min(ratios), "ratio_max": max(ratios)}
+               "ratio_median": statistics.median(ratios), "ratio_min": min(ratios), "ratio_max": max(ratios),
+               "max_diff_over_rms": agree}
     if all(x is not None for x in per_ghz["ours"] + per_ghz["vendor"]):
         rg = [o / v for o, v in zip(per_ghz["ours"], per_ghz["vendor"])]
         summary.update({"ours_tops_per_ghz_median": statistics.median(per_ghz["ours"]),
