@@ -288,9 +288,10 @@ QG_API int  qg_gemv_w4a16(const void* X, const void* W, const void* S, const voi
 
 /* qg_gemv_w4a16 with flags.  QG_GEMV_WEIGHTS_CONST: the kernel that precedes
  * this call on `stream` does not write W, S or Z (a decode loop over fixed
- * weights, e.g. the previous GEMV call); the 1-2-row kernel then issues its
- * first weight loads before waiting for that kernel to finish, overlapping
- * the previous call's tail.  Other bits are rejected with QG_ERR_ARG.
+ * weights, e.g. the previous GEMV call); the 1-row and 2-8-row kernels then
+ * issue their first weight loads before waiting for that kernel to finish,
+ * overlapping the previous call's tail.  Other bits are rejected with
+ * QG_ERR_ARG.
  * No counterpart in the reference. */
 #define QG_GEMV_WEIGHTS_CONST 1u
 QG_API int  qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, const void* Z, void* Y,
@@ -302,15 +303,17 @@ QG_API int  qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, const 
  * budget is already claimed, or a latency-critical decode path where an
  * allocation is not acceptable).  No counterpart in the reference.
  * Scratch comes from a 16 MiB array compiled into the library, which every GPU
- * that loads the library holds until the process exits; shapes whose
- * workspace (qg_gemv_w4a16_workspace_bytes) exceeds 16 MiB are rejected with
- * QG_ERR_ARG (configs[3], M <= 16, K = 8192, N = 28672, fits).  The call
- * allocates nothing; before the kernel runs it zeroes, on `stream`, the few
- * bytes of split-K tickets that must start at zero (everything else in the
- * array is written by the call before the call reads it).  All calls share the one array per device, so calls
- * that overlap on the GPU (other streams, other threads) race: serialise them.
- * The first call on a device looks up the array's device address; make that
- * first call before any stream capture. */
+ * that loads the library holds until the process exits: its first 256 KiB
+ * hold the split-K tickets of every call, the rest the partial sums and
+ * prepared activations.  Shapes whose workspace (qg_gemv_w4a16_workspace_bytes)
+ * does not fit are rejected with QG_ERR_ARG (configs[3], M <= 16, K = 8192,
+ * N = 28672, fits).  The call allocates nothing and clears nothing: every call
+ * leaves its tickets zero, and everything else it reads it wrote first; the
+ * first call on a device zeroes the ticket region once, on `stream`.  All
+ * calls share the one array per device, so calls that overlap on the GPU
+ * (other streams, other threads) race: serialise them.  The first call on a
+ * device also looks up the array's device address; make that first call
+ * before any stream capture. */
 QG_API int  qg_gemv_w4a16_noalloc(const void* X, const void* W, const void* S, const void* Z, void* Y,
                                   int out_type, int M, int N, int K, void* stream);
 

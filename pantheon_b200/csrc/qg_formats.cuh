@@ -72,9 +72,11 @@ int gemm_nvfp4(const void* A, const void* SFA, const void* B, const void* SFB, f
 int gen_w4a16(void* X, void* W, void* S, void* Z, int M, int N, int K, uint64_t seed, uint32_t tid0, cudaStream_t s);
 uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int sm_count);
 // `chk.expect` (when set) is the golden output, compared word for word by the writer of each output.
+// With `tickets` the split-K tickets live there (zero on entry, left zero) and the
+// workspace holds only the rest (gemv_w4a16_workspace_bytes minus the tickets).
 int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,
                void* workspace, uint64_t workspace_bytes, cudaStream_t stream, unsigned int flags,
-               const LaunchCheck& chk = LaunchCheck{});
+               const LaunchCheck& chk = LaunchCheck{}, unsigned int* tickets = nullptr);
 int verify_words(const void* actual, const void* expected, uint64_t nwords, void* counters, void* log, int log_cap,
                  cudaStream_t s);
 int flip_bit(void* word, cudaStream_t s);

@@ -437,7 +437,7 @@ uint64_t gemv_w4a16_workspace_bytes(int M, int N, int K, int /*sm_count*/) {
 
 int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M, int N, int K,
                void* workspace, uint64_t workspace_bytes, cudaStream_t stream, unsigned int flags,
-               const LaunchCheck& chk) {
+               const LaunchCheck& chk, unsigned int* tickets) {
     QG_CHECK_ARG(X && W && S && Z && Y, "qg_gemv_w4a16: null operand");
     QG_CHECK_ARG((flags & ~(unsigned int)QG_GEMV_WEIGHTS_CONST) == 0, "qg_gemv_w4a16: unknown flags 0x%x", flags);
     QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemv_w4a16: empty shape %dx%dx%d", M, N, K);
@@ -450,13 +450,14 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
     DeviceInfo* info = nullptr;
     int rc = current_device_info(&info);
     if (rc) return rc;
-    const uint64_t need = gemv_w4a16_workspace_bytes(M, N, K, info->sm_count);
+    const uint64_t need = gemv_w4a16_workspace_bytes(M, N, K, info->sm_count) - (tickets ? ticket_bytes(N) : 0);
     QG_CHECK_ARG(workspace && workspace_bytes >= need,
                  "qg_gemv_w4a16: workspace of %llu bytes needed (got %llu)", (unsigned long long)need,
                  (unsigned long long)workspace_bytes);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const uint64_t tickets_off = need - ticket_bytes(N);
+    const uint64_t tickets_off = need - (tickets ? 0 : ticket_bytes(N));
     const uint64_t xprep_off = tickets_off - xprep_bytes(M, K);
+    unsigned int* const tk = tickets ? tickets : reinterpret_cast<unsigned int*>(ws + tickets_off);
     for (int m0 = 0; m0 < M; m0 += w4::MAX_M) {
         const int mrows = (M - m0) < w4::MAX_M ? (M - m0) : w4::MAX_M;
         const size_t y_off = (size_t)m0 * N * (out_type == QG_OUT_F32 ? 4 : 2);
@@ -466,7 +467,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
             const size_t fp_off = (size_t)(m0 / w4::MAX_M) * N;   // per-column fingerprints of this row chunk
             rc = gemv_w4a16_tc(static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K, W, S, Z,
                                static_cast<uint8_t*>(Y) + y_off, out_type, mrows, N, K, reinterpret_cast<float*>(ws),
-                               reinterpret_cast<unsigned int*>(ws + tickets_off), ws + xprep_off, stream,
+                               tk, ws + xprep_off, stream,
                                chk.record ? chk.record + fp_off : nullptr, chk.expect ? chk.expect + fp_off : nullptr,
                                chk.count);
             if (rc) return rc;
@@ -475,8 +476,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         if (path == Path::kMma) {
             rc = gemv_w4a16_mma(static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K, W, S, Z,
                                 static_cast<uint8_t*>(Y) + y_off, out_type, mrows, N, K, reinterpret_cast<float*>(ws),
-                                reinterpret_cast<unsigned int*>(ws + tickets_off),
-                                (flags & QG_GEMV_WEIGHTS_CONST) != 0, stream, golden, chk.count);
+                                tk, (flags & QG_GEMV_WEIGHTS_CONST) != 0, stream, golden, chk.count);
             if (rc) return rc;
             continue;
         }
@@ -489,7 +489,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         p.Z = static_cast<const __half*>(Z);
         p.Y = static_cast<uint8_t*>(Y) + (size_t)m0 * N * (out_type == QG_OUT_F32 ? 4 : 2);
         p.ws = reinterpret_cast<float*>(ws);
-        p.tickets = reinterpret_cast<unsigned int*>(ws + tickets_off);
+        p.tickets = tk;
         p.M = mrows;
         p.N = N;
         p.K = K;
@@ -521,14 +521,14 @@ extern "C" int qg_gemv_w4a16_workspace_bytes(int M, int N, int K, uint64_t* byte
 extern "C" int qg_gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int M,
                              int N, int K, void* workspace, uint64_t workspace_bytes, void* stream) {
     return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, workspace, workspace_bytes,
-                          static_cast<cudaStream_t>(stream), 0u, qg::LaunchCheck{});
+                          static_cast<cudaStream_t>(stream), 0u, qg::LaunchCheck{}, nullptr);
 }
 
 extern "C" int qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type,
                                 int M, int N, int K, void* workspace, uint64_t workspace_bytes, unsigned int flags,
                                 void* stream) {
     return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, workspace, workspace_bytes,
-                          static_cast<cudaStream_t>(stream), flags, qg::LaunchCheck{});
+                          static_cast<cudaStream_t>(stream), flags, qg::LaunchCheck{}, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -547,6 +547,13 @@ extern "C" int qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, con
 // The array lives in every GPU that loads the library, for the life of the
 // process: kNoAllocScratchBytes of device memory per GPU.
 constexpr uint64_t kNoAllocScratchBytes = 16ull << 20;   // 16 MiB
+// Its first part holds the split-K tickets of every call, whatever the shape
+// (N/8 bytes at most: N up to 2^21 columns); the rest the partial sums and
+// prepared activations.  Every call leaves its tickets zero, so after one
+// clearing at the first call on a device no call needs a memset: a memset
+// between two calls would also keep the second from overlapping the first
+// (programmatic dependent launch), ~4 us per call.
+constexpr uint64_t kNoAllocTicketBytes = 256ull << 10;   // 256 KiB
 
 static __device__ __align__(256) uint8_t g_gemv_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -559,8 +566,9 @@ static void* g_noalloc_ptr[kNoAllocMaxDevices];
 
 // Device address of this device's scratch array.  In host code the array's
 // name is only a host-side stand-in, so the address is looked up once per
-// device, with that device current, and cached.
-static int noalloc_scratch(void** out) {
+// device, with that device current, and cached; the first lookup also clears
+// the ticket region on `stream` (ordered before the call that follows).
+static int noalloc_scratch(void** out, cudaStream_t stream) {
     int dev = 0;
     QG_CUDA(cudaGetDevice(&dev));
     QG_CHECK_ARG(dev >= 0 && dev < kNoAllocMaxDevices, "qg_gemv_w4a16_noalloc: device %d out of range", dev);
@@ -572,6 +580,7 @@ static int noalloc_scratch(void** out) {
             set_error("qg_gemv_w4a16_noalloc: cudaGetSymbolAddress failed: %s (%d)", cudaGetErrorString(e), (int)e);
             return QG_ERR_CUDA;
         }
+        QG_CUDA(cudaMemsetAsync(p, 0, (size_t)kNoAllocTicketBytes, stream));
         g_noalloc_ptr[dev] = p;
     }
     *out = g_noalloc_ptr[dev];
@@ -584,21 +593,23 @@ static int noalloc_scratch(void** out) {
 extern "C" int qg_gemv_w4a16_noalloc(const void* X, const void* W, const void* S, const void* Z, void* Y,
                                      int out_type, int M, int N, int K, void* stream) {
     QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemv_w4a16_noalloc: empty shape %dx%dx%d", M, N, K);
-    const uint64_t need = qg::gemv_w4a16_workspace_bytes(M, N, K, 0);
-    QG_CHECK_ARG(need <= kNoAllocScratchBytes,
-                 "qg_gemv_w4a16_noalloc: shape %dx%dx%d needs %llu bytes of scratch, above the built-in maximum of "
-                 "%llu bytes; use qg_gemv_w4a16 with a caller-provided workspace",
-                 M, N, K, (unsigned long long)need, (unsigned long long)kNoAllocScratchBytes);
-    void* scratch = nullptr;
-    int rc = qg::w4::noalloc_scratch(&scratch);
-    if (rc) return rc;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // The array keeps whatever the previous call (of any shape) left in it.
-    // Only the tickets must start at zero: every split-K partial and every
-    // prepared activation tile is written by this call before this call reads
-    // it.  The tickets sit at the end of this shape's part of the array, where a
-    // call of another shape may have left partial sums, so clear just them.
     const uint64_t tickets = qg::ticket_bytes(N);
-    QG_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(scratch) + (need - tickets), 0, (size_t)tickets, s));
-    return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, scratch, kNoAllocScratchBytes, s, 0u, qg::LaunchCheck{});
+    const uint64_t rest = qg::gemv_w4a16_workspace_bytes(M, N, K, 0) - tickets;
+    QG_CHECK_ARG(tickets <= kNoAllocTicketBytes && rest <= kNoAllocScratchBytes - kNoAllocTicketBytes,
+                 "qg_gemv_w4a16_noalloc: shape %dx%dx%d needs %llu bytes of scratch and %llu of tickets, above the "
+                 "built-in maximum of %llu and %llu bytes; use qg_gemv_w4a16 with a caller-provided workspace",
+                 M, N, K, (unsigned long long)rest, (unsigned long long)tickets,
+                 (unsigned long long)(kNoAllocScratchBytes - kNoAllocTicketBytes), (unsigned long long)kNoAllocTicketBytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* scratch = nullptr;
+    int rc = qg::w4::noalloc_scratch(&scratch, s);
+    if (rc) return rc;
+    // The array keeps whatever the previous call (of any shape) left in it.
+    // Every split-K partial and every prepared activation tile is written by
+    // this call before this call reads it, and the tickets (in their own
+    // region) are zero: the previous call left them so.
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    return qg::gemv_w4a16(X, W, S, Z, Y, out_type, M, N, K, base + kNoAllocTicketBytes,
+                          kNoAllocScratchBytes - kNoAllocTicketBytes, s, 0u, qg::LaunchCheck{},
+                          reinterpret_cast<unsigned int*>(base));
 }

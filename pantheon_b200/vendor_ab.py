@@ -1,7 +1,7 @@
 """Interleaved A/B of this library's GEMMs against the vendor library (cuBLAS through
 torch) on the same operands and the same GPU, with the SM clock sampled per batch.
 
-    python -m pantheon_b200.vendor_ab --format nvfp4|fp8|bf16|fp16|e4m3|int8 [--m M --n N --k K]
+    python -m pantheon_b200.vendor_ab --format nvfp4|bf16|fp16|e4m3|int8 [--m M --n N --k K]
                                       [--batch 20] [--repeats 6]
 
 Each repeat runs one batch of ours then one batch of the vendor GEMM (the
@@ -28,8 +28,7 @@ import torch
 
 import pantheon_b200 as pb
 
-DEFAULT_SHAPES = {"nvfp4": (16384, 16384, 16384), "fp8": (8192, 8192, 16384), "bf16": (8192, 8192, 8192),
-                  "fp16": (8192, 8192, 8192),
+DEFAULT_SHAPES = {"nvfp4": (16384, 16384, 16384), "bf16": (8192, 8192, 8192), "fp16": (8192, 8192, 8192),
                   "e4m3": (8192, 8192, 8192), "int8": (8192, 8192, 8192)}
 
 
@@ -96,21 +95,6 @@ def setup(fmt: str, M: int, N: int, K: int):
                                swizzle_a=[F.SwizzleType.SWIZZLE_32_4_4, F.SwizzleType.NO_SWIZZLE],
                                swizzle_b=[F.SwizzleType.SWIZZLE_32_4_4, F.SwizzleType.NO_SWIZZLE],
                                output_dtype=torch.bfloat16)
-    elif fmt == "fp8":
-        # e4m3 with 1x128 (A) and 128x128 (B) fp32 block scales; the vendor
-        # GEMM takes A's scales M-fastest and B's as [K/128, N/128] K-fastest
-        A, B, sa, sb = pb.gen_fp8(M, N, K, seed=2)
-        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-        a8, b8t = A.view(torch.float8_e4m3fn), B.view(torch.float8_e4m3fn).t()
-        sa_mf = sa.t().contiguous().t()
-        sb_kf = sb.t()
-
-        def ours():
-            pb.gemm_fp8_b128(A, B, sa, sb, out=out)
-
-        def theirs():
-            return F.scaled_mm(a8, b8t, [sa_mf], [F.ScalingType.BlockWise1x128], [sb_kf],
-                               [F.ScalingType.BlockWise128x128], output_dtype=torch.bfloat16)
     elif fmt == "int8":
         A = pb.gen_i8(M * K, seed=3, tensor_id=0)[:M * K].view(M, K)
         B = pb.gen_i8(N * K, seed=3, tensor_id=1)[:N * K].view(N, K)
