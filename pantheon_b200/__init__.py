@@ -31,6 +31,7 @@ from ._lib import (  # noqa: F401
     QG_OUT_S32,
     QG_OUT_F16,
     QG_GEMV_WEIGHTS_CONST,
+    QG_GEMV_ACTIVATIONS_CONST,
     QGError,
     load_library,
 )
@@ -65,5 +66,5 @@ __all__ = [
     "gen_w4a16", "gen_i8", "gen_uniform_f32", "gen_normal_f32", "verify_words",
     "QG_FMT_INT8", "QG_FMT_FP8", "QG_FMT_NVFP4", "QG_FMT_W4A16",
     "QG_FMT_BF16", "QG_FMT_FP16", "QG_FMT_TF32", "QG_FMT_E4M3", "QG_FMT_FP32",
-    "QG_OUT_BF16", "QG_OUT_F32", "QG_OUT_S32", "QG_OUT_F16", "QG_GEMV_WEIGHTS_CONST",
+    "QG_OUT_BF16", "QG_OUT_F32", "QG_OUT_S32", "QG_OUT_F16", "QG_GEMV_WEIGHTS_CONST", "QG_GEMV_ACTIVATIONS_CONST",
 ]

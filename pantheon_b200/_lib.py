@@ -22,6 +22,7 @@ QG_FMT_INT8, QG_FMT_FP8, QG_FMT_NVFP4, QG_FMT_W4A16 = 0, 1, 2, 3
 QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3, QG_FMT_FP32 = 4, 5, 6, 7, 8
 QG_OUT_BF16, QG_OUT_F32, QG_OUT_S32, QG_OUT_F16 = 0, 1, 2, 3
 QG_GEMV_WEIGHTS_CONST = 1
+QG_GEMV_ACTIVATIONS_CONST = 2
 
 
 class QGError(RuntimeError):

@@ -205,12 +205,14 @@ int qg_run(qg_ctx* c, int iters, void* stream) {
     QG_CHECK_ARG(c && iters >= 0, "qg_run: bad argument");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     for (int i = 0; i < iters; ++i) {
-        // From the second launch on, the kernel before each GEMV on this stream is
-        // the previous GEMV of this loop, which does not write the weights: their
-        // first loads may start before the dependency wait.
         const qg::CopyBuffers& cp = c->copies[(size_t)c->next_copy];
         const qg::LaunchCheck chk = run_check(c, cp);
-        int rc = qg::launch_copy(c->cfg, c->layout, cp, s, i > 0 ? QG_GEMV_WEIGHTS_CONST : 0u, chk);
+        // From the second launch on, the kernel before each GEMV on this stream
+        // is the previous GEMV of this loop, which writes neither the weights
+        // nor the activations: their first loads (and the activations'
+        // quantisation) may start before the dependency wait.
+        int rc = qg::launch_copy(c->cfg, c->layout, cp, s,
+                                 i > 0 ? (QG_GEMV_WEIGHTS_CONST | QG_GEMV_ACTIVATIONS_CONST) : 0u, chk);
         if (rc) return fail(c, rc);
         if (chk.count) ++c->launches_checked;
         c->next_copy = (c->next_copy + 1) % (int)c->copies.size();

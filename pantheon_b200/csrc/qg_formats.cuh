@@ -39,7 +39,7 @@ struct CopyBuffers {
 
 int layout_for(const qg_cfg& cfg, Layout* L);
 int fill_copy(const qg_cfg& cfg, const Layout& L, CopyBuffers& cp, int copy_index, uint64_t seed, cudaStream_t s);
-// `gemv_flags` (QG_GEMV_WEIGHTS_CONST or 0) is passed to the W4A16 GEMV; `chk`
+// `gemv_flags` (QG_GEMV_WEIGHTS_CONST | QG_GEMV_ACTIVATIONS_CONST, or 0) is passed to the W4A16 GEMV; `chk`
 // makes the launch record (golden) or check its own output (qg_check.cuh).
 int launch_copy(const qg_cfg& cfg, const Layout& L, const CopyBuffers& cp, cudaStream_t s, unsigned int gemv_flags = 0,
                 const LaunchCheck& chk = LaunchCheck{});

@@ -60,12 +60,13 @@ uint64_t gemv_w4a16_mma_ticket_count(int N);
 
 // One call (one launch) for `mrows` (1..16) activation rows.  `partials`
 // (16-byte aligned) and `tickets` (zero on entry and on return) come from the
-// caller's workspace; `weights_const` is QG_GEMV_WEIGHTS_CONST (the kernel
-// ahead on the stream writes no W, S or Z).  With `golden` (a checked launch)
+// caller's workspace; `flags` are the QG_GEMV_* declarations about the kernel
+// ahead on the stream (QG_GEMV_WEIGHTS_CONST: it writes no W, S or Z;
+// QG_GEMV_ACTIVATIONS_CONST: it writes no X).  With `golden` (a checked launch)
 // every stored output word is compared with the golden output and
 // differences are counted into `check_count`.
 int gemv_w4a16_mma(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
-                   int K, float* partials, unsigned int* tickets, bool weights_const, cudaStream_t stream,
+                   int K, float* partials, unsigned int* tickets, unsigned int flags, cudaStream_t stream,
                    const void* golden = nullptr, unsigned long long* check_count = nullptr);
 
 } // namespace qg

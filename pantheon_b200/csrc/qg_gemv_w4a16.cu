@@ -439,7 +439,8 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
                void* workspace, uint64_t workspace_bytes, cudaStream_t stream, unsigned int flags,
                const LaunchCheck& chk, unsigned int* tickets) {
     QG_CHECK_ARG(X && W && S && Z && Y, "qg_gemv_w4a16: null operand");
-    QG_CHECK_ARG((flags & ~(unsigned int)QG_GEMV_WEIGHTS_CONST) == 0, "qg_gemv_w4a16: unknown flags 0x%x", flags);
+    QG_CHECK_ARG((flags & ~(unsigned int)(QG_GEMV_WEIGHTS_CONST | QG_GEMV_ACTIVATIONS_CONST)) == 0,
+                 "qg_gemv_w4a16: unknown flags 0x%x", flags);
     QG_CHECK_ARG(M > 0 && N > 0 && K > 0, "qg_gemv_w4a16: empty shape %dx%dx%d", M, N, K);
     QG_CHECK_ARG(K % w4::GROUP == 0, "qg_gemv_w4a16: K=%d must be a multiple of 128 (group size)", K);
     QG_CHECK_ARG(N % 4 == 0, "qg_gemv_w4a16: N=%d must be a multiple of 4", N);
@@ -476,7 +477,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         if (path == Path::kMma) {
             rc = gemv_w4a16_mma(static_cast<const __nv_bfloat16*>(X) + (size_t)m0 * K, W, S, Z,
                                 static_cast<uint8_t*>(Y) + y_off, out_type, mrows, N, K, reinterpret_cast<float*>(ws),
-                                tk, (flags & QG_GEMV_WEIGHTS_CONST) != 0, stream, golden, chk.count);
+                                tk, flags, stream, golden, chk.count);
             if (rc) return rc;
             continue;
         }

@@ -11,7 +11,7 @@ import ctypes as C
 
 import torch
 
-from ._lib import (QG_GEMV_WEIGHTS_CONST, QG_FMT_INT8, QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3, QG_FMT_FP32, QG_OUT_BF16, QG_OUT_F16,
+from ._lib import (QG_GEMV_ACTIVATIONS_CONST, QG_GEMV_WEIGHTS_CONST, QG_FMT_INT8, QG_FMT_BF16, QG_FMT_FP16, QG_FMT_TF32, QG_FMT_E4M3, QG_FMT_FP32, QG_OUT_BF16, QG_OUT_F16,
                    QG_OUT_F32, QG_OUT_S32, QGCfg, QGMismatch, QGError, check,
                    last_error, load_library)
 
@@ -194,7 +194,7 @@ def gemv_w4a16_workspace_bytes(M: int, N: int, K: int) -> int:
 
 def gemv_w4a16(X: torch.Tensor, W: torch.Tensor, S: torch.Tensor, Z: torch.Tensor, out_type: int = QG_OUT_BF16,
                workspace: torch.Tensor | None = None, out: torch.Tensor | None = None,
-               weights_const: bool = False) -> torch.Tensor:
+               weights_const: bool = False, activations_const: bool = False) -> torch.Tensor:
     """Y = X @ dequant(W) on the W4A16 path (1 row CUDA cores, 2-8 warp MMAs, 9-16 tcgen05).
 
     X bf16 [M,K]; W int32/uint32 [K/8,N] packed int4 (nibble j = k offset j);
@@ -202,7 +202,8 @@ def gemv_w4a16(X: torch.Tensor, W: torch.Tensor, S: torch.Tensor, Z: torch.Tenso
     zero-filled, qg_gemv_w4a16_workspace_bytes) is allocated when not given.
     `weights_const`: the kernel before this call on the stream does not write
     W, S or Z (QG_GEMV_WEIGHTS_CONST), so the first weight loads may start
-    before it finishes.
+    before it finishes; `activations_const`: it does not write X
+    (QG_GEMV_ACTIVATIONS_CONST), so the activations may be quantised before.
     """
     _require_cuda(X, W, S, Z)
     M, K = X.shape
@@ -212,7 +213,7 @@ def gemv_w4a16(X: torch.Tensor, W: torch.Tensor, S: torch.Tensor, Z: torch.Tenso
     need = gemv_w4a16_workspace_bytes(M, N, K)
     if workspace is None:
         workspace = torch.zeros((need,), dtype=torch.uint8, device=X.device)
-    flags = QG_GEMV_WEIGHTS_CONST if weights_const else 0
+    flags = (QG_GEMV_WEIGHTS_CONST if weights_const else 0) | (QG_GEMV_ACTIVATIONS_CONST if activations_const else 0)
     check("qg_gemv_w4a16_ex", load_library().qg_gemv_w4a16_ex(_ptr(X), _ptr(W), _ptr(S), _ptr(Z), _ptr(out), out_type,
                                                                M, N, K, _ptr(workspace), workspace.numel(), flags,
                                                                _stream(X.device)))

@@ -113,8 +113,9 @@ def test_gemv_rejects_unknown_flags(qglib):
     """qg_gemv_w4a16_ex checks its flags before touching the device."""
     import pantheon_b200 as pb
     fake = 1 << 20   # aligned, never dereferenced: the call returns before any device access
-    assert qglib.qg_gemv_w4a16_ex(fake, fake, fake, fake, fake, pb.QG_OUT_BF16, 1, 128, 128, fake, 1 << 20, 2,
-                                  None) == pb._lib.QG_ERR_ARG
+    known = pb.QG_GEMV_WEIGHTS_CONST | pb.QG_GEMV_ACTIVATIONS_CONST
+    assert qglib.qg_gemv_w4a16_ex(fake, fake, fake, fake, fake, pb.QG_OUT_BF16, 1, 128, 128, fake, 1 << 20,
+                                  known << 1, None) == pb._lib.QG_ERR_ARG
     assert "unknown flags" in pb._lib.last_error()
 
 

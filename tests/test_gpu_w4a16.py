@@ -87,13 +87,16 @@ def test_full_size_config3(cuda_device, oracle, shape):
 
 
 @pytest.mark.parametrize("M", [1, 2, 8])
-def test_weights_const_flag_is_bit_identical(cuda_device, oracle, M):
-    """QG_GEMV_WEIGHTS_CONST only moves the first weight loads before the dependency wait:
-    back-to-back calls over fixed weights give the same bits as the default path."""
+@pytest.mark.parametrize("flags", ["weights", "activations", "both"])
+def test_const_flags_are_bit_identical(cuda_device, oracle, M, flags):
+    """QG_GEMV_WEIGHTS_CONST / QG_GEMV_ACTIVATIONS_CONST only move the first weight loads
+    and the activations' quantisation before the dependency wait: back-to-back calls over
+    fixed operands give the same bits as the default path."""
     N, K = 4096, 2048
     host, dev = _operands(oracle, M, N, K, seed=11, dev=cuda_device)
     ref = pb.gemv_w4a16(*dev, out_type=pb.QG_OUT_F32)
-    outs = [pb.gemv_w4a16(*dev, out_type=pb.QG_OUT_F32, weights_const=True) for _ in range(6)]
+    kw = {"weights_const": flags in ("weights", "both"), "activations_const": flags in ("activations", "both")}
+    outs = [pb.gemv_w4a16(*dev, out_type=pb.QG_OUT_F32, **kw) for _ in range(6)]
     torch.cuda.synchronize()
     for y in outs:
         assert torch.equal(y.view(torch.int32), ref.view(torch.int32))
