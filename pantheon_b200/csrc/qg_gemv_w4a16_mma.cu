@@ -206,13 +206,15 @@ __device__ __forceinline__ void prep_x(const Params& p, uint8_t* xsm, int xcount
         const int tau = r * THREADS + threadIdx.x;
         const bool active = tau < ntask;               // whole lane quads are active or not
         const int q = tau / TPG, m = (tau % TPG) / STEPS, s = tau % STEPS;
-        uint32_t amax = 0;
+        // group absmax: |x| bits of both halves of each word at once (packed 16-bit max)
+        uint32_t am2 = 0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const uint32_t w4[4] = {v[r][i].x, v[r][i].y, v[r][i].z, v[r][i].w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) amax = max(amax, max(w4[e] & 0x7FFFu, (w4[e] >> 16) & 0x7FFFu));
+            for (int e = 0; e < 4; ++e) am2 = __vmaxu2(am2, w4[e] & 0x7FFF7FFFu);
         }
+        uint32_t amax = max(am2 & 0xFFFFu, am2 >> 16);
         amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
         amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
         // xi = round(x * 2^(13 - E)), E = the absmax's exponent: |xi| <= 2^14.  A
@@ -221,40 +223,44 @@ __device__ __forceinline__ void prep_x(const Params& p, uint8_t* xsm, int xcount
         const bool usable = ebits >= 14;
         const float mul = usable ? __uint_as_float((uint32_t)(127 + 13 + 127 - ebits) << 23) : 0.0f;
         const float scale = usable ? __uint_as_float((uint32_t)(ebits - 13) << 23) : 0.0f;
-        int isum = 0;
+        // Rounding through the 1.5 * 2^23 shifter: x * mul is exact (a power of
+        // two), so fmaf(x, mul, 1.5 * 2^23) rounds it half to even and leaves
+        // bits = 0x4B400000 + xi, with 0x4B400000 a multiple of 2^22: bits 0-6
+        // are l and bits 7-14 are h = xi >> 7 (two's complement), and the
+        // clamp of xi to 2^14 - 1 is an integer min on the bits.
+        constexpr float kShift = 12582912.0f;
+        constexpr int kBase = 0x4B400000;
+        int bsum = 0;   // sum of the bits words: isum = bsum - 32 kBase (mod 2^32, exact)
         uint8_t* xstep = xsm + (size_t)q * C::XG + s * C::XF_STEP;
         const int b = m >> 2, nh = 2 * (m & 3);   // B fragment; digit rows nh (h) and nh + 1 (l)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {   // k = 8i .. 8i+7 of the step: lane (digit row, t = i)
             const uint32_t w4[4] = {v[r][i].x, v[r][i].y, v[r][i].z, v[r][i].w};
-            int xiv[8];
+            uint32_t bits[8];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                // exact scaling by a power of two, then round half to even via the 1.5 * 2^23 shifter
-                const float lo = __uint_as_float(w4[e] << 16) * mul;
-                const float hi = __uint_as_float(w4[e] & 0xFFFF0000u) * mul;
-                xiv[2 * e] = min(__float_as_int(lo + 12582912.0f) - 0x4B400000, 16383);
-                xiv[2 * e + 1] = min(__float_as_int(hi + 12582912.0f) - 0x4B400000, 16383);
+                bits[2 * e] = (uint32_t)min(__float_as_int(fmaf(__uint_as_float(w4[e] << 16), mul, kShift)), kBase + 16383);
+                bits[2 * e + 1] =
+                    (uint32_t)min(__float_as_int(fmaf(__uint_as_float(w4[e] & 0xFFFF0000u), mul, kShift)), kBase + 16383);
+                bsum += (int)(bits[2 * e] + bits[2 * e + 1]);
             }
-            uint32_t hb[8], lb[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                isum += xiv[e];
-                hb[e] = (uint32_t)(xiv[e] >> 7) & 0xFFu;   // arithmetic shift: floor
-                lb[e] = (uint32_t)xiv[e] & 0x7Fu;
-            }
+            // the low bytes of four words, in order, as one word
+            auto pack4 = [](uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3) {
+                return __byte_perm(__byte_perm(a0, a1, 0x0040), __byte_perm(a2, a3, 0x0040), 0x5410);
+            };
             // register 0: k = 8i + 0, 2, 4, 6; register 1: k = 8i + 1, 3, 5, 7
             if (active) {
                 *reinterpret_cast<uint2*>(xstep + frag_offset<NB>(b, 4 * nh + i)) =
-                    make_uint2(hb[0] | (hb[2] << 8) | (hb[4] << 16) | (hb[6] << 24),
-                               hb[1] | (hb[3] << 8) | (hb[5] << 16) | (hb[7] << 24));
+                    make_uint2(pack4(bits[0] >> 7, bits[2] >> 7, bits[4] >> 7, bits[6] >> 7),
+                               pack4(bits[1] >> 7, bits[3] >> 7, bits[5] >> 7, bits[7] >> 7));
                 *reinterpret_cast<uint2*>(xstep + frag_offset<NB>(b, 4 * (nh + 1) + i)) =
-                    make_uint2(lb[0] | (lb[2] << 8) | (lb[4] << 16) | (lb[6] << 24),
-                               lb[1] | (lb[3] << 8) | (lb[5] << 16) | (lb[7] << 24));
+                    make_uint2(pack4(bits[0], bits[2], bits[4], bits[6]) & 0x7F7F7F7Fu,
+                               pack4(bits[1], bits[3], bits[5], bits[7]) & 0x7F7F7F7Fu);
             }
         }
-        isum += __shfl_xor_sync(0xffffffffu, isum, 1);
-        isum += __shfl_xor_sync(0xffffffffu, isum, 2);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);
+        const int isum = (int)((uint32_t)bsum - (uint32_t)(GROUP * kBase));
         if (active && s == 0)
             *(reinterpret_cast<int4*>(xsm + (size_t)q * C::XG + C::XS_OFF) + ((m & 3) * NB + b)) =
                 make_int4(__float_as_int(scale), __float_as_int((float)isum), 8 * isum, 0);
