@@ -47,11 +47,13 @@ uint64_t gemv_w4a16_tc_xprep_bytes(int K);
 // workspace, tickets zero on entry (and on return).  Per-launch check
 // (qg_check.cuh): with `fp_record` the writer of each output column stores the
 // column's fingerprint (N entries); with `fp_expect` it compares it with the
-// recorded one and counts differing columns into `check_count`.
+// recorded one and counts differing columns into `check_count`.  With
+// QG_GEMV_ACTIVATIONS_CONST in `flags` the pre-pass quantises X before waiting
+// for the kernel ahead on the stream (it waits only before its stores).
 int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
                   int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream,
                   uint32_t* fp_record = nullptr, const uint32_t* fp_expect = nullptr,
-                  unsigned long long* check_count = nullptr);
+                  unsigned long long* check_count = nullptr, unsigned int flags = 0);
 
 // The warp-MMA GEMV for up to 8 rows (qg_gemv_w4a16_mma.cu): workspace parts
 // for `mrows` rows of N x K (fp32 partials, tickets).

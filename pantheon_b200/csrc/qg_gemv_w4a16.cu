@@ -71,6 +71,7 @@ struct Params {
     int splits;
     int out_type;
     int early_w;             // QG_GEMV_WEIGHTS_CONST: first weight loads before the dependency wait
+    int early_x;             // QG_GEMV_ACTIVATIONS_CONST: with early_w, the whole prologue before the wait
     const void* golden;      // per-launch check: the golden Y (same layout), or null
     unsigned long long* check_count;   // differing output words found
 };
@@ -132,23 +133,29 @@ gemv_w4a16_kernel(Params p) {
     // Launched with programmatic stream serialization: this CTA may be resident
     // before the previous kernel on the stream has finished, so nothing global
     // is read or written until that grid is complete (a no-op otherwise) --
-    // except, when the caller declares the weights constant (the previous
-    // kernel does not write W), the first weight batches, which then overlap
-    // the previous call's tail.
+    // except what the caller declares the previous kernel does not write: with
+    // the weights constant (no W, S, Z) the first weight batches, and with the
+    // activations constant as well (no X) the whole prologue below, which
+    // reads only W, S, Z and X and writes only shared memory; all of it then
+    // overlaps the previous call's tail.
     if (p.early_w && active) {
         load_batch(wa, 0);
         if (DEPTH < len) load_batch(wb, DEPTH);
     }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (!p.early_w && active) {
-        load_batch(wa, 0);
-        if (DEPTH < len) load_batch(wb, DEPTH);
-    }
     // The next call on the stream may launch once every CTA of this one has
-    // passed this point (so all of them are resident: none can be starved of
-    // an SM by the next grid); its CTAs take SMs as these exit, and wait for
-    // this grid before touching anything it writes.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // passed the wait (so all of them are resident: none can be starved of an
+    // SM by the next grid); its CTAs take SMs as these exit, and wait for this
+    // grid before touching anything it writes.
+    const bool early_prologue = p.early_w && p.early_x;
+    auto wait_previous = [&]() {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (!p.early_w && active) {
+            load_batch(wa, 0);
+            if (DEPTH < len) load_batch(wb, DEPTH);
+        }
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    };
+    if (!early_prologue) wait_previous();
 
     // Scales and zero points of this CTA's groups, staged once with 64-bit
     // loads (rows of S and Z are 8-byte aligned because N % 4 == 0): the group
@@ -226,6 +233,8 @@ gemv_w4a16_kernel(Params p) {
         xi[(size_t)ch * MT + m] = make_int4(pk(q[0], q[2]), pk(q[4], q[6]), pk(q[1], q[3]), pk(q[5], q[7]));
     }
     __syncthreads();
+
+    if (early_prologue) wait_previous();   // Y and the workspace are written only past this point
 
     float y[MT][CPT];
 #pragma unroll
@@ -470,7 +479,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
                                static_cast<uint8_t*>(Y) + y_off, out_type, mrows, N, K, reinterpret_cast<float*>(ws),
                                tk, ws + xprep_off, stream,
                                chk.record ? chk.record + fp_off : nullptr, chk.expect ? chk.expect + fp_off : nullptr,
-                               chk.count);
+                               chk.count, flags);
             if (rc) return rc;
             continue;
         }
@@ -497,6 +506,7 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
         p.splits = splits;
         p.out_type = out_type;
         p.early_w = (flags & QG_GEMV_WEIGHTS_CONST) ? 1 : 0;
+        p.early_x = (flags & QG_GEMV_ACTIVATIONS_CONST) ? 1 : 0;
         p.golden = golden;
         p.check_count = chk.count;
         const size_t smem = w4::smem_bytes(mt, K, splits);

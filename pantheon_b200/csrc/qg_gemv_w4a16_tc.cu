@@ -600,11 +600,19 @@ gemv_w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmW, Params p) {
 // groups past K come out as zero tiles with zero scales.
 template <int MR>
 __global__ void __launch_bounds__(XPREP_THREADS)
-xprep_kernel(const __nv_bfloat16* __restrict__ X, int M, int K, int G, uint8_t* __restrict__ xprep, int G2) {
+xprep_kernel(const __nv_bfloat16* __restrict__ X, int M, int K, int G, uint8_t* __restrict__ xprep, int G2,
+             int early_x) {
     using T = Tile<MR>;
-    // programmatic stream serialization: X may come from the previous kernel
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // Programmatic stream serialization: X may come from the previous kernel,
+    // and the previous GEMV may still be reading the prepared-X area.  So the
+    // kernel waits for it before reading X -- or, when the caller declares
+    // that the previous kernel does not write X (early_x), quantises X into
+    // registers first and waits only before its stores.
+    auto wait_previous = []() {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    };
+    if (!early_x) wait_previous();
     const int xi = threadIdx.x;
     const int m = xi >> 3;                      // row 0..15
     const int g = (xi >> 2) & 1;                // group of the pair
@@ -635,9 +643,9 @@ xprep_kernel(const __nv_bfloat16* __restrict__ X, int M, int K, int G, uint8_t* 
     const float scale = usable ? __uint_as_float((uint32_t)(ebits - 13) << 23) : 0.0f;
     int isum = 0;
     uint8_t* xt = xprep + (size_t)grp * T::XT_GROUP;
+    uint32_t hw[2][4], lw[2][4];   // per 16-byte chunk c: h and l digit words
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
-        uint32_t hw[4], lw[4];
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
             const uint4 vv = v[2 * c + rr];
@@ -659,18 +667,23 @@ xprep_kernel(const __nv_bfloat16* __restrict__ X, int M, int K, int G, uint8_t* 
                 lb[e] = (uint32_t)xiv[e] & 0x7Fu;
             }
             // K order (x0, x2, x4, x6, x1, x3, x5, x7)
-            hw[2 * rr] = hb[0] | (hb[2] << 8) | (hb[4] << 16) | (hb[6] << 24);
-            hw[2 * rr + 1] = hb[1] | (hb[3] << 8) | (hb[5] << 16) | (hb[7] << 24);
-            lw[2 * rr] = lb[0] | (lb[2] << 8) | (lb[4] << 16) | (lb[6] << 24);
-            lw[2 * rr + 1] = lb[1] | (lb[3] << 8) | (lb[5] << 16) | (lb[7] << 24);
-        }
-        if (m < T::MROWS) {   // an 8-row tile has no rows 8-15 (their threads only join the shuffles)
-            *reinterpret_cast<uint4*>(xt + xt_offset(m, 2 * qk + c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4*>(xt + xt_offset(T::MROWS + m, 2 * qk + c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            hw[c][2 * rr] = hb[0] | (hb[2] << 8) | (hb[4] << 16) | (hb[6] << 24);
+            hw[c][2 * rr + 1] = hb[1] | (hb[3] << 8) | (hb[5] << 16) | (hb[7] << 24);
+            lw[c][2 * rr] = lb[0] | (lb[2] << 8) | (lb[4] << 16) | (lb[6] << 24);
+            lw[c][2 * rr + 1] = lb[1] | (lb[3] << 8) | (lb[5] << 16) | (lb[7] << 24);
         }
     }
     isum += __shfl_xor_sync(0xffffffffu, isum, 1);
     isum += __shfl_xor_sync(0xffffffffu, isum, 2);
+    if (early_x) wait_previous();
+    if (m < T::MROWS) {   // an 8-row tile has no rows 8-15 (their threads only join the shuffles)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            *reinterpret_cast<uint4*>(xt + xt_offset(m, 2 * qk + c)) = make_uint4(hw[c][0], hw[c][1], hw[c][2], hw[c][3]);
+            *reinterpret_cast<uint4*>(xt + xt_offset(T::MROWS + m, 2 * qk + c)) =
+                make_uint4(lw[c][0], lw[c][1], lw[c][2], lw[c][3]);
+        }
+    }
     if (qk == 0 && m < T::MROWS) {
         float* xs = reinterpret_cast<float*>(xprep + (size_t)G2 * T::XT_GROUP) + (size_t)grp * T::XS_GROUP;
         xs[m] = scale;
@@ -715,7 +728,7 @@ uint64_t gemv_w4a16_tc_xprep_bytes(int K) {
 
 int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
                   int K, float* partials, unsigned int* tickets, void* xprep, cudaStream_t stream, uint32_t* fp_record,
-                  const uint32_t* fp_expect, unsigned long long* check_count) {
+                  const uint32_t* fp_expect, unsigned long long* check_count, unsigned int flags) {
     QG_CHECK_ARG(mrows >= 1 && mrows <= w4tc::MAX_MROWS, "gemv_w4a16_tc: %d rows (1..16)", mrows);
     DeviceStatus* status = nullptr;
     int rc = device_status_ptr(&status);
@@ -760,12 +773,12 @@ int gemv_w4a16_tc(const void* X, const void* W, const void* S, const void* Z, vo
     uint8_t* xp = static_cast<uint8_t*>(xprep);
     if (mrows <= 8) {
         QG_CUDA(launch_pdl(w4tc::xprep_kernel<8>, dim3(s.upt), dim3(w4tc::XPREP_THREADS), 0, stream, Xb, mrows, K, s.G, xp,
-                           s.upt * w4tc::UG));
+                           s.upt * w4tc::UG, (flags & QG_GEMV_ACTIVATIONS_CONST) ? 1 : 0));
         QG_CUDA(launch_pdl(w4tc::gemv_w4a16_tc_kernel<8>, dim3(s.ctas), dim3(w4tc::THREADS),
                            (size_t)w4tc::smem_bytes<8>(), stream, tmW, p));
     } else {
         QG_CUDA(launch_pdl(w4tc::xprep_kernel<16>, dim3(s.upt), dim3(w4tc::XPREP_THREADS), 0, stream, Xb, mrows, K, s.G, xp,
-                           s.upt * w4tc::UG));
+                           s.upt * w4tc::UG, (flags & QG_GEMV_ACTIVATIONS_CONST) ? 1 : 0));
         QG_CUDA(launch_pdl(w4tc::gemv_w4a16_tc_kernel<16>, dim3(s.ctas), dim3(w4tc::THREADS),
                            (size_t)w4tc::smem_bytes<16>(), stream, tmW, p));
     }
