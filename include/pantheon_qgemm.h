@@ -298,9 +298,11 @@ QG_API int  qg_gemv_w4a16(const void* X, const void* W, const void* S, const voi
  * does not write X (a loop of GEMVs over one activation set, such as the
  * workload's timed loop; not a decode step, whose X the layer before just
  * wrote).  The 2-8-row kernel then quantises its activations before waiting
- * for that kernel, overlapping the previous call's tail, and the 1-row kernel,
- * when QG_GEMV_WEIGHTS_CONST is set too, stages its activations, scales and
- * zero points before the wait.  Either, both or neither flag may be set. */
+ * for that kernel, overlapping the previous call's tail; the 9-16-row path's
+ * pre-pass quantises them before its wait (and stores them after it); and the
+ * 1-row kernel, when QG_GEMV_WEIGHTS_CONST is set too, stages its
+ * activations, scales and zero points before the wait.  Either, both or
+ * neither flag may be set. */
 #define QG_GEMV_ACTIVATIONS_CONST 2u
 QG_API int  qg_gemv_w4a16_ex(const void* X, const void* W, const void* S, const void* Z, void* Y,
                              int out_type, int M, int N, int K, void* workspace, uint64_t workspace_bytes,
