@@ -116,8 +116,11 @@ QG_API int  qg_golden(qg_ctx* ctx);
  * and the dense tensor formats, 128 for FP8 and NVFP4; INT8 also folds its
  * INT32 accumulators) into a fingerprint and compares it with the one the
  * golden launch recorded; the GEMV compares every output word it writes with
- * the golden output.  Differences are counted on the device for qg_verify, so
- * a corruption in any launch of a batch is seen, not only in the last.
+ * the golden output (9-16 rows: per-column fingerprints, like the GEMMs).
+ * Differences are counted on the device for qg_verify, so a corruption in any
+ * launch of a batch is seen, not only in the last.  W4A16 launches after the
+ * first pass QG_GEMV_WEIGHTS_CONST | QG_GEMV_ACTIVATIONS_CONST: the kernel
+ * ahead is the previous GEMV, which writes neither.
  * Replaces: the ai_workload_kernel launch of the timed loop
  *           (ai_workload_template.h:370). Asynchronous. */
 QG_API int  qg_run(qg_ctx* ctx, int iters, void* stream);
