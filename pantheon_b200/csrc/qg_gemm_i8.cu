@@ -584,6 +584,202 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
 }
 
+// ---------------------------------------------------------------------------
+// Wide CTA-pair variant (M >= 256, N > 256, 2- and 4-byte kinds): a cluster of two CTAs computes
+// 256x512 tiles as two 256-column halves, each half one tcgen05.mma
+// .cta_group::2 (M = 256, N = 256, K = 32) per K step into its own 256 TMEM
+// columns.  Per K block each CTA loads its 128 rows of A and its 128 rows of
+// each half of B: 48 KB for 128 x 512 x 128 products, a quarter fewer bytes
+// per product than the 256x256 pair tile (32 KB for 128 x 256 x 128).  The
+// operand stream into shared memory is what bounds the 256x256 kernel: with
+// B's loads left out (a timing copy, wrong results) it ran 12 % faster at the
+// maximum clock and 15 % faster under the power cap, with no loads at all
+// 21 %.  The accumulator now fills TMEM (512 columns), so there is no second
+// buffer: the epilogue drains the two halves in parallel (warps 4-7 columns
+// 0-255, warps 8-11 columns 256-511) and releases each on its own barrier,
+// and the next tile's first MMA into a half waits only for that half.
+// Protocol otherwise as the 256x256 pair kernel's.
+constexpr int W_BN = 2 * BN;                        // 512 tile columns
+constexpr int W_STAGES = 4;
+constexpr int WA_BYTES = BM * BK;                   // 16 KB: this CTA's A rows
+constexpr int WB_HALF = (BN / 2) * BK;              // 16 KB: its 128 rows of one half of B
+constexpr int WB_BYTES = 2 * WB_HALF;
+constexpr int W_STAGE_BYTES = WA_BYTES + WB_BYTES;  // 48 KB
+constexpr int W_SMEM_BYTES = W_STAGES * W_STAGE_BYTES + 1024 + 256;
+constexpr int W_EPI_WARPS = 8;
+constexpr int W_THREADS = (EPI_WARP0 + W_EPI_WARPS) * 32;   // 384
+
+template <int KIND, int OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W_THREADS, 1)
+gemm_i8_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + W_STAGES * WA_BYTES;
+    struct WBarriers {
+        uint64_t full[W_STAGES];
+        uint64_t empty[W_STAGES];
+        uint64_t acc_full;
+        uint64_t acc_empty[2];   // per 256-column half
+        uint64_t drain;
+        uint32_t tmem_base;
+        int abort;
+    };
+    WBarriers* bars = reinterpret_cast<WBarriers*>(smem + W_STAGES * W_STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
+    const int tiles_n = (p.N + W_BN - 1) / W_BN;
+    const int tiles = tiles_m * tiles_n;
+    const int nk = (p.K * elem_bytes(KIND) + BK - 1) / BK;   // 128-byte K blocks
+    const int pair = blockIdx.x >> 1;
+    const int pairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < W_STAGES; ++s) { mbar_init(&bars->full[s], 1); mbar_init(&bars->empty[s], 1); }
+        mbar_init(&bars->acc_full, 1);
+        for (int h = 0; h < 2; ++h) mbar_init(&bars->acc_empty[h], 2 * (W_EPI_WARPS / 2));
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 2) {
+        tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+    volatile int* abort_flag = &bars->abort;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------ producer (both CTAs)
+        uint32_t stage = 0, phase = 0;
+        uint32_t armed = 0, armed_phase = 0;
+        bool ok = true;
+        for (int t = pair; t < tiles && ok; t += pairs) {
+            int mt, nt;
+            tile_coords<group_m(KIND)>(t, tiles_m, tiles_n, mt, nt);
+            for (int kb = 0; kb < nk; ++kb) {
+                if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort_flag, p.status, SITE_PRODUCER, p.wait_ns)) { ok = false; break; }
+                if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * W_STAGE_BYTES);
+                const uint32_t full_leader = mapa_shared(smem_u32(&bars->full[stage]), 0);
+                tma_load_2d_pair(sA + stage * WA_BYTES, &tmA, full_leader, kb * BK, mt * 2 * BM + (int)rank * BM);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    tma_load_2d_pair(sB + stage * WB_BYTES + h * WB_HALF, &tmB, full_leader, kb * BK,
+                                     nt * W_BN + h * BN + (int)rank * (BN / 2));
+                armed |= 1u << stage;
+                armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+        if (!ok && leader) {
+            // copies of both CTAs complete on these barriers: let them land
+            for (int s = 0; s < W_STAGES; ++s)
+                if (armed & (1u << s)) mbar_wait(&bars->full[s], (armed_phase >> s) & 1u, nullptr, nullptr, 0);
+        }
+    } else if (warp == 1 && lane == 0 && leader) {
+        // ------------------------------------------------------------ MMA issuer (even CTA)
+        constexpr uint32_t IDESC = kind_idesc(KIND, 2 * BM, BN);
+        uint32_t stage = 0, phase = 0;
+        bool ok = true, issued = false;
+        int iter = 0;
+        for (int t = pair; t < tiles && ok; t += pairs, ++iter) {
+            const uint32_t acc_phase = iter & 1;
+            for (int kb = 0; kb < nk && ok; ++kb) {
+                if (!mbar_wait(&bars->full[stage], phase, abort_flag, p.status, SITE_MMA_FULL, p.wait_ns)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(sA + stage * WA_BYTES);
+                const uint32_t b_addr = smem_u32(sB + stage * WB_BYTES);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (kb == 0) {   // this half of the accumulator drained by the previous tile's epilogue
+                        if (!mbar_wait(&bars->acc_empty[h], acc_phase ^ 1u, abort_flag, p.status, SITE_MMA_TMEM, p.wait_ns)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                    }
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k)
+                        umma_kind_pair<KIND>(tmem_base + h * BN, make_sdesc_kmajor_sw128(a_addr + k * UMMA_K),
+                                             make_sdesc_kmajor_sw128(b_addr + h * WB_HALF + k * UMMA_K), IDESC,
+                                             (kb | k) != 0 ? 1u : 0u);
+                    issued = true;
+                }
+                if (!ok) break;
+                const uint32_t e = smem_u32(&bars->empty[stage]);
+                umma_commit_pair(mapa_shared(e, 0));
+                umma_commit_pair(mapa_shared(e, 1));
+                if (++stage == W_STAGES) { stage = 0; phase ^= 1u; }
+            }
+            if (ok) {
+                const uint32_t f = smem_u32(&bars->acc_full);
+                umma_commit_pair(mapa_shared(f, 0));
+                umma_commit_pair(mapa_shared(f, 1));
+            }
+        }
+        if (!ok && issued) {
+            umma_commit_pair(mapa_shared(smem_u32(&bars->drain), 0));
+            mbar_wait(&bars->drain, 0, nullptr, nullptr, 0);
+        }
+    } else if (warp >= EPI_WARP0) {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int ew = warp - EPI_WARP0;
+        const int h = ew >> 2;                  // column half
+        const int q = warp & 3;                 // TMEM lane quarter (a warp reaches lanes 32 (warp % 4) ..)
+        const int row = q * 32 + lane;
+        const bool fold = p.chk.record != nullptr || p.chk.expect != nullptr;
+        int iter = 0;
+        for (int t = pair; t < tiles; t += pairs, ++iter) {
+            int mt, nt;
+            tile_coords<group_m(KIND)>(t, tiles_m, tiles_n, mt, nt);
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(&bars->acc_full, iter & 1, abort_flag, p.status, SITE_EPI, p.wait_ns) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const int m = mt * 2 * BM + (int)rank * BM + row;
+            const bool row_ok = m < p.M;
+            const int n0 = nt * W_BN + h * BN;
+            const float sam = (KIND == KIND_I8 && OUT != QG_OUT_S32 && row_ok) ? __ldg(p.sa + m) : 0.0f;
+            uint32_t ck = 0, ofp = 0;
+            const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + h * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld_32x32b_x32(t_row + c, r);
+                tmem_ld_wait_regs(r);
+                epilogue_chunk<KIND, OUT>(r, m, n0 + c, row_ok, sam, p, ck, fold, ofp);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&bars->acc_empty[h]), 0));
+            if (p.row_cksum && row_ok) atomicAdd(p.row_cksum + m, ck);
+            // this half is one 256-column fingerprint segment of the row
+            if (fold) check_segment(p.chk, row_ok && n0 < p.N, seg_index(m, 2 * nt + h, p.N), ck + ofp);
+        }
+    }
+
+    // the even CTA's MMAs read this CTA's shared memory and write its TMEM:
+    // neither CTA frees anything before both are done
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
+        if (lane == 0 && *abort_flag) atomicAdd(&p.status->drained, 1u);   // gave up, drained, TMEM freed
+    }
+}
 template <int KIND, int OUT>
 static int launch(const void* A, const void* B, const float* sa, const float* sb, float alpha, void* C,
                   uint32_t* cksum, int M, int N, int K, cudaStream_t stream, const LaunchCheck& chk = LaunchCheck{},
@@ -608,6 +804,8 @@ static int launch(const void* A, const void* B, const float* sa, const float* sb
         QG_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<KIND, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         QG_CUDA(cudaFuncSetAttribute(gemm_i8_pair_kernel<KIND, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      P_SMEM_BYTES));
+        QG_CUDA(cudaFuncSetAttribute(gemm_i8_wide_kernel<KIND, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     W_SMEM_BYTES));
         attr_set[dev & 63] = true;
     }
     if (cksum) QG_CUDA(cudaMemsetAsync(cksum, 0, sizeof(uint32_t) * (size_t)M, stream));
@@ -619,21 +817,33 @@ static int launch(const void* A, const void* B, const float* sa, const float* sb
         if ((rc = make_tmap_2d(&tmBh, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, kb, (uint64_t)N, kb, BK, BN / 2,
                                CU_TENSOR_MAP_SWIZZLE_128B)))
             return rc;
-        const int tiles2 = ceil_div(M, 2 * BM) * ceil_div(N, BN);
         // persistent pairs: only as many as can be resident at once (a pair needs
         // two free SMs of one GPC, so this can be below sm_count / 2)
-        static int resident[64] = {};
-        if (!resident[dev & 63]) {
+        // 256x512 tiles for the 2- and 4-byte kinds wider than 256 columns
+        // (8192^3, burst / ~1 s at the power cap: BF16 +4.8 / +4.7 %, FP16
+        // +5.3 / +4.6 %, TF32 +7.0 / +10 %).  The 1-byte kinds keep 256x256:
+        // their MMA is twice as fast per K byte, so the single accumulator
+        // buffer's drain between tiles weighs twice as much (E4M3 -0.9 %), and
+        // INT8's epilogue (checksum, dequant, fingerprint: ~9 instructions per
+        // element, ~4.6k cycles per 128x512 drain) more still (-1.5 % at the
+        // maximum clock, -9 % per clock under the power cap).
+        const bool wide = elem_bytes(KIND) >= 2 && N > BN;
+        static int resident[64][2] = {};
+        int& res = resident[dev & 63][wide ? 1 : 0];
+        if (!res) {
             cudaLaunchConfig_t lc = {};
             lc.gridDim = dim3(info->sm_count & ~1);
-            lc.blockDim = dim3(THREADS);
-            lc.dynamicSmemBytes = P_SMEM_BYTES;
+            lc.blockDim = dim3(wide ? W_THREADS : THREADS);
+            lc.dynamicSmemBytes = wide ? W_SMEM_BYTES : P_SMEM_BYTES;
             int n = 0;
-            QG_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_i8_pair_kernel<KIND, OUT>, &lc));
-            resident[dev & 63] = n > 0 ? n : 1;
+            if (wide) QG_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_i8_wide_kernel<KIND, OUT>, &lc));
+            else QG_CUDA(cudaOccupancyMaxActiveClusters(&n, gemm_i8_pair_kernel<KIND, OUT>, &lc));
+            res = n > 0 ? n : 1;
         }
-        const int pairs = tiles2 < resident[dev & 63] ? tiles2 : resident[dev & 63];
-        gemm_i8_pair_kernel<KIND, OUT><<<2 * pairs, THREADS, P_SMEM_BYTES, stream>>>(tmA, tmBh, p);
+        const int tiles2 = ceil_div(M, 2 * BM) * ceil_div(N, wide ? W_BN : BN);
+        const int pairs = tiles2 < res ? tiles2 : res;
+        if (wide) gemm_i8_wide_kernel<KIND, OUT><<<2 * pairs, W_THREADS, W_SMEM_BYTES, stream>>>(tmA, tmBh, p);
+        else gemm_i8_pair_kernel<KIND, OUT><<<2 * pairs, THREADS, P_SMEM_BYTES, stream>>>(tmA, tmBh, p);
         QG_CUDA(cudaGetLastError());
         return QG_OK;
     }
