@@ -91,9 +91,9 @@ def workload_spec(name: str, m: int = 0):
         m = m or 1
         return {"name": "w4a16", "fmt": pb.QG_FMT_W4A16, "shape": (m, 28672, 8192), "copies": 4, "seed": 3,
                 "unit": "GB/s", "bound": "hbm", "dtype": "bf16 x int4 (fp32 acc)",
-                # per 16-row chunk: one launch (1 row: CUDA cores; 2-8 rows: warp MMAs), or the X
-                # pre-pass + the tcgen05 GEMV (9-16 rows)
-                "launches_per_step": sum(2 if min(16, m - m0) >= 9 else 1 for m0 in range(0, m, 16)),
+                # per 16-row chunk: one launch (1 row: CUDA cores; 2-12 rows: warp MMAs), or the X
+                # pre-pass + the tcgen05 GEMV (13-16 rows)
+                "launches_per_step": sum(2 if min(16, m - m0) >= 13 else 1 for m0 in range(0, m, 16)),
                 "traffic_key": f"gemv_w4a16_m{m}",
                 "config": {"workload": f"configs[3] W4A16 group-128 GEMV M={m} K=8192 N=28672, bf16 out",
                            "M": m, "N": 28672, "K": 8192, "seed": 3, "operand_sets": 4,

@@ -116,7 +116,7 @@ QG_API int  qg_golden(qg_ctx* ctx);
  * and the dense tensor formats, 128 for FP8 and NVFP4; INT8 also folds its
  * INT32 accumulators) into a fingerprint and compares it with the one the
  * golden launch recorded; the GEMV compares every output word it writes with
- * the golden output (9-16 rows: per-column fingerprints, like the GEMMs).
+ * the golden output (13-16 rows: per-column fingerprints, like the GEMMs).
  * Differences are counted on the device for qg_verify, so a corruption in any
  * launch of a batch is seen, not only in the last.  W4A16 launches after the
  * first pass QG_GEMV_WEIGHTS_CONST | QG_GEMV_ACTIVATIONS_CONST: the kernel
@@ -271,8 +271,8 @@ QG_API int  qg_gemm_nvfp4(const void* A, const void* sfa, const void* B, const v
                           float ga, float gb, void* C, int out_type, int M, int N, int K, void* stream);
 QG_API int  qg_nvfp4_sf_bytes(int rows, int K, uint64_t* bytes);
 
-/* W4A16 group-128 decode GEMV / skinny GEMM (1 row on the CUDA cores, 2-8
- * rows on warp MMAs, 9-16 rows on tcgen05, more rows in chunks of 16):
+/* W4A16 group-128 decode GEMV / skinny GEMM (1 row on the CUDA cores, 2-12
+ * rows on warp MMAs, 13-16 rows on tcgen05, more rows in chunks of 16):
  *   Y[m,n] = sum_k X[m,k] * (q[k,n] - Z[k/128,n]) * S[k/128,n],  q = u - 8
  *   X bf16 [M,K]; W uint32 [K/8, N] with nibble j of word (k8, n) = u(8*k8+j, n)
  *   in [0,15]; S, Z fp16 [K/128, N]; Y bf16 or fp32 [M,N] (out_type).
@@ -291,7 +291,7 @@ QG_API int  qg_gemv_w4a16(const void* X, const void* W, const void* S, const voi
 
 /* qg_gemv_w4a16 with flags.  QG_GEMV_WEIGHTS_CONST: the kernel that precedes
  * this call on `stream` does not write W, S or Z (a decode loop over fixed
- * weights, e.g. the previous GEMV call); the 1-row and 2-8-row kernels then
+ * weights, e.g. the previous GEMV call); the 1-row and 2-12-row kernels then
  * issue their first weight loads before waiting for that kernel to finish,
  * overlapping the previous call's tail.  Other bits are rejected with
  * QG_ERR_ARG.
@@ -300,8 +300,8 @@ QG_API int  qg_gemv_w4a16(const void* X, const void* W, const void* S, const voi
 /* QG_GEMV_ACTIVATIONS_CONST: the kernel that precedes this call on `stream`
  * does not write X (a loop of GEMVs over one activation set, such as the
  * workload's timed loop; not a decode step, whose X the layer before just
- * wrote).  The 2-8-row kernel then quantises its activations before waiting
- * for that kernel, overlapping the previous call's tail; the 9-16-row path's
+ * wrote).  The 2-12-row kernel then quantises its activations before waiting
+ * for that kernel, overlapping the previous call's tail; the 13-16-row path's
  * pre-pass quantises them before its wait (and stores them after it); and the
  * 1-row kernel, when QG_GEMV_WEIGHTS_CONST is set too, stages its
  * activations, scales and zero points before the wait.  Either, both or

@@ -12,9 +12,9 @@
 //           rounds away in bf16 still shows -- and, in the golden launch,
 //           records it; in every later launch it compares it with the recorded
 //           one;
-//   GEMV    the CUDA-core (1 row) and warp-MMA (2-8 rows) kernels compare each
+//   GEMV    the CUDA-core (1 row) and warp-MMA (2-12 rows) kernels compare each
 //           output word they write with the golden output; the tcgen05 kernel
-//           (9-16 rows) folds the words of each output column into a
+//           (13-16 rows) folds the words of each output column into a
 //           fingerprint, recorded by
 //           the golden launch and compared by later launches, with the
 //           expected value loaded when the column's tile starts (a compare at

@@ -1,6 +1,6 @@
 // qg_gemv.cuh -- what the three W4A16 GEMV kernels share: the SM count their
-// work split is sized for, and the entries of the tcgen05 kernel (9..16
-// activation rows) and the warp-MMA kernel (2..8 rows), used by the C entry
+// work split is sized for, and the entries of the tcgen05 kernel (13..16
+// activation rows) and the warp-MMA kernel (2..12 rows), used by the C entry
 // points in qg_gemv_w4a16.cu.
 #pragma once
 

@@ -1,6 +1,6 @@
 // qg_gemv_w4a16.cu -- weight-only W4A16 group-128 decode GEMV: the C entry
 // points, and the CUDA-core kernel for the single-row decode step
-// (bandwidth-bound).  2-8 rows run on warp MMAs (qg_gemv_w4a16_mma.cu), 9-16
+// (bandwidth-bound).  2-12 rows run on warp MMAs (qg_gemv_w4a16_mma.cu), 13-16
 // on tcgen05 (qg_gemv_w4a16_tc.cu); larger M is processed 16 rows at a time.
 //
 //   Y[m, n] = sum_k X[m, k] * (q[k, n] - Z[k/128, n]) * S[k/128, n],  q = u - 8
@@ -396,15 +396,15 @@ static size_t smem_bytes(int mt, int K, int splits) { return smem_bytes_len(mt, 
 
 // Row chunks of up to 16 rows, each on the kernel that is fastest for its
 // row count (configs[3] shape, per call): 1 row on the CUDA cores (this file;
-// the decode step), 2-8 on register-fed warp MMAs (qg_gemv_w4a16_mma.cu:
-// 25.1 us at 2 rows against 33.9 us here, where the dp2a work doubles), 9-16
-// on the tcgen05 tensor cores (qg_gemv_w4a16_tc.cu).  At 9-16 rows the warp
-// MMAs would need 8 m16n8k32 per 32 x 32 weight tile (two activation digits
-// x 16 rows) at 0.5 per clock per SM, ~3/4 of the weight stream's time in the
-// MMA pipe alone; one tcgen05 M=128 N=32 K=32 MMA does 8x that work in ~45
-// cycles.
+// the decode step), 2-12 on register-fed warp MMAs (qg_gemv_w4a16_mma.cu:
+// 25.1 us at 2 rows against 33.9 us here, where the dp2a work doubles; 33.0
+// us at 12 rows against 43.2 on tcgen05), 13-16 on the tcgen05 tensor cores
+// (qg_gemv_w4a16_tc.cu).  At 16 rows the warp MMAs need 8 m16n8k32 per
+// 32 x 32 weight tile (two activation digits x 16 rows) at 0.5 per clock per
+// SM, ~3/4 of the weight stream's time in the MMA pipe alone, and a 16-row
+// build of that kernel only tied the tcgen05 one (43.4 us each).
 constexpr int kMmaMinRows = 2;
-constexpr int kTcMinRows = 9;
+constexpr int kTcMinRows = 13;
 
 enum class Path { kCudaCore, kMma, kTc };
 static Path path_for(int mrows) {

@@ -1,4 +1,4 @@
-// qg_gemv_w4a16_mma.cu -- W4A16 group-128 skinny GEMM for 2..8 activation
+// qg_gemv_w4a16_mma.cu -- W4A16 group-128 skinny GEMM for 2..12 activation
 // rows on register-fed warp MMAs (mma.sync m16n8k32, u8 x s8 -> s32).
 //
 //   Y[m, n] = sum_k X[m, k] * (q[k, n] - Z[k/128, n]) * S[k/128, n],  q = u - 8
@@ -7,7 +7,7 @@
 // (nibble j of word (k8, n) is u(8*k8 + j, n)); S, Z fp16 [K/128, N]; Y bf16
 // or fp32 [M, N].
 //
-// Why warp MMAs.  At 2..8 rows the call is a 117 MB weight stream (configs[3]:
+// Why warp MMAs.  At 2..12 rows the call is a 117 MB weight stream (configs[3]:
 // K = 8192, N = 28672) with M multiply-adds per weight: the FP32 pipes cannot
 // keep up, so the products go to tensor cores, but only ~100 TOPS of them.
 // The warp-level MMA takes both operands from registers, so each weight goes
@@ -15,9 +15,11 @@
 // TMEM round trip, no single issuing thread and no barrier between producer
 // and consumer roles (the tcgen05 kernel, qg_gemv_w4a16_tc.cu, spends most of
 // its time in those hand-offs).  Measured on this part the warp MMA sustains
-// 0.5 m16n8k32 per clock per SM (~1.1 POPS int8).  Past 8 rows the MMA count
-// doubles (below) and the tcgen05 kernel takes over (a 16-row build of this
-// kernel measured 43.7 against 43.3 us at 16 rows, 41.6 against 43.2 at 9).
+// 0.5 m16n8k32 per clock per SM (~1.1 POPS int8).  Each 4 rows add 2 MMAs
+// per lane quad and K step (below); past 12 rows the tcgen05 kernel takes
+// over (per call at configs[3]: 12 rows 33.0 us here against 43.2 there; a
+// 16-row build of this kernel, four fragments, 43.4 against 43.4, and with a
+// 4-deep ring, whose activations no longer fit one wave, 57.3).
 //
 // Integer arithmetic, exact up to the fold -- the same per-group numbers as
 // the tcgen05 kernel:
@@ -45,8 +47,8 @@
 // digit of activation row 4b + r and digit row 2r + 1 its l digit, so the
 // accumulator pair (c0, c1) of lane (g, t) is (C_h, C_l) of activation row
 // 4b + t and one weight column: the fold needs no data exchange between lanes.
-// NB = 1 or 2 B fragments serve up to 4 or 8 rows: 2 NB MMAs per lane quad
-// and K step.
+// NB = 1, 2 or 3 B fragments serve up to 4, 8 or 12 rows: 2 NB MMAs per
+// lane quad and K step.
 //
 // Work split.  A super-tile is 512 columns (16 warps x 32); an iteration is one
 // (super-tile, group) pair, and the iterations, super-tile-major, are cut into
@@ -87,15 +89,17 @@ constexpr int SMEM_BUDGET = 227 * 1024;
 
 template <int NB>
 struct Cfg {
-    static_assert(NB == 1 || NB == 2, "1 or 2 B fragments");
+    static_assert(NB >= 1 && NB <= 3, "1 to 3 B fragments");
     static constexpr int MR = 4 * NB;                        // activation rows, padded
     static constexpr int XF_STEP = NB * 256;                 // B fragments of one K step
     static constexpr int XS_OFF = STEPS * XF_STEP;           // then per (t, b): {2^e, sum xi, 8 sum xi, 0}
     static constexpr int XG = XS_OFF + 4 * NB * 16;          // prepared bytes per group
     // Weight ring depth per warp (groups copied ahead of the one computed).
     // Measured at configs[3]: 3 instead of 5 at one fragment cost 2 %, 5
-    // instead of 4 at two fragments 2 % too (fewer registers for the rest).
-    static constexpr int RING = NB == 2 ? 4 : 5;
+    // instead of 4 at two fragments 2 % too (fewer registers for the rest);
+    // at three fragments 3 measured 1 % faster than 4 and leaves room to
+    // stage the activations of a CTA's whole range (one wave).
+    static constexpr int RING = NB == 1 ? 5 : (NB == 2 ? 4 : 3);
     static constexpr int RING_BYTES = WARPS * RING * SLOT;
     static constexpr int XMAX = (SMEM_BUDGET - RING_BYTES) / XG;   // groups of activations a CTA can stage
     static_assert(XG % 16 == 0 && RING_BYTES % 16 == 0, "16-byte copies");
@@ -103,11 +107,12 @@ struct Cfg {
 };
 
 // Byte offset of lane `lane`'s 8 bytes of B fragment b inside one K step.
-// With two fragments a lane reads both with one 16-byte load, and 32 lanes x
-// 16 bytes are contiguous (no bank conflicts).
+// Fragments go in pairs: a lane reads both of a pair with one 16-byte load,
+// and 32 lanes x 16 bytes are contiguous (no bank conflicts); an odd last
+// fragment follows as 32 lanes x 8 bytes.
 template <int NB>
 __host__ __device__ __forceinline__ int frag_offset(int b, int lane) {
-    return NB == 1 ? lane * 8 : lane * 16 + b * 8;
+    return (NB & 1) && b == NB - 1 ? (NB - 1) * 256 + lane * 8 : (b >> 1) * 512 + lane * 16 + (b & 1) * 8;
 }
 
 struct Params {
@@ -473,13 +478,15 @@ gemv_w4a16_mma_kernel(Params p) {
                 const uint32_t a1[4] = {w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu};
                 const uint8_t* xf = xg + s * C::XF_STEP;
                 uint32_t bf[NB][2];
-                if constexpr (NB == 1) {
-                    const uint2 v = *reinterpret_cast<const uint2*>(xf + lane * 8);
-                    bf[0][0] = v.x; bf[0][1] = v.y;
-                } else {
-                    const uint4 v = *reinterpret_cast<const uint4*>(xf + lane * 16);
-                    bf[0][0] = v.x; bf[0][1] = v.y;
-                    bf[1][0] = v.z; bf[1][1] = v.w;
+    #pragma unroll
+                for (int b = 0; b + 1 < NB; b += 2) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(xf + frag_offset<NB>(b, lane));
+                    bf[b][0] = v.x; bf[b][1] = v.y;
+                    bf[b + 1][0] = v.z; bf[b + 1][1] = v.w;
+                }
+                if constexpr (NB & 1) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(xf + frag_offset<NB>(NB - 1, lane));
+                    bf[NB - 1][0] = v.x; bf[NB - 1][1] = v.y;
                 }
     #pragma unroll
                 for (int b = 0; b < NB; ++b) {
@@ -557,7 +564,7 @@ static Shape shape_of(int N, int K) {
     return s;
 }
 
-static int nb_for(int mrows) { return mrows <= 4 ? 1 : 2; }
+static int nb_for(int mrows) { return (mrows + 3) / 4; }   // B fragments for 1..12 rows
 
 template <int NB>
 static int launch(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
@@ -603,7 +610,7 @@ static int launch(const void* X, const void* W, const void* S, const void* Z, vo
 uint64_t gemv_w4a16_mma_partial_bytes(int mrows, int N, int K) {
     using namespace w4mma;
     const int nb = nb_for(mrows);
-    const int maxp = nb == 1 ? shape_of<1>(N, K).maxp : shape_of<2>(N, K).maxp;
+    const int maxp = nb == 1 ? shape_of<1>(N, K).maxp : nb == 2 ? shape_of<2>(N, K).maxp : shape_of<3>(N, K).maxp;
     const uint64_t nst = (uint64_t)((N + ST_COLS - 1) / ST_COLS);
     return maxp == 1 ? 0 : nst * maxp * WARPS * 32 * 4 * nb * 4;
 }
@@ -613,11 +620,12 @@ uint64_t gemv_w4a16_mma_ticket_count(int N) { return (uint64_t)((N + w4mma::ST_C
 int gemv_w4a16_mma(const void* X, const void* W, const void* S, const void* Z, void* Y, int out_type, int mrows, int N,
                    int K, float* partials, unsigned int* tickets, unsigned int flags, cudaStream_t stream,
                    const void* golden, unsigned long long* check_count) {
-    QG_CHECK_ARG(mrows >= 1 && mrows <= 8, "gemv_w4a16_mma: %d rows (1..8)", mrows);
+    QG_CHECK_ARG(mrows >= 1 && mrows <= 12, "gemv_w4a16_mma: %d rows (1..12)", mrows);
     QG_CHECK_ARG(((uintptr_t)partials & 15) == 0, "gemv_w4a16_mma: the partial sums must be 16-byte aligned");
     switch (w4mma::nb_for(mrows)) {
         case 1: return w4mma::launch<1>(X, W, S, Z, Y, out_type, mrows, N, K, partials, tickets, flags, stream, golden, check_count);
-        default: return w4mma::launch<2>(X, W, S, Z, Y, out_type, mrows, N, K, partials, tickets, flags, stream, golden, check_count);
+        case 2: return w4mma::launch<2>(X, W, S, Z, Y, out_type, mrows, N, K, partials, tickets, flags, stream, golden, check_count);
+        default: return w4mma::launch<3>(X, W, S, Z, Y, out_type, mrows, N, K, partials, tickets, flags, stream, golden, check_count);
     }
 }
 

@@ -1,7 +1,7 @@
 // qg_gemv_w4a16_tc.cu -- W4A16 group-128 skinny GEMM for up to 16 activation
 // rows on the sm_100a tensor cores (tcgen05.mma kind::i8, A operand in TMEM);
-// the GEMV entry routes 9..16 rows here (2..8 rows run faster on register-fed
-// warp MMAs, qg_gemv_w4a16_mma.cu).
+// the GEMV entry routes 13..16 rows here (2..12 rows run faster on
+// register-fed warp MMAs, qg_gemv_w4a16_mma.cu).
 //
 //   Y[m, n] = sum_k X[m, k] * (q[k, n] - Z[k/128, n]) * S[k/128, n],  q = u - 8
 //
@@ -9,11 +9,11 @@
 // W uint32 [K/8, N] (nibble j of word (k8, n) is u(8*k8 + j, n)); S, Z fp16
 // [K/128, N]; Y bf16 or fp32 [M, N].
 //
-// At 9-16 rows a CUDA-core GEMV needs M FMAs per weight (3.8 GFMA per call at
+// At 13-16 rows a CUDA-core GEMV needs M FMAs per weight (3.8 GFMA per call at
 // M = 16, >= 100 us on the FP32 pipes against ~19 us of HBM time), and warp
 // MMAs need twice the MMA count of 8 rows (two activation digits x 16 rows =
-// 8 m16n8k32 per 32 x 32 weight tile), so the products go to tcgen05 with the
-// weights as the MMA's M side:
+// 8 m16n8k32 per 32 x 32 weight tile; a 16-row warp-MMA build tied this
+// kernel), so the products go to tcgen05 with the weights as the MMA's M side:
 // D[n, r] = sum_k Wt[n, k] * B[r, k], M = 128 weight columns, N = 32 rows.
 //
 // Integer arithmetic, exact up to the fold (the CUDA-core path's numerics):

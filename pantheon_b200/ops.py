@@ -195,7 +195,7 @@ def gemv_w4a16_workspace_bytes(M: int, N: int, K: int) -> int:
 def gemv_w4a16(X: torch.Tensor, W: torch.Tensor, S: torch.Tensor, Z: torch.Tensor, out_type: int = QG_OUT_BF16,
                workspace: torch.Tensor | None = None, out: torch.Tensor | None = None,
                weights_const: bool = False, activations_const: bool = False) -> torch.Tensor:
-    """Y = X @ dequant(W) on the W4A16 path (1 row CUDA cores, 2-8 warp MMAs, 9-16 tcgen05).
+    """Y = X @ dequant(W) on the W4A16 path (1 row CUDA cores, 2-12 warp MMAs, 13-16 tcgen05).
 
     X bf16 [M,K]; W int32/uint32 [K/8,N] packed int4 (nibble j = k offset j);
     S, Z fp16 [K/128,N]; returns Y [M,N] (bf16 or fp32).  `workspace` (uint8,

@@ -27,6 +27,7 @@ CASES = [
     ("e4m3", (256, 512, 256), 0, 0, 6),
     ("w4a16_m1", (1, 4096, 2048), 0, 1, 6),         # CUDA-core GEMV
     ("w4a16_m8", (8, 4096, 2048), 0, 1, 6),         # warp-MMA GEMV
+    ("w4a16_m12", (12, 4096, 2048), 0, 1, 6),       # warp-MMA GEMV, three B fragments
     ("w4a16_m16", (16, 4096, 2048), 0, 1, 6),       # tcgen05 GEMV
 ]
 
@@ -35,7 +36,7 @@ def _fmt(name):
     import pantheon_b200 as pb
     return {"int8": pb.QG_FMT_INT8, "int8_pair": pb.QG_FMT_INT8, "fp8": pb.QG_FMT_FP8, "nvfp4": pb.QG_FMT_NVFP4,
             "bf16": pb.QG_FMT_BF16, "e4m3": pb.QG_FMT_E4M3, "w4a16_m1": pb.QG_FMT_W4A16,
-            "w4a16_m8": pb.QG_FMT_W4A16, "w4a16_m16": pb.QG_FMT_W4A16}[name]
+            "w4a16_m8": pb.QG_FMT_W4A16, "w4a16_m12": pb.QG_FMT_W4A16, "w4a16_m16": pb.QG_FMT_W4A16}[name]
 
 
 @pytest.mark.parametrize("name,shape,slot,byte,bit", CASES, ids=[c[0] for c in CASES])

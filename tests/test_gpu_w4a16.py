@@ -1,4 +1,4 @@
-"""W4A16 group-128 GEMV (1 row on the CUDA cores, 2-8 on warp MMAs, 9-16 on
+"""W4A16 group-128 GEMV (1 row on the CUDA cores, 2-12 on warp MMAs, 13-16 on
 tcgen05): parity with the CPU oracle, through the C ABI.
 
 X bf16 [M in {1,8,16}, 8192] ~ N(0,1); W int4 [8192, 28672] uniform in
@@ -40,10 +40,10 @@ def test_generator_matches_oracle(cuda_device, oracle):
     np.testing.assert_array_equal(_np(Z.view(torch.int16)).view(np.uint16), rZ)
 
 
-# 1 row runs on the CUDA cores, 2-8 on warp MMAs, 9-16 on tcgen05, more in chunks of 16
+# 1 row runs on the CUDA cores, 2-12 on warp MMAs, 13-16 on tcgen05, more in chunks of 16
 SHAPES = [(1, 512, 128), (1, 1028, 1024), (3, 2048, 2048), (8, 4096, 1024), (16, 1536, 4096),
           (17, 516, 256), (5, 28672, 256), (4, 300, 384), (12, 1028, 1024), (8, 128, 8192), (16, 36, 128),
-          (34, 260, 512)]
+          (34, 260, 512), (9, 2052, 1024), (13, 1028, 1024), (11, 36, 128)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
@@ -61,9 +61,11 @@ def test_gemv_matches_oracle(cuda_device, oracle, shape):
 
 # configs[3] at M = 1, 8, 16, each row-count boundary of the three kernels, and
 # shapes whose warp-MMA grid runs in two waves (more groups per CTA than its
-# shared memory can hold at once in one wave): 8 x 57344 x 8192, 4 x 65536 x 8192.
+# shared memory can hold at once in one wave): 8 x 57344 x 8192, 4 x 65536 x 8192,
+# 12 x 57344 x 8192.
 FULL = [(1, 28672, 8192), (2, 28672, 8192), (3, 28672, 8192), (4, 28672, 8192), (5, 28672, 8192),
-        (8, 28672, 8192), (9, 28672, 8192), (16, 28672, 8192), (8, 57344, 8192), (4, 65536, 8192)]
+        (8, 28672, 8192), (9, 28672, 8192), (12, 28672, 8192), (13, 28672, 8192), (16, 28672, 8192),
+        (8, 57344, 8192), (4, 65536, 8192), (12, 57344, 8192)]
 
 
 @pytest.mark.parametrize("shape", FULL, ids=lambda s: "x".join(map(str, s)))
@@ -86,7 +88,7 @@ def test_full_size_config3(cuda_device, oracle, shape):
         assert pb.device_status(0) == 0
 
 
-@pytest.mark.parametrize("M", [1, 2, 8])
+@pytest.mark.parametrize("M", [1, 2, 8, 12, 16])
 @pytest.mark.parametrize("flags", ["weights", "activations", "both"])
 def test_const_flags_are_bit_identical(cuda_device, oracle, M, flags):
     """QG_GEMV_WEIGHTS_CONST / QG_GEMV_ACTIVATIONS_CONST only move the first weight loads
@@ -103,7 +105,7 @@ def test_const_flags_are_bit_identical(cuda_device, oracle, M, flags):
     assert oracle.max_rel_err(_np(ref), oracle.gemv_w4a16(*host, out_type=1), 1) < 1e-4
 
 
-@pytest.mark.parametrize("M", [2, 8])
+@pytest.mark.parametrize("M", [2, 8, 12])
 def test_workspace_reusable_and_checked(cuda_device, oracle, M):
     N, K = 2048, 2048
     host, dev = _operands(oracle, M, N, K, seed=1, dev=cuda_device)
