@@ -35,7 +35,7 @@ def _bf16_bits(t):
     return t.view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-@pytest.mark.parametrize("M", [1, 8, 16])   # CUDA cores; warp MMAs; tcgen05
+@pytest.mark.parametrize("M", [1, 8, 12, 16])   # CUDA cores; warp MMAs (two, three B fragments); tcgen05
 def test_noalloc_matches_workspace_entry_point_twice(cuda_device, oracle, qglib, M):
     N, K = 28672, 8192                       # configs[3]
     X, W, S, Z = pb.gen_w4a16(M, N, K, seed=21 + M)
@@ -59,7 +59,7 @@ def test_noalloc_after_calls_of_other_shapes(cuda_device, qglib, out_type):
     the output of the workspace entry point with a fresh zeroed workspace."""
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     for M, N, K in [(16, 28672, 8192), (1, 4096, 2048), (8, 28672, 8192), (24, 4096, 4096), (2, 28672, 8192),
-                    (16, 28672, 8192)]:
+                    (12, 28672, 8192), (28, 4096, 2048), (16, 28672, 8192)]:
         X, W, S, Z = pb.gen_w4a16(M, N, K, seed=100 + M + N)
         ref = pb.gemv_w4a16(X, W, S, Z, out_type=out_type)
         y = torch.full_like(ref, float("nan"))
