@@ -33,6 +33,9 @@ Printed by rank 0, one JSON line:
             configs[4] NVFP4 16384^3, each with its device-timed value,
             roofline, clocks and mismatch count; at N > 1 each also lists every
             rank's rate and mismatch count ("per_rank").
+  golden_digest  the digest of the golden result (qg_golden_digest); at N > 1
+            "golden_digests" lists every rank's and whether they agree (the same
+            seed gives the same golden result on every healthy GPU).
 Multi-GPU: one process per GPU (torchrun), each an independent instance with
 no data-path collective ("scaling": "weak"); NCCL carries only the barrier,
 the max of the timings and the per-rank figures.
@@ -473,6 +476,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     w = pb.Workload(wl["fmt"], *wl["shape"], copies=wl["copies"], seed=wl["seed"], device=local_rank)
     w.fill(wl["seed"])
     w.golden()
+    digest = w.golden_digest(0)   # the same on every healthy GPU: compared across ranks below
     stream = torch.cuda.current_stream(dev)
     ops = w.ops_per_launch
     nbytes = w.bytes_per_launch
@@ -515,6 +519,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     del host_ops
 
     ms_max, e2e_max, mm_max, bad = max_over_ranks([ms, e2e_ms, float(mismatches), float(status != 0)], world, dev)
+    # each rank's golden digest, as two exact 32-bit halves
+    digests = [(int(hi) << 32) | int(lo) for hi, lo in gather_over_ranks([digest >> 32, digest & 0xFFFFFFFF], world, dev)]
     peaks = _peaks()
     secondary = None
     if not args.no_secondary and args.workload == "int8":
@@ -538,7 +544,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "gpu_launches": steps * wl["launches_per_step"],
             "mismatches": int(mm_max),
             "device_timeouts": int(bad),
+            "golden_digest": f"0x{digests[0]:016x}",
         }
+        if world > 1:
+            # identical seeds give identical golden results: a rank that differs computed a wrong one
+            result["golden_digests"] = {"agree": len(set(digests)) == 1,
+                                        "per_rank": [f"0x{d:016x}" for d in digests]}
         if secondary is not None:
             result["secondary"] = secondary
         if world == 1 and not args.no_cpu_baseline and wl["name"] == "int8":

@@ -140,6 +140,20 @@ QG_API int  qg_verify(qg_ctx* ctx, uint64_t* mismatches);
 QG_API int  qg_verify_detail(const qg_ctx* ctx, uint64_t* words, uint64_t* launch_diffs,
                              uint64_t* launches_checked);
 
+/* A 64-bit digest of copy `copy`'s golden result (after qg_golden): the sum
+ * mod 2^64 of splitmix64(i * 0x9E3779B97F4A7C15 + w_i + salt) over the golden
+ * output's 32-bit words w_i (salt 0, the output padded to whole words with
+ * zeros) and, for INT8, its golden row checksums (salt 0xC2B2AE3D27D4EB4F).
+ * Processes given the same format, shape, output type and seed compute the
+ * same golden result on every healthy GPU, so the runner can compare the
+ * digests of all GPUs of a run: a GPU whose digest differs from the others'
+ * computed a wrong golden result (a silent data corruption that the per-GPU
+ * compare against its own golden cannot see).  Synchronous.
+ * Replaces: nothing in the reference (its golden never leaves the GPU); it
+ * lets the runner compare the GPUs of one run with each other, with no
+ * collective between them. */
+QG_API int  qg_golden_digest(qg_ctx* ctx, int copy, uint64_t* digest);
+
 /* Flip bit `bit` (0-7) of byte `byte` of operand `slot` (qg_tensor's slots
  * 0..3, or 0..3 of NVFP4's five) of copy `copy`, on `stream`, so the launches
  * that read it compute a wrong result; flipping it again restores the operand.

@@ -51,6 +51,7 @@ _SIGNATURES = {
     "qg_run": (C.c_int, [_V, C.c_int, _V]),
     "qg_verify": (C.c_int, [_V, C.POINTER(C.c_uint64)]),
     "qg_verify_detail": (C.c_int, [_V, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    "qg_golden_digest": (C.c_int, [_V, C.c_int, C.POINTER(C.c_uint64)]),
     "qg_flip_operand_bit": (C.c_int, [_V, C.c_int, C.c_int, C.c_uint64, C.c_int, _V]),
     "qg_mismatch_log": (C.c_int, [_V, C.POINTER(QGMismatch), C.c_int]),
     "qg_inject": (C.c_int, [_V]),

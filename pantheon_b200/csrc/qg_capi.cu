@@ -30,6 +30,9 @@ struct qg_ctx {
 
 namespace {
 
+// Salt of the INT8 row checksums' terms in the golden digest (the output words' is 0).
+constexpr uint64_t kCksumDigestSalt = 0xC2B2AE3D27D4EB4Full;
+
 int fail(qg_ctx* c, int rc) {
     if (c) c->err = qg::last_error();
     return rc;
@@ -248,6 +251,24 @@ int qg_verify(qg_ctx* c, uint64_t* mismatches) {
     c->last_launches = c->launches_checked;
     c->launches_checked = 0;
     *mismatches = h[0] + d;
+    return QG_OK;
+}
+
+int qg_golden_digest(qg_ctx* c, int copy, uint64_t* digest) {
+    QG_CHECK_ARG(c && digest && copy >= 0 && copy < (int)c->copies.size(), "qg_golden_digest: bad argument");
+    QG_CHECK_ARG(c->golden_ready, "qg_golden_digest: no golden result (call qg_golden first)");
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    const qg::CopyBuffers& cp = c->copies[(size_t)copy];
+    // counters[0] is free outside qg_verify
+    CTX_CUDA(c, cudaMemsetAsync(c->counters, 0, sizeof(unsigned long long), c->stream));
+    int rc = qg::digest_words(cp.golden, (c->layout.out_bytes + 3) / 4, 0ull, c->counters, c->stream);
+    if (!rc && c->layout.cksum_bytes)
+        rc = qg::digest_words(cp.golden_cksum, c->layout.cksum_bytes / 4, kCksumDigestSalt, c->counters, c->stream);
+    if (rc) return fail(c, rc);
+    unsigned long long h = 0;
+    CTX_CUDA(c, cudaMemcpyAsync(&h, c->counters, sizeof(h), cudaMemcpyDeviceToHost, c->stream));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    *digest = h;
     return QG_OK;
 }
 

@@ -79,6 +79,8 @@ int gemv_w4a16(const void* X, const void* W, const void* S, const void* Z, void*
                const LaunchCheck& chk = LaunchCheck{}, unsigned int* tickets = nullptr);
 int verify_words(const void* actual, const void* expected, uint64_t nwords, void* counters, void* log, int log_cap,
                  cudaStream_t s);
+// Adds the digest of nwords 32-bit words (qg_verify.cu) to the uint64 at `out`.
+int digest_words(const void* words, uint64_t nwords, uint64_t salt, void* out, cudaStream_t s);
 int flip_bit(void* word, cudaStream_t s);
 int flip_bit_at(void* base, uint64_t byte, int bit, cudaStream_t s);
 

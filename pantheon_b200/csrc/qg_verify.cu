@@ -8,6 +8,7 @@
 // word); and the first `log_cap` mismatches are recorded with their index and
 // both values, as the reference's fault log does (kernels/common/fault_log.h:36-50).
 #include "qg_common.cuh"
+#include "qg_gen.cuh"
 
 namespace qg {
 namespace ver {
@@ -51,6 +52,21 @@ __global__ void verify_words_kernel(const uint32_t* __restrict__ actual, const u
     if ((threadIdx.x & 31) == 0 && warp_total) atomicAdd(&counters[0], (unsigned long long)warp_total);
 }
 
+// Digest of a word array: the sum (mod 2^64) of splitmix64(i * GAMMA + w_i +
+// salt) over the words w_i.  A sum is independent of the order the atomics
+// land in, so the digest is reproducible; each term is a bijection of w_i, so
+// a change of any single word always changes it.
+__global__ void digest_words_kernel(const uint32_t* __restrict__ words, uint64_t nwords, uint64_t salt,
+                                    unsigned long long* out) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    uint64_t local = 0;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nwords; i += stride)
+        local += gen::splitmix64(i * gen::GAMMA + (uint64_t)__ldcs(words + i) + salt);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+    if ((threadIdx.x & 31) == 0 && local) atomicAdd(out, (unsigned long long)local);
+}
+
 __global__ void flip_bit_kernel(uint32_t* word) { word[0] ^= 0x00000080u; }
 
 __global__ void flip_bit_at_kernel(uint8_t* base, uint64_t byte, uint32_t bit) { base[byte] ^= (uint8_t)(1u << bit); }
@@ -73,6 +89,20 @@ int verify_words(const void* actual, const void* expected, uint64_t nwords, void
                                                   static_cast<const uint32_t*>(expected), nwords,
                                                   static_cast<unsigned long long*>(counters),
                                                   static_cast<qg_mismatch*>(log), log_cap);
+    QG_CUDA(cudaGetLastError());
+    return QG_OK;
+}
+
+int digest_words(const void* words, uint64_t nwords, uint64_t salt, void* out, cudaStream_t s) {
+    QG_CHECK_ARG(words && out, "digest_words: null argument");
+    if (nwords == 0) return QG_OK;
+    DeviceInfo* info = nullptr;
+    int rc = current_device_info(&info);
+    if (rc) return rc;
+    const uint64_t need = (nwords + 255) / 256;
+    const uint64_t cap = (uint64_t)info->sm_count * 8;
+    ver::digest_words_kernel<<<(int)(need < cap ? need : cap), 256, 0, s>>>(
+        static_cast<const uint32_t*>(words), nwords, salt, static_cast<unsigned long long*>(out));
     QG_CUDA(cudaGetLastError());
     return QG_OK;
 }

@@ -445,6 +445,15 @@ int main(int argc, char* argv[]) {
         Phase ph("qg:golden");
         if (qg_golden(ctx) != QG_OK || qg_synchronize(ctx) != QG_OK) return fail_ctx(ctx, "qg_golden");
     }
+    {
+        // The same arguments give the same golden result on every healthy GPU:
+        // the runner compares this line across the GPUs of a run.
+        uint64_t digest = 0;
+        if (qg_golden_digest(ctx, 0, &digest) != QG_OK) return fail_ctx(ctx, "qg_golden_digest");
+        char hex[24];
+        snprintf(hex, sizeof(hex), "0x%016llx", (unsigned long long)digest);
+        std::cout << "  -> Golden Digest: " << hex << std::endl;
+    }
 
     // Warm-up, then a timing probe: without --kernel_loops it sizes the batch
     // (~200 ms per sync, as the reference's vendor GEMM batches:

@@ -344,6 +344,13 @@ class Workload:
         self._check("qg_verify_detail", self.lib.qg_verify_detail(self.ctx, C.byref(w), C.byref(d), C.byref(n)))
         return w.value, d.value, n.value
 
+    def golden_digest(self, copy: int = 0) -> int:
+        """64-bit digest of copy `copy`'s golden result (qg_golden_digest): equal on every
+        healthy GPU that ran the same workload with the same seed."""
+        d = C.c_uint64()
+        self._check("qg_golden_digest", self.lib.qg_golden_digest(self.ctx, copy, C.byref(d)))
+        return d.value
+
     def flip_operand_bit(self, copy: int, slot: int, byte: int, bit: int, stream=None):
         """Flip one bit of an operand of copy `copy` on `stream` (a second flip restores it)."""
         s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)

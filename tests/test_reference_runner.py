@@ -106,6 +106,27 @@ def test_hook_turns_an_injected_fault_into_a_fault_verdict(runner):
     assert row[runner_hook.ROW_FIELD] >= 1
 
 
+def test_hook_files_a_golden_digest_outlier_as_a_fault(runner):
+    """Four GPUs run the same clean workload; one reports another golden digest.  Each
+    run passes its own compares, so only the cross-GPU check finds it: after
+    check_golden_digests the runner's own verdict is FAULT for that GPU alone."""
+    run = next(r for r in _runs() if r["case"] == "quantized_gemm_clean")
+    runner_hook.install(runner)
+    rows = []
+    for gpu, digest in enumerate(["0x00c0ffee00c0ffee"] * 3 + ["0x00c0ffee00c0ffef"]):
+        out = run["stdout"].replace("  -> Kernel Loops:", f"  -> Golden Digest: {digest}\n  -> Kernel Loops:")
+        score, unit, status, _, kept = runner.parse_kernel_output(out, run["stderr"], run["returncode"], "quantized_gemm")
+        assert status == "PASS" and f"-> Golden Digest: {digest}" in kept
+        row = runner.build_result_row("quantized_gemm", gpu, 2, 50, score, unit, {}, status=status)
+        row.update(runner_hook.row_fields("quantized_gemm", out))
+        rows.append(row)
+    assert runner.assess_gpu(rows, 3, "NVIDIA B200")["verdict"] != "FAULT"
+    bad = runner_hook.check_golden_digests(rows)
+    assert [r["GPU ID"] for r in bad] == [3]
+    assert runner.assess_gpu(rows, 3, "NVIDIA B200")["verdict"] == "FAULT"
+    assert all(runner.assess_gpu(rows, g, "NVIDIA B200")["verdict"] != "FAULT" for g in range(3))
+
+
 def _dropin_env(monkeypatch, tmp_path):
     monkeypatch.setenv("PANTHEON_BUILD_CACHE_DIR", str(tmp_path / "cache"))
     monkeypatch.setenv("PANTHEON_CUDA_ARCH", "100")

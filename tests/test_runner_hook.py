@@ -59,3 +59,47 @@ def test_binary_prints_the_line_the_hook_reads():
     src = (Path(__file__).resolve().parent.parent / "pantheon_b200" / "csrc" / "quantized_gemm_main.cpp").read_text()
     assert '"  -> Mismatches:    " << mismatches' in src
     assert runner_hook.mismatch_count("  -> Mismatches:    12345") == 12345
+
+
+CLEAN_RUN = """[PANTHEON] GPU 0: Quantized GEMM (INT8 W8A8, sm_100a)
+  -> Working Set:   385 MiB (1 operand copy)
+  -> Golden Digest: 0x{digest}
+Throughput: 2665.02 TOPS
+  -> Mismatches:    0
+Verification: PASS (0 mismatches)
+"""
+
+
+def test_golden_digest_and_row_fields():
+    out = CLEAN_RUN.format(digest="9E3779B97F4A7C15")
+    assert runner_hook.golden_digest(out) == "0x9e3779b97f4a7c15"
+    assert runner_hook.row_fields("quantized_gemm", out) == {"SDC Mismatches": 0, "Golden Digest": "0x9e3779b97f4a7c15"}
+    assert runner_hook.golden_digest("  -> Golden Digest: 0x123\n") is None   # 16 hex digits or nothing
+    assert runner_hook.row_fields("march_test", out) == {}
+    # the runner keeps the line in its log
+    assert "-> Golden Digest: 0x9E3779B97F4A7C15" in parse_kernel_output(out, "", 0, "quantized_gemm")[4]
+
+
+def _rows(test, digests):
+    return [{"Test Name": test, "GPU ID": g, "Status": "PASS", "Golden Digest": d} for g, d in enumerate(digests)]
+
+
+def test_check_golden_digests_majority_and_ties():
+    a, b = "0x" + "a" * 16, "0x" + "b" * 16
+    rows = _rows("quantized_gemm", [a, a, b, a]) + _rows("llm_decode", [a, b]) + _rows("mma_virus", [b, b])
+    rows.append({"Test Name": "quantized_gemm", "GPU ID": 9, "Status": "PASS"})   # no digest: untouched
+    bad = runner_hook.check_golden_digests(rows)
+    # quantized_gemm: GPU 2 is the outlier; llm_decode: two GPUs that differ, neither trusted
+    assert sorted((r["Test Name"], r["GPU ID"]) for r in bad) == [("llm_decode", 0), ("llm_decode", 1),
+                                                                  ("quantized_gemm", 2)]
+    assert all(r["Status"] == "FAIL" and r["Golden Digest Agrees"] is False for r in bad)
+    good = [r for r in rows if r not in bad and "Golden Digest" in r]
+    assert len(good) == 5 and all(r["Status"] == "PASS" and r["Golden Digest Agrees"] is True for r in good)
+    assert "Golden Digest Agrees" not in rows[-1]
+    assert runner_hook.check_golden_digests(_rows("quantized_gemm", [a])) == []   # one GPU agrees with itself
+
+
+def test_binary_prints_the_digest_line_the_hook_reads():
+    from pathlib import Path
+    src = (Path(__file__).resolve().parent.parent / "pantheon_b200" / "csrc" / "quantized_gemm_main.cpp").read_text()
+    assert '"  -> Golden Digest: " << hex' in src and '"0x%016llx"' in src
