@@ -18,6 +18,8 @@ Printed by rank 0, one JSON line:
             (qg_run_copy) and the bf16 result is read back (qg_download);
             steps are pipelined over two device operand sets and three
             streams (upload / launch / read-back overlap across steps);
+            e2e.link is its roofline: one step's upload and download timed
+            alone, concurrently (the PCIe floor of a pipelined step);
   roofline  tensor-bound: achieved TOPS of the GEMM kernel vs the measured
             peak: 2 x the measured bf16 dense figure of MEASURED_PEAKS.json
             (INT8 being twice bf16 on this part; 4 x for FP4), the sustained
@@ -291,7 +293,9 @@ def e2e_loop(w, host_ops, out_bytes: int, copies: int, steps: int, dev, barrier)
     pipelined over three streams -- step i+1's upload and step i-1's download overlap
     step i's launch (PCIe is full duplex) -- each step still moving all its bytes
     inside the timed region; with one set they run back to back on one stream.
-    Returns (elapsed ms, description)."""
+    Returns (elapsed ms, description, link ms): the last is the time of one step's
+    upload and download alone, run concurrently (PCIe is full duplex) -- the floor of
+    a pipelined step, the e2e figure's own roofline -- or None with one operand set."""
     import torch
     nbuf = 2 if copies >= 2 else 1
     host_out = [torch.empty((out_bytes,), dtype=torch.uint8).pin_memory() for _ in range(nbuf)]
@@ -312,7 +316,7 @@ def e2e_loop(w, host_ops, out_bytes: int, copies: int, steps: int, dev, barrier)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
-        return e0.elapsed_time(e1), "qg_upload + qg_run_copy + qg_download (pinned host buffers), one stream"
+        return e0.elapsed_time(e1), "qg_upload + qg_run_copy + qg_download (pinned host buffers), one stream", None
 
     s_up, s_run, s_down = (torch.cuda.Stream(dev) for _ in range(3))
     up_done = [torch.cuda.Event() for _ in range(nbuf)]
@@ -346,9 +350,21 @@ def e2e_loop(w, host_ops, out_bytes: int, copies: int, steps: int, dev, barrier)
         s_down.wait_event(ev)
     e1.record(s_down)
     torch.cuda.synchronize(dev)
+    elapsed = e0.elapsed_time(e1)
+    # the link alone: a step's upload (set 0) and a result's download (set 1) at once
+    reps = 5
+    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0.record(s_up)
+    s_down.wait_stream(s_up)
+    for _ in range(reps):
+        w.upload(0, host_ops, s_up)
+        w.download(1, host_out[1], s_down)
+    s_up.wait_stream(s_down)
+    l1.record(s_up)
+    torch.cuda.synchronize(dev)
     barrier()
-    return e0.elapsed_time(e1), ("qg_upload + qg_run_copy + qg_download (pinned host buffers), pipelined over "
-                                 f"{nbuf} device operand sets and three streams")
+    return elapsed, ("qg_upload + qg_run_copy + qg_download (pinned host buffers), pipelined over "
+                     f"{nbuf} device operand sets and three streams"), l0.elapsed_time(l1) / reps
 
 
 def roofline(wl, work: float, per_launch_s: float, timed_s: float, peaks: dict, traffic=None) -> dict:
@@ -514,11 +530,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # enough steps that the pipeline's fill and drain (one upload and one
     # download not overlapped) stay a few percent of the timed region
     e2e_steps = max(3, min(steps, 40))
-    e2e_ms, e2e_path = e2e_loop(w, host_ops, out_bytes, wl["copies"], e2e_steps, dev, barrier)
+    e2e_ms, e2e_path, link_ms = e2e_loop(w, host_ops, out_bytes, wl["copies"], e2e_steps, dev, barrier)
     w.close()
     del host_ops
 
-    ms_max, e2e_max, mm_max, bad = max_over_ranks([ms, e2e_ms, float(mismatches), float(status != 0)], world, dev)
+    ms_max, e2e_max, mm_max, bad, link_max = max_over_ranks(
+        [ms, e2e_ms, float(mismatches), float(status != 0), link_ms if link_ms is not None else -1.0], world, dev)
     # each rank's golden digest, as two exact 32-bit halves
     digests = [(int(hi) << 32) | int(lo) for hi, lo in gather_over_ranks([digest >> 32, digest & 0xFFFFFFFF], world, dev)]
     peaks = _peaks()
@@ -550,6 +567,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             # identical seeds give identical golden results: a rank that differs computed a wrong one
             result["golden_digests"] = {"agree": len(set(digests)) == 1,
                                         "per_rank": [f"0x{d:016x}" for d in digests]}
+        if link_max > 0:
+            # the e2e figure's roofline: a step can go no faster than its bytes over the link
+            bound = work * world / (link_max / 1e3)
+            result["e2e"]["link"] = {"ms_per_step": link_max, "h2d_GBps": h2d / link_max / 1e6,
+                                     "d2h_GBps": out_bytes / link_max / 1e6, "bound_value": bound,
+                                     "frac": e2e_value / bound,
+                                     "what": "one step's upload and download alone, concurrently (PCIe full duplex)"}
         if secondary is not None:
             result["secondary"] = secondary
         if world == 1 and not args.no_cpu_baseline and wl["name"] == "int8":
