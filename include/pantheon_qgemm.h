@@ -100,13 +100,15 @@ QG_API int  qg_create(qg_ctx** out, int device, const qg_cfg* cfg);
  * (used by the binary's --mem sizing). */
 QG_API int  qg_required_bytes(const qg_cfg* cfg, uint64_t* bytes);
 
-/* Fill all operand copies from the counter-based generator.
+/* Fill all operand copies from the counter-based generator (after waiting for
+ * all work on the device, so no launch still reads the old operands).
  * Replaces: ai_initialize (ai_workload_template.h:85-94) and
  *           pantheon_gemm_fill (kernels/common/vendor_gemm.h:184-191). */
 QG_API int  qg_fill(qg_ctx* ctx, uint64_t seed);
 
 /* Run every copy once and keep the outputs (and INT8 row checksums) as the
- * golden result of this run.
+ * golden result of this run (after waiting for all work on the device, so no
+ * earlier launch on another stream still writes the outputs).
  * Replaces: the golden GEMM + D2D copy of kernels/mma_virus/mma_virus.cpp:331-337. */
 QG_API int  qg_golden(qg_ctx* ctx);
 
@@ -124,6 +126,15 @@ QG_API int  qg_golden(qg_ctx* ctx);
  * Replaces: the ai_workload_kernel launch of the timed loop
  *           (ai_workload_template.h:370). Asynchronous. */
 QG_API int  qg_run(qg_ctx* ctx, int iters, void* stream);
+
+/* qg_run as a CUDA graph: the batch of `iters` launches is captured once per
+ * (iters, the copy it starts at) from the context's own stream, instantiated,
+ * and replayed on `stream` (NULL: the legacy default stream) with one
+ * cudaGraphLaunch, so a batch costs the host one call however many launches
+ * it holds.  Same launches, flags, checks and copy rotation as qg_run; the
+ * captured batches are dropped by qg_fill and qg_golden.  Asynchronous.
+ * Replaces: the timed batch of vendor_gemm.h:560-571 (launches between syncs). */
+QG_API int  qg_run_graph(qg_ctx* ctx, int iters, void* stream);
 
 /* Compare every copy's latest output (and checksums) with the golden result on
  * the device; `*mismatches` receives the number of differing 32-bit words plus

@@ -49,6 +49,7 @@ _SIGNATURES = {
     "qg_fill": (C.c_int, [_V, C.c_uint64]),
     "qg_golden": (C.c_int, [_V]),
     "qg_run": (C.c_int, [_V, C.c_int, _V]),
+    "qg_run_graph": (C.c_int, [_V, C.c_int, _V]),
     "qg_verify": (C.c_int, [_V, C.POINTER(C.c_uint64)]),
     "qg_verify_detail": (C.c_int, [_V, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "qg_golden_digest": (C.c_int, [_V, C.c_int, C.POINTER(C.c_uint64)]),

@@ -25,6 +25,14 @@ struct qg_ctx {
     uint64_t launches_checked = 0;            // launches run with the per-launch check since the last qg_verify
     uint64_t last_words = 0, last_launch_diffs = 0, last_launches = 0;   // split of the last qg_verify
     cudaStream_t stream = nullptr;            // internal stream for fill / golden / verify
+    // Batches of qg_run_graph, captured once per (launches, first copy) and
+    // replayed; dropped when qg_fill or qg_golden changes what a launch checks.
+    struct GraphBatch {
+        int iters;
+        int start;
+        cudaGraphExec_t exec;
+    };
+    std::vector<GraphBatch> graphs;
     std::string err;
 };
 
@@ -47,7 +55,13 @@ int fail(qg_ctx* c, int rc) {
         }                                                                                       \
     } while (0)
 
+void drop_graphs(qg_ctx* c) {
+    for (auto& g : c->graphs) cudaGraphExecDestroy(g.exec);
+    c->graphs.clear();
+}
+
 void free_ctx_memory(qg_ctx* c) {
+    drop_graphs(c);
     for (auto& cp : c->copies) {
         for (int i = 0; i < qg::kMaxOperands; ++i)
             if (cp.op[i]) cudaFree(cp.op[i]);
@@ -171,6 +185,8 @@ void qg_destroy(qg_ctx* c) {
 int qg_fill(qg_ctx* c, uint64_t seed) {
     QG_CHECK_ARG(c, "qg_fill: null context");
     CTX_CUDA(c, cudaSetDevice(c->device));
+    // launches still running on a caller's stream read the operands rewritten here
+    CTX_CUDA(c, cudaDeviceSynchronize());
     c->cfg.seed = seed;
     for (size_t i = 0; i < c->copies.size(); ++i) {
         int rc = qg::fill_copy(c->cfg, c->layout, c->copies[i], (int)i, seed, c->stream);
@@ -178,12 +194,16 @@ int qg_fill(qg_ctx* c, uint64_t seed) {
     }
     CTX_CUDA(c, cudaStreamSynchronize(c->stream));
     c->golden_ready = false;
+    drop_graphs(c);
     return QG_OK;
 }
 
 int qg_golden(qg_ctx* c) {
     QG_CHECK_ARG(c, "qg_golden: null context");
     CTX_CUDA(c, cudaSetDevice(c->device));
+    // launches still running on a caller's stream write the outputs and row
+    // checksums the golden launches write here
+    CTX_CUDA(c, cudaDeviceSynchronize());
     for (auto& cp : c->copies) {
         qg::LaunchCheck record;   // the golden launch records its fingerprints for the later launches
         record.record = static_cast<uint32_t*>(cp.check_fp);
@@ -201,6 +221,7 @@ int qg_golden(qg_ctx* c) {
     c->launches_checked = 0;
     c->golden_ready = true;
     c->next_copy = 0;
+    drop_graphs(c);
     return QG_OK;
 }
 
@@ -220,6 +241,48 @@ int qg_run(qg_ctx* c, int iters, void* stream) {
         if (chk.count) ++c->launches_checked;
         c->next_copy = (c->next_copy + 1) % (int)c->copies.size();
     }
+    return QG_OK;
+}
+
+int qg_run_graph(qg_ctx* c, int iters, void* stream) {
+    QG_CHECK_ARG(c && iters >= 0, "qg_run_graph: bad argument");
+    if (iters == 0) return QG_OK;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    const int copies = (int)c->copies.size();
+    const int start = c->next_copy;
+    cudaGraphExec_t exec = nullptr;
+    for (const auto& g : c->graphs)
+        if (g.iters == iters && g.start == start) exec = g.exec;
+    if (!exec) {
+        // the same launches as qg_run's, captured from the context's own stream
+        CTX_CUDA(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+        int rc = QG_OK;
+        for (int i = 0, copy = start; i < iters && rc == QG_OK; ++i, copy = (copy + 1) % copies) {
+            const qg::CopyBuffers& cp = c->copies[(size_t)copy];
+            rc = qg::launch_copy(c->cfg, c->layout, cp, c->stream,
+                                 i > 0 ? (QG_GEMV_WEIGHTS_CONST | QG_GEMV_ACTIVATIONS_CONST) : 0u, run_check(c, cp));
+        }
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+        if (rc != QG_OK || e != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            if (rc == QG_OK) {
+                qg::set_error("qg_run_graph: stream capture failed: %s (%d)", cudaGetErrorString(e), (int)e);
+                rc = QG_ERR_CUDA;
+            }
+            return fail(c, rc);
+        }
+        const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ei != cudaSuccess) {
+            qg::set_error("qg_run_graph: cudaGraphInstantiate failed: %s (%d)", cudaGetErrorString(ei), (int)ei);
+            return fail(c, QG_ERR_CUDA);
+        }
+        c->graphs.push_back({iters, start, exec});
+    }
+    CTX_CUDA(c, cudaGraphLaunch(exec, static_cast<cudaStream_t>(stream)));
+    if (run_check(c, c->copies[(size_t)start]).count) c->launches_checked += (uint64_t)iters;
+    c->next_copy = (int)((start + (long long)iters) % copies);
     return QG_OK;
 }
 

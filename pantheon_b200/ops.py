@@ -325,6 +325,11 @@ class Workload:
         s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)
         self._check("qg_run", self.lib.qg_run(self.ctx, iters, s))
 
+    def run_graph(self, iters: int = 1, stream=None):
+        """run(), as one CUDA graph per (iters, first copy), captured on first use and replayed."""
+        s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)
+        self._check("qg_run_graph", self.lib.qg_run_graph(self.ctx, iters, s))
+
     def run_copy(self, copy: int, stream=None):
         s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream(self.device)
         self._check("qg_run_copy", self.lib.qg_run_copy(self.ctx, copy, s))
