@@ -38,6 +38,9 @@ struct qg_ctx {
 
 namespace {
 
+// Captured batches qg_run_graph keeps per context (each holds its own graph).
+constexpr size_t kMaxGraphs = 16;
+
 // Salt of the INT8 row checksums' terms in the golden digest (the output words' is 0).
 constexpr uint64_t kCksumDigestSalt = 0xC2B2AE3D27D4EB4Full;
 
@@ -56,6 +59,8 @@ int fail(qg_ctx* c, int rc) {
     } while (0)
 
 void drop_graphs(qg_ctx* c) {
+    if (c->graphs.empty()) return;
+    cudaDeviceSynchronize();   // no replay of these graphs may still be running
     for (auto& g : c->graphs) cudaGraphExecDestroy(g.exec);
     c->graphs.clear();
 }
@@ -277,6 +282,11 @@ int qg_run_graph(qg_ctx* c, int iters, void* stream) {
         if (ei != cudaSuccess) {
             qg::set_error("qg_run_graph: cudaGraphInstantiate failed: %s (%d)", cudaGetErrorString(ei), (int)ei);
             return fail(c, QG_ERR_CUDA);
+        }
+        if (c->graphs.size() >= kMaxGraphs) {   // keep the most recent batches only
+            CTX_CUDA(c, cudaDeviceSynchronize());   // the oldest may still be replaying
+            cudaGraphExecDestroy(c->graphs.front().exec);
+            c->graphs.erase(c->graphs.begin());
         }
         c->graphs.push_back({iters, start, exec});
     }

@@ -64,3 +64,18 @@ def test_graph_and_eager_batches_interleave(cuda_device):
         torch.cuda.synchronize()
         assert w.verify() == 0
         assert w.verify_detail()[2] == 54
+
+
+def test_graph_cache_keeps_the_latest_batches(cuda_device):
+    """More distinct batch lengths than the cache holds: the oldest graphs are evicted
+    (after the device drains) and every batch still runs and checks correctly."""
+    with pb.Workload(pb.QG_FMT_W4A16, 1, 4096, 2048, copies=1, seed=9) as w:
+        w.fill(9)
+        w.golden()
+        total = 0
+        for n in list(range(1, 21)) + [1, 2, 3]:
+            w.run_graph(n)
+            total += n
+        torch.cuda.synchronize()
+        assert w.verify() == 0
+        assert w.verify_detail()[2] == total
