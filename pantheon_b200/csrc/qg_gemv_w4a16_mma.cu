@@ -95,10 +95,10 @@ struct Cfg {
     static constexpr int XS_OFF = STEPS * XF_STEP;           // then per (t, b): {2^e, sum xi, 8 sum xi, 0}
     static constexpr int XG = XS_OFF + 4 * NB * 16;          // prepared bytes per group
     // Weight ring depth per warp (groups copied ahead of the one computed).
-    // Measured at configs[3]: 3 instead of 5 at one fragment cost 2 %, 5
-    // instead of 4 at two fragments 2 % too (fewer registers for the rest);
-    // at three fragments 3 measured 1 % faster than 4 and leaves room to
-    // stage the activations of a CTA's whole range (one wave).
+    // Measured at configs[3]: 3 instead of 5 at one fragment cost 2 %, 5 or 3
+    // instead of 4 at two fragments 2 % and 0.4 % (5: fewer registers for the
+    // rest); at three fragments 3 measured 1 % faster than 4 and leaves room
+    // to stage the activations of a CTA's whole range (one wave).
     static constexpr int RING = NB == 1 ? 5 : (NB == 2 ? 4 : 3);
     static constexpr int RING_BYTES = WARPS * RING * SLOT;
     static constexpr int XMAX = (SMEM_BUDGET - RING_BYTES) / XG;   // groups of activations a CTA can stage
