@@ -405,10 +405,13 @@ int main(int argc, char* argv[]) {
     const uint64_t budget = free_b / 100 * (uint64_t)o.mem_pct;
     uint64_t one = 0;
     if (qg_required_bytes(&cfg, &one) != QG_OK) return fail_ctx(nullptr, "bad configuration");
+    // Four weight sets (4 x 125 MB at configs[3], four times the 126 MB L2) are
+    // enough to stream every call from HBM; more only spread the stream over
+    // more pages (configs[3] M=1, 10 s runs: 8 sets 4925 GB/s, 4 sets 5048).
     if (o.copies > 0) cfg.copies = o.copies;
     else if (o.format == QG_FMT_W4A16) {
         uint64_t fit = one ? budget / one : 1;
-        cfg.copies = (int)(fit < 1 ? 1 : (fit > 8 ? 8 : fit));
+        cfg.copies = (int)(fit < 1 ? 1 : (fit > 4 ? 4 : fit));
     }
     uint64_t need = 0;
     qg_required_bytes(&cfg, &need);
