@@ -252,7 +252,7 @@ def run_reference(args, rank: int):
     for _ in range(warm):
         O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
     t0 = time.perf_counter()
-    for s in range(steps):
+    for _ in range(steps):
         O.gemm_i8(A, B, sa, sb, out_type=0, rows=rows)
     dt = time.perf_counter() - t0
     tops = 2.0 * len(rows) * N * K * steps / dt / 1e12
