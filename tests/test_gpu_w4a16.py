@@ -43,7 +43,9 @@ def test_generator_matches_oracle(cuda_device, oracle):
 # 1 row runs on the CUDA cores, 2-12 on warp MMAs, 13-16 on tcgen05, more in chunks of 16
 SHAPES = [(1, 512, 128), (1, 1028, 1024), (3, 2048, 2048), (8, 4096, 1024), (16, 1536, 4096),
           (17, 516, 256), (5, 28672, 256), (4, 300, 384), (12, 1028, 1024), (8, 128, 8192), (16, 36, 128),
-          (34, 260, 512), (9, 2052, 1024), (13, 1028, 1024), (11, 36, 128)]
+          (34, 260, 512), (9, 2052, 1024), (13, 1028, 1024), (11, 36, 128),
+          # the smallest widths: one or two live column quads of a super-tile
+          (2, 4, 128), (9, 8, 128), (12, 4, 256), (13, 4, 128), (16, 4, 128)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
